@@ -1,0 +1,156 @@
+/*
+ * boltz_b200.h -- C ABI of the B200 (sm_100a) kernels for Boltz-2's pair path.
+ *
+ * Every entry point takes plain device pointers, element counts and a
+ * cudaStream_t passed as void*, launches asynchronously on that stream and
+ * returns a BL_* status.  On failure bl_last_error() holds a message (per
+ * calling thread).  No entry point allocates device memory; intermediate
+ * buffers are passed in by the caller.  Inference only: nothing here records
+ * autograd state.
+ *
+ * Each declaration names the reference interface it replaces
+ * (lauritsf/boltz-lumi, path relative to src/boltz_lumi/).
+ */
+#ifndef BOLTZ_B200_H
+#define BOLTZ_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BL_API __attribute__((visibility("default")))
+#else
+#define BL_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+enum {
+  BL_OK = 0,
+  BL_ERR_INVALID = 1,     /* bad shape, dtype, alignment or pointer          */
+  BL_ERR_CUDA = 2,        /* a CUDA runtime call failed                       */
+  BL_ERR_UNSUPPORTED = 3, /* valid request outside what the kernels cover     */
+  BL_ERR_TIMEOUT = 4      /* a bounded device-side wait gave up               */
+};
+
+/* Element types. */
+enum { BL_F32 = 0, BL_BF16 = 1 };
+
+/* Diffusion epilogue kinds; values match the reference's operation codes
+ * (diffusion.py:27 MODULATION, GATE, GATED_SWIGLU = 0, 1, 3). */
+enum { BL_EPI_MODULATION = 0, BL_EPI_GATE = 1, BL_EPI_GATED_SWIGLU = 3 };
+
+/* Message for the last failed call on this thread ("" if none). */
+BL_API const char *bl_last_error(void);
+
+/* ABI version of this library. */
+BL_API int bl_version(void);
+
+/* Device-side status word of the current device: 0 when every bounded wait
+ * completed, otherwise a code naming the wait that gave up.  reset != 0
+ * clears it.  Synchronises the device. */
+BL_API int bl_device_status(int reset);
+
+/*
+ * LayerNorm over `cols` channels, fp32 statistics.
+ * Replaces kernels/multiplication_hip.cu:149 `multiplication_norm`
+ * (bound as extension("multiplication").norm, used at triangle.py:240 and
+ * multiplication.py:88,124).
+ *   channel_first = 0: x is [rows, cols] row-major.
+ *   channel_first = 1: x is [cols, rows] (one plane per channel); cols must be 128.
+ * out is [rows, cols] row-major.  weight / bias may be NULL (no affine).
+ */
+BL_API int bl_layernorm(const void *x, int x_dtype, int64_t rows, int64_t cols, int channel_first,
+                 const float *weight, const float *bias, float eps, void *out, int out_dtype,
+                 void *stream);
+
+/*
+ * Sigmoid gate: out = bf16(p * bf16(sigmoid(g))), all bf16, n elements.
+ * Replaces kernels/multiplication_gate_hip.cu:81 `multiplication_gate`
+ * (extension("multiplication_gate").gate, multiplication.py:137).
+ */
+BL_API int bl_gate(const void *p, const void *g, void *out, int64_t n, void *stream);
+
+/*
+ * Gate, mask and pack the triangle-multiplication operands into
+ * channel-first planes for a per-channel batched matmul.
+ * Replaces kernels/multiplication_gate_hip.cu:140 `multiplication_gate_pack`
+ * (multiplication.py:106).  p, g: bf16 [n, n, 256] with row stride
+ * `pair_stride` elements (256 dense, 512 for a joint projection); mask: fp32
+ * [n, n].  Outputs left, right: bf16 [128, n, n]:
+ *   outgoing: left[c][i][k] = a[i][k][c], right[c][k][j] = b[j][k][c]
+ *   incoming: left[c][i][k] = a[k][i][c], right[c][k][j] = b[k][j][c]
+ * where a / b are channels 0..127 / 128..255 of bf16(p * bf16(sigmoid(g))) * mask.
+ */
+BL_API int bl_gate_pack(const void *p, const void *g, int64_t pair_stride, const float *mask, int64_t n,
+                 int outgoing, void *left, void *right, void *stream);
+
+/*
+ * Gate and mask into channel-last halves: a, b bf16 [n*n, 128].
+ * Replaces kernels/multiplication_gate_hip.cu:96 `multiplication_gate_split`
+ * (multiplication.py:110).
+ */
+BL_API int bl_gate_split(const void *p, const void *g, int64_t pair_stride, const float *mask, int64_t n,
+                  void *a, void *b, void *stream);
+
+/*
+ * out = bf16(bf16(silu(a)) * b), all bf16, n elements, any alignment.
+ * Replaces kernels/pair_hip.cu:42 `pair_silu_mul` (pair_transition.py:161).
+ */
+BL_API int bl_silu_mul(const void *a, const void *b, void *out, int64_t n, void *stream);
+
+/*
+ * fp32 diffusion epilogues over rows x cols outputs (contiguous):
+ *   MODULATION:   out = sigmoid(b) * a + c
+ *   GATE:         out = sigmoid(a) * b
+ *   GATED_SWIGLU: a is [rows, 2*cols]; out = silu(a[:, cols:]) * a[:, :cols] * b
+ * Replaces kernels/diffusion_hip.cu:80 `diffusion_epilogue` (diffusion.py:52-68).
+ */
+BL_API int bl_diffusion_epilogue(const float *a, const float *b, const float *c, float *out,
+                          int64_t rows, int64_t cols, int kind, void *stream);
+
+/*
+ * Fused AdaLN modulation: out = sigmoid(scale) * LayerNorm(a) + shift, where
+ * the LayerNorm has no affine (upstream AdaLN.a_norm).  fp32, [rows, cols].
+ * Fuses the a_norm call and the MODULATION epilogue of diffusion.py:52-57.
+ */
+BL_API int bl_adaln_modulate(const float *a, const float *scale, const float *shift, float *out,
+                      int64_t rows, int64_t cols, float eps, void *stream);
+
+/*
+ * Ordered bias softmax of materialised triangle scores:
+ *   p = softmax(round(round(s + mask) + bias)) rounded to the score dtype.
+ * Replaces kernels/triangle_softmax.py:120 `ordered_softmax` and
+ * kernels/triangle_block_softmax_hip.cu:120 `triangle_block_softmax`
+ * (triangle.py:88-100).  scores: [B, I, H, N, N] of `dtype` with element
+ * strides ss[5]; bias: `dtype`, indexed by (b, h, q, k) with strides bs[4];
+ * mask: fp32 indexed by (b, i, k) with strides ms[3]; out: contiguous
+ * [B, I, H, N, N] of `dtype`.
+ */
+BL_API int bl_triangle_softmax(const void *scores, int dtype, int64_t batch, int64_t outer, int64_t heads,
+                        int64_t n, const int64_t *ss, const void *bias, const int64_t *bs,
+                        const float *mask, const int64_t *ms, void *out, void *stream);
+
+/*
+ * Batched bf16 GEMM on tcgen05 tensor cores, fp32 accumulation, bf16 output:
+ *   C[b](m, n) = sum_k A[b](m, k) * B[b](n, k) + bias[n]   (bias may be NULL)
+ * Replaces the torch.bmm / torch.matmul calls of the reference path
+ * (multiplication.py:122 `torch.bmm(left, right)`, triangle.py:194,208).
+ * A is K-major (A[b][m][k] at a + b*a_batch_stride + m*a_ld + k) or, with
+ * a_mn_major, MN-major (A[b][k][m] at a + b*a_batch_stride + k*a_ld + m);
+ * likewise B.  C[b][m][n] at c + b*c_batch_stride + m*c_ld + n.
+ * Pointers 16-byte aligned; leading dimensions and batch strides multiples
+ * of 8 elements.  Rows/columns past m, n, k are handled by the TMA bounds.
+ */
+BL_API int bl_batched_gemm(const void *a, int a_mn_major, int64_t a_ld, int64_t a_batch_stride,
+                           const void *b, int b_mn_major, int64_t b_ld, int64_t b_batch_stride, void *c,
+                           int64_t c_ld, int64_t c_batch_stride, int64_t batch, int64_t m, int64_t n,
+                           int64_t k, const float *bias, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BOLTZ_B200_H */
