@@ -1,0 +1,429 @@
+"""Benchmark: Boltz-2 Pairformer ms/block at N = 512 (bf16 trunk contract).
+
+One step = one full Pairformer block (TriMulOut, TriMulIn, TriAttStart,
+TriAttEnd, Transition(z), then the fp32 single track) applied to z in place on
+synthetic seeded inputs: z ~ N(0,1) [1, 512, 512, 128] fp32, s ~ N(0,1)
+[1, 512, 384], masks all ones, weights ~ N(0, 1/128) with unit-mean norm
+weights.  Consecutive steps chain like the trunk's consecutive blocks.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+With N > 1 the driver starts one rank per GPU (torch.distributed.run); every
+rank runs its own independent block (separate inputs, no collective in the
+data path: weak scaling) and the step time is the max over ranks.  Rank 0
+prints one JSON line.  ``--impl reference`` times the CPU restatement of the
+reference path (the oracle) on this host's cores instead; under torchrun only
+rank 0 runs it.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Pairformer ms/block at N=512 bf16"
+UNIT = "ms/block"
+N_TOKENS = 512
+C_S, C_Z = 384, 128
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--n", type=int, default=N_TOKENS, help="tokens (default 512, the metric's config)")
+    p.add_argument("--e2e-steps", type=int, default=5)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def load_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            data = json.loads(path.read_text())
+            return {k: float(data[k]) for k in FALLBACK_PEAKS}, "measured"
+        except (KeyError, ValueError):
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def seeded_block(cls, seed=1234):
+    """Weights ~ N(0, 1/128), norm weights N(1, 1/128), from a fixed CPU generator."""
+    module = cls()
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        for name, p in module.named_parameters():
+            mean = 1.0 if "norm" in name and name.endswith("weight") else 0.0
+            p.copy_(torch.randn(p.shape, generator=g) * (1.0 / 128) ** 0.5 + mean)
+    return module.eval()
+
+
+def synthetic_inputs(n, seed):
+    g = torch.Generator().manual_seed(seed)
+    s = torch.randn(1, n, C_S, generator=g)
+    z = torch.randn(1, n, n, C_Z, generator=g)
+    mask = torch.ones(1, n)
+    pair_mask = torch.ones(1, n, n)
+    return s, z, mask, pair_mask
+
+
+def cpu_info():
+    model = "unknown"
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return model
+
+
+# ---------------------------------------------------------------------------
+# CPU restatement of the reference path (oracle), bounded sample
+# ---------------------------------------------------------------------------
+def cpu_block_sample(n, attention_rows=4):
+    """Time one Pairformer block of the CPU oracle; the two attention ops are
+    timed on ``attention_rows`` and ``2 * attention_rows`` outer rows and
+    extrapolated linearly to n rows (rows are independent).  Returns (ms, sample)."""
+    import oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    ref = seeded_block(oracle.PairformerLayer)
+    s, z, mask, pair_mask = synthetic_inputs(n, seed=99)
+    timings = {}
+    with torch.inference_mode():
+        t = time.perf_counter()
+        z = z + ref.tri_mul_out(z, pair_mask)
+        z = z + ref.tri_mul_in(z, pair_mask)
+        timings["tri_mul"] = time.perf_counter() - t
+        att = 0.0
+        for op in (ref.tri_att_start, ref.tri_att_end):
+            t0 = time.perf_counter()
+            op(z, pair_mask, rows=attention_rows)
+            t1 = time.perf_counter()
+            op(z, pair_mask, rows=2 * attention_rows)
+            t2 = time.perf_counter()
+            base, per_row = t1 - t0, max((t2 - t1) - (t1 - t0), 0.0) / attention_rows
+            att += base + per_row * (n - attention_rows)
+        timings["tri_att_extrapolated"] = att
+        t = time.perf_counter()
+        z = z + ref.transition_z(z)
+        timings["transition_z"] = time.perf_counter() - t
+        t = time.perf_counter()
+        sn = torch.nn.functional.layer_norm(s, (C_S,), ref.pre_norm_s.weight, ref.pre_norm_s.bias, 1e-5)
+        s = s + ref.attention(sn, z, mask, sn)
+        s = s + ref.transition_s(s, bf16=False)
+        timings["single_track"] = time.perf_counter() - t
+    total_ms = 1000.0 * sum(timings.values())
+    sample = (f"one block at N={n} on {threads} threads ({cpu_info()}); TriMul, Transition and single track "
+              f"in full, both triangle attentions timed on {attention_rows} and {2 * attention_rows} outer rows "
+              f"and extrapolated to {n}; parts_s=" + json.dumps({k: round(v, 3) for k, v in timings.items()}))
+    return total_ms, sample, threads
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    n = args.n
+    for _ in range(args.warmup):
+        cpu_block_sample(n, attention_rows=2)
+    values = []
+    sample = ""
+    threads = os.cpu_count() or 1
+    for _ in range(args.steps):
+        ms, sample, threads = cpu_block_sample(n, attention_rows=2)
+        values.append(ms)
+    value = statistics.mean(values)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 3), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16-rounding oracle)", "data": "synthetic",
+        "config": {"workload": f"Pairformer block N={n}", "tokens": n, "c_s": C_S, "c_z": C_Z, "heads": "4x32",
+                   "parallelism": "cpu host"},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def algorithmic_work(name, a):
+    """(kind, amount per launch, label) of one C-ABI call, from its arguments."""
+    if name == "bl_batched_gemm":
+        batch, m, n, k = a[11], a[12], a[13], a[14]
+        return "flops", 2.0 * batch * m * n * k, f"bl_batched_gemm[b={batch},m={m},n={n},k={k}]"
+    if name == "bl_triangle_attention":
+        heads, d, n = a[14], a[15], a[16]
+        return "flops", 4.0 * n ** 3 * heads * d, f"bl_triangle_attention[n={n},heads={heads},d={d}]"
+    if name == "bl_layernorm":
+        size = {0: 4, 1: 2}
+        rows, cols = a[2], a[3]
+        return "bytes", rows * cols * (size[a[1]] + size[a[9]]), f"bl_layernorm[rows={rows},cols={cols}]"
+    if name == "bl_layernorm_planes":
+        n, out_size = a[1], 2 if a[7] == 1 else 4
+        return "bytes", n * n * 128 * (2 + out_size), f"bl_layernorm_planes[n={n}]"
+    if name == "bl_trimul_pack_planes":
+        n, plane_ld = a[3], a[4]
+        return "bytes", n * n * (512 * 2 + 4) + 2 * 128 * n * plane_ld * 2, f"bl_trimul_pack_planes[n={n}]"
+    if name == "bl_swiglu_rows":
+        rows, width = a[2], a[3]
+        return "bytes", rows * width * 6, f"bl_swiglu_rows[rows={rows},width={width}]"
+    if name == "bl_gate":
+        return "bytes", a[3] * 6, f"bl_gate[n={a[3]}]"
+    return "bytes", 0.0, name
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.samples = []
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", ident, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, RuntimeError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 7:
+                self.samples.append(parts)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        sm, sm_max, reasons = [], [], set()
+        for parts in self.samples:
+            try:
+                sm.append(float(parts[0]))
+                sm_max.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[3:]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(sm_max) if sm_max else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def run_b200(args):
+    world, rank, local = dist_env()
+    if not torch.cuda.is_available():
+        print(json.dumps({"metric": METRIC, "error": "no CUDA device"}))
+        return 1
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist_mod
+
+        dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        dist = dist_mod
+
+    from boltz_lumi_b200 import _lib, layers
+
+    n = args.n
+    block = seeded_block(layers.PairformerLayer).to(device)
+    s_h, z_h, mask_h, pmask_h = synthetic_inputs(n, seed=1000 + rank)
+    s, z, mask, pmask = (t.to(device) for t in (s_h, z_h, mask_h, pmask_h))
+
+    def step():
+        nonlocal s, z
+        s, z = block(s, z, mask, pmask)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    with torch.inference_mode():
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+
+        # Untimed profiling step: per-call device time of every C-ABI entry point.
+        observer = _lib.CallObserver(timed=("*",))
+        _lib.set_observer(observer)
+        step()
+        _lib.set_observer(None)
+        torch.cuda.synchronize()
+        launches_per_step = observer.calls
+        per_label = {}
+        for name, a, e0, e1 in observer.records:
+            kind, amount, label = algorithmic_work(name, a)
+            entry = per_label.setdefault(label, {"name": name, "kind": kind, "amount": amount, "ms": 0.0, "n": 0})
+            entry["ms"] += e0.elapsed_time(e1)
+            entry["n"] += 1
+        top_label = max(per_label, key=lambda k: per_label[k]["ms"])
+        top = per_label[top_label]
+
+        # Timed region: K chained blocks; the dominant kernel is event-timed in place.
+        observer = _lib.CallObserver(timed=(top["name"],))
+        clocks = ClockSampler(device)
+        barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        _lib.set_observer(observer)
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        torch.cuda.synchronize()
+        _lib.set_observer(None)
+        barrier()
+        clock_info = clocks.stop()
+        elapsed_ms = start.elapsed_time(end)
+        launches_timed = observer.calls
+        top_times = [e0.elapsed_time(e1) for name, a, e0, e1 in observer.records
+                     if algorithmic_work(name, a)[2] == top_label]
+        if dist is not None:
+            t = torch.tensor([elapsed_ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            elapsed_ms = float(t.item())
+        ms_per_step = elapsed_ms / args.steps
+        value = ms_per_step / world  # aggregate: `world` blocks complete per step
+
+        # End to end through the public module API with pinned host buffers.
+        z_host = z_h.pin_memory()
+        s_host = s_h.pin_memory()
+        z_back = torch.empty_like(z_host).pin_memory()
+        s_back = torch.empty_like(s_host).pin_memory()
+        h2d = z_host.numel() * 4 + s_host.numel() * 4 + mask_h.numel() * 4 + pmask_h.numel() * 4
+        d2h = z_back.numel() * 4 + s_back.numel() * 4
+        barrier()
+        torch.cuda.synchronize()
+        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_start.record()
+        for _ in range(args.e2e_steps):
+            zd = z_host.to(device, non_blocking=True)
+            sd = s_host.to(device, non_blocking=True)
+            md = mask_h.to(device, non_blocking=True)
+            pd = pmask_h.to(device, non_blocking=True)
+            so, zo = block(sd, zd, md, pd)
+            z_back.copy_(zo, non_blocking=True)
+            s_back.copy_(so, non_blocking=True)
+        e_end.record()
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = e_start.elapsed_time(e_end)
+        if dist is not None:
+            t = torch.tensor([e2e_ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e_value = e2e_ms / args.e2e_steps / world
+        assert torch.isfinite(z_back).all() and torch.isfinite(s_back).all(), "non-finite block output"
+        status = _lib.device_status(reset=True)
+        if status:
+            raise RuntimeError(f"device-side bounded wait timed out (status {status:#x})")
+
+    peaks, peak_source = load_peaks()
+    avg_ms = statistics.mean(top_times) if top_times else top["ms"] / max(top["n"], 1)
+    if top["kind"] == "flops":
+        achieved = top["amount"] / (avg_ms * 1e-3) / 1e12
+        peak = peaks["bf16_tflops_sustained"]
+        roofline = {"bound": "tensor", "unit": "TFLOP/s"}
+    else:
+        achieved = top["amount"] / (avg_ms * 1e-3) / 1e9
+        peak = peaks["hbm_gbs"]
+        roofline = {"bound": "hbm", "unit": "GB/s"}
+    roofline.update({
+        "achieved": round(achieved, 2), "peak": peak, "frac": round(achieved / peak, 4),
+        "traffic": traffic_for(top_label), "kernel": top_label, "avg_launch_ms": round(avg_ms, 4),
+        "launches_timed": len(top_times), "algorithmic_per_launch": top["amount"],
+        "peak_source": f"{peak_source} ({'bf16_tflops_sustained' if top['kind'] == 'flops' else 'hbm_gbs'})",
+    })
+
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(ms_per_step, 4), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) inputs, N(0,1/128) weights)",
+        "config": {"workload": f"Pairformer block N={n} (TriMulOut+In, TriAttStart+End, Transition(z), single track)",
+                   "tokens": n, "c_s": C_S, "c_z": C_Z, "heads": "4x32", "parallelism": f"dp{world} (one block per GPU)",
+                   "l2": "inputs larger than L2: z 128 MiB fp32 plus per-op intermediates up to 272 MiB"},
+        "e2e": {"value": round(e2e_value, 4), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_timed,
+        "launches_per_step": launches_per_step,
+        "roofline": roofline,
+        "clocks": clock_info,
+        "kernels_ms_per_step": {k: round(v["ms"], 4) for k, v in sorted(per_label.items(), key=lambda kv: -kv[1]["ms"])},
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_ms, sample, threads = cpu_block_sample(n)
+        line["cpu_baseline"] = {"value": round(cpu_ms, 2), "unit": UNIT, "cores": threads, "kind": "port",
+                                "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+def traffic_for(label):
+    """DRAM bytes per launch of `label` from the committed ncu summary, if one exists."""
+    for path in sorted((ROOT / "profiles").glob("*.md")):
+        for line in path.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:") and label in line:
+                try:
+                    return float(line.split(":", 1)[1].split()[0])
+                except ValueError:
+                    return None
+    return None
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -35,6 +35,12 @@ SIGNATURES = {
     "bl_triangle_softmax": [_p, c_int, c_int64, c_int64, c_int64, c_int64, _i64p, _p, _i64p, _p, _i64p, _p, _p],
     "bl_batched_gemm": [_p, c_int, c_int64, c_int64, _p, c_int, c_int64, c_int64, _p, c_int64, c_int64,
                         c_int64, c_int64, c_int64, c_int64, _p, _p],
+    "bl_layernorm_planes": [_p, c_int64, c_int64, _p, _p, c_float, _p, c_int, _p],
+    "bl_trimul_pack_planes": [_p, c_int64, _p, c_int64, c_int64, _p, _p, _p],
+    "bl_swiglu_rows": [_p, c_int64, c_int64, c_int64, _p, c_int64, _p],
+    "bl_triangle_bias_planes": [_p, c_int64, c_int64, c_int64, c_int, _p, c_int64, _p],
+    "bl_triangle_attention": [_p, _p, _p, _p, c_int64, c_int64, c_int64, _p, c_int64, c_int64, _p, c_int64,
+                              c_int64, c_float, c_int64, c_int64, c_int64, _p, c_int64, _p],
 }
 _RESTYPES = {"bl_last_error": ctypes.c_char_p}
 
@@ -59,10 +65,49 @@ def load():
     return _lib
 
 
+class CallObserver:
+    """Optional hook around every C-ABI call: counts calls and, for the entry
+    points in ``timed``, records CUDA events on the launching stream.  Used by
+    the benchmark to count launches and time the dominant kernel in place."""
+
+    def __init__(self, timed=()):
+        self.timed = set(timed)
+        self.calls = 0
+        self.records = []  # (name, args, start_event, end_event)
+
+    def before(self, name, args):
+        self.calls += 1
+        if name in self.timed or "*" in self.timed:
+            start = torch.cuda.Event(enable_timing=True)
+            start.record()
+            return start
+        return None
+
+    def after(self, name, args, start):
+        if start is not None:
+            end = torch.cuda.Event(enable_timing=True)
+            end.record()
+            self.records.append((name, args, start, end))
+
+
+_observer = None
+
+
+def set_observer(observer):
+    """Install (or with None remove) a CallObserver; returns the previous one."""
+    global _observer
+    previous, _observer = _observer, observer
+    return previous
+
+
 def call(name, *args):
     """Call ``name`` and raise ``RuntimeError`` with the library's message on failure."""
     lib = load()
+    observer = _observer
+    token = observer.before(name, args) if observer is not None else None
     status = getattr(lib, name)(*args)
+    if observer is not None:
+        observer.after(name, args, token)
     if status != 0:
         message = lib.bl_last_error().decode(errors="replace")
         raise RuntimeError(f"{name} failed with status {status}: {message}")

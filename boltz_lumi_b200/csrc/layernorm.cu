@@ -97,18 +97,21 @@ __global__ void layernorm_rows_generic_kernel(const Tin *x, const float *w, cons
   }
 }
 
-// Channel-first input [128, M]; block = 8 warps, 32 rows per tile.
+// Channel-first input: channel c of row m at x[c * plane + (m / inner) * ld + m % inner]
+// (a dense [128, M] tensor is inner = ld = plane = M).  Block = 8 warps, 32 rows per tile.
 template <typename Tin, typename Tout>
 __global__ void __launch_bounds__(256) layernorm_channel_first_kernel(const Tin *x, const float *w,
                                                                       const float *b, Tout *out, int64_t m,
+                                                                      int64_t inner, int64_t ld, int64_t plane,
                                                                       float eps) {
   __shared__ float tile[128][33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int64_t start = blockIdx.x * 32ll; start < m; start += int64_t(gridDim.x) * 32) {
     // Coalesced plane reads: warp w reads channels w, w+8, ...; lane = row.
+    const int64_t row_l = start + lane;
+    const int64_t offset = (row_l / inner) * ld + row_l % inner;
     for (int c = warp; c < 128; c += 8) {
-      int64_t row = start + lane;
-      tile[c][lane] = row < m ? load_as_float(x + int64_t(c) * m + row) : 0.f;
+      tile[c][lane] = row_l < m ? load_as_float(x + int64_t(c) * plane + offset) : 0.f;
     }
     __syncthreads();
     // Each warp normalises 4 rows; lane holds channels lane*4 .. lane*4+3.
@@ -142,18 +145,24 @@ __global__ void __launch_bounds__(256) layernorm_channel_first_kernel(const Tin 
 }
 
 template <typename Tin, typename Tout>
+static int launch_channel_first(const Tin *x, int64_t rows, int64_t inner, int64_t ld, int64_t plane,
+                                const float *w, const float *b, float eps, Tout *out, cudaStream_t s) {
+  BL_REQUIRE(aligned_to(out, 8 * sizeof(Tout) / 2), "bl_layernorm: output misaligned");
+  int64_t blocks = (rows + 31) / 32, cap = int64_t(num_sms()) * 16;
+  if (blocks > cap) blocks = cap;
+  layernorm_channel_first_kernel<Tin, Tout><<<int(blocks), 256, 0, s>>>(x, w, b, out, rows, inner, ld, plane, eps);
+  BL_LAUNCH_CHECK();
+  return BL_OK;
+}
+
+template <typename Tin, typename Tout>
 static int launch_layernorm(const Tin *x, int64_t rows, int64_t cols, int channel_first, const float *w,
                             const float *b, float eps, Tout *out, cudaStream_t s) {
   const int threads = 256;
   int64_t cap = int64_t(num_sms()) * 16;
   if (channel_first) {
     BL_REQUIRE(cols == 128, "bl_layernorm: channel-first input needs 128 channels");
-    BL_REQUIRE(aligned_to(out, 8 * sizeof(Tout) / 2), "bl_layernorm: output misaligned");
-    int64_t blocks = (rows + 31) / 32;
-    if (blocks > cap) blocks = cap;
-    layernorm_channel_first_kernel<Tin, Tout><<<int(blocks), threads, 0, s>>>(x, w, b, out, rows, eps);
-    BL_LAUNCH_CHECK();
-    return BL_OK;
+    return launch_channel_first(x, rows, rows, rows, rows, w, b, eps, out, s);
   }
   int64_t blocks = (rows + 7) / 8;
   if (blocks > cap) blocks = cap;
@@ -207,4 +216,17 @@ extern "C" int bl_layernorm(const void *x, int x_dtype, int64_t rows, int64_t co
                             static_cast<float *>(out), s);
   return launch_layernorm(static_cast<const __nv_bfloat16 *>(x), rows, cols, channel_first, weight, bias, eps,
                           static_cast<__nv_bfloat16 *>(out), s);
+}
+
+extern "C" int bl_layernorm_planes(const void *planes, int64_t n, int64_t ld, const float *weight, const float *bias,
+                                   float eps, void *out, int out_dtype, void *stream) {
+  BL_REQUIRE(out_dtype == BL_F32 || out_dtype == BL_BF16, "bl_layernorm_planes: bad output dtype");
+  BL_REQUIRE(n >= 0 && ld >= n && eps > 0.f, "bl_layernorm_planes: bad shape");
+  if (n == 0) return BL_OK;
+  BL_REQUIRE(planes && out, "bl_layernorm_planes: null pointer");
+  auto x = static_cast<const __nv_bfloat16 *>(planes);
+  auto s = as_stream(stream);
+  if (out_dtype == BL_F32)
+    return launch_channel_first(x, n * n, n, ld, n * ld, weight, bias, eps, static_cast<float *>(out), s);
+  return launch_channel_first(x, n * n, n, ld, n * ld, weight, bias, eps, static_cast<__nv_bfloat16 *>(out), s);
 }

@@ -1,0 +1,366 @@
+// Flash triangle attention (starting and ending node) with the upstream bf16
+// rounding points and the fused sigmoid output gate.
+//
+// For every outer row a of the pair tensor, head h and query b:
+//   s(b, c) = bf16(q_s(a, b) . k(a, c))                    q_s = bf16(q / sqrt(d))
+//   t(b, c) = bf16(bf16(s + inf * (mask(a, c) - 1)) + bias(h, b, c))
+//   o(a, b) = bf16(sum_c softmax_c(t) v(a, c))
+//   out(a, b) = bf16(o * bf16(sigmoid(g(a, b))))
+// This is the reference's ordered_triangle_forward (triangle.py:32-104 and
+// kernels/triangle_softmax.py:90-113) plus upstream _wrap_up's gate, without
+// materialising the [I, H, N, N] scores.  The ending node is the same
+// computation on z transposed; the caller expresses it through row strides
+// (pair row of (outer, inner) = outer * so + inner * si) and a transposed bias
+// plane, so no transposed copy of z or of q/k/v is made.
+//
+// Head dim 32 makes the core exp/ALU-bound rather than tensor-bound, so this
+// version keeps the two small contractions on mma.sync m16n8k16 (bf16 in,
+// fp32 accumulate) and spends its issue slots on the softmax.
+#include "common.cuh"
+
+namespace bl {
+namespace {
+
+constexpr int kD = 32;
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kBQ = kWarps * 16;  // 128 queries per CTA
+constexpr int kBK = 64;           // keys per tile
+constexpr int kBiasLd = kBK + 8;  // padded smem row (144 B): conflict-free fragment reads
+
+struct FlashArgs {
+  const __nv_bfloat16 *q, *k, *v, *g;
+  int64_t ld;      // elements per pair row of q/k/v/g; head h at columns [h*32, h*32+32)
+  int64_t so, si;  // pair row of (outer, inner)
+  const __nv_bfloat16 *bias;  // bias(h, q, k) at bias + h*bias_hs + q*bias_ld + k
+  int64_t bias_ld, bias_hs;
+  const float *mask;  // mask(outer, key) at mask + outer*ms_o + key*ms_k
+  int64_t ms_o, ms_k;
+  float inf;
+  float q_divisor;
+  __nv_bfloat16 *out;
+  int64_t out_ld;
+  int n;
+};
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return uint32_t(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_addr(p)));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_addr(p)));
+}
+
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// [rows][32] bf16 tile, 4 chunks of 16 B per row, chunk c of row r stored at
+// c ^ ((r >> 1) & 3): conflict-free for ldmatrix row groups of 8.
+__device__ __forceinline__ int qkv_chunk_offset(int row, int chunk) {
+  return row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4);
+}
+
+struct Smem {
+  alignas(128) __nv_bfloat16 q[kBQ * kD];
+  alignas(128) __nv_bfloat16 k[2][kBK * kD];
+  alignas(128) __nv_bfloat16 v[2][kBK * kD];
+  alignas(128) __nv_bfloat16 bias[2][kBQ * kBiasLd];
+  // followed by the per-key mask bias of this outer row (n floats, dynamic)
+};
+
+__global__ void __launch_bounds__(kThreads, 2) tri_flash_kernel(const FlashArgs args) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
+  float *mask_bias = reinterpret_cast<float *>(smem_raw + sizeof(Smem));
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n = args.n;
+  const int q0 = blockIdx.x * kBQ;
+  const int64_t outer = blockIdx.y;
+  const int h = blockIdx.z;
+  const int col0 = h * kD;
+
+  // Per-key additive mask of this outer row; padding keys get -inf.
+  const int n_tiles = (n + kBK - 1) / kBK;
+  for (int key = tid; key < n_tiles * kBK; key += kThreads)
+    mask_bias[key] = key < n ? args.inf * (args.mask[outer * args.ms_o + int64_t(key) * args.ms_k] - 1.f) : -INFINITY;
+
+  auto row_ptr = [&](const __nv_bfloat16 *base, int inner) {
+    return base + (outer * args.so + int64_t(inner) * args.si) * args.ld + col0;
+  };
+
+  // Q tile (128 rows x 4 chunks).
+  for (int c = tid; c < kBQ * 4; c += kThreads) {
+    int row = c >> 2, chunk = c & 3;
+    int qi = q0 + row;
+    bool valid = qi < n;
+    const __nv_bfloat16 *src = valid ? row_ptr(args.q, qi) + chunk * 8 : args.q;
+    cp_async16(reinterpret_cast<uint8_t *>(sm.q) + qkv_chunk_offset(row, chunk), src, valid);
+  }
+  auto load_tile = [&](int tile, int buf) {
+    const int k0 = tile * kBK;
+    {  // K and V: 64 rows x 4 chunks each, one chunk per thread per operand
+      int row = tid >> 2, chunk = tid & 3;
+      int key = k0 + row;
+      bool valid = key < n;
+      const __nv_bfloat16 *ks = valid ? row_ptr(args.k, key) + chunk * 8 : args.k;
+      const __nv_bfloat16 *vs = valid ? row_ptr(args.v, key) + chunk * 8 : args.v;
+      cp_async16(reinterpret_cast<uint8_t *>(sm.k[buf]) + qkv_chunk_offset(row, chunk), ks, valid);
+      cp_async16(reinterpret_cast<uint8_t *>(sm.v[buf]) + qkv_chunk_offset(row, chunk), vs, valid);
+    }
+    // Bias: 128 query rows x 8 chunks of 8 keys.
+    const __nv_bfloat16 *bias_h = args.bias + int64_t(h) * args.bias_hs;
+    for (int c = tid; c < kBQ * 8; c += kThreads) {
+      int row = c >> 3, chunk = c & 7;
+      int qi = q0 + row, key = k0 + chunk * 8;
+      bool valid = qi < n && key < args.bias_ld;
+      const __nv_bfloat16 *src = valid ? bias_h + int64_t(qi) * args.bias_ld + key : args.bias;
+      cp_async16(sm.bias[buf] + row * kBiasLd + chunk * 8, src, valid);
+    }
+  };
+
+  load_tile(0, 0);
+  cp_async_commit();
+
+  // Per-thread state: rows g = lane/4 and g+8 of this warp's 16 queries.
+  const int g = lane >> 2, t = lane & 3;
+  float o_acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o_acc[i][j] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  uint32_t qf[2][4];
+  constexpr float kLog2e = 1.4426950408889634f;
+
+  for (int tile = 0; tile < n_tiles; ++tile) {
+    const int buf = tile & 1;
+    if (tile + 1 < n_tiles) load_tile(tile + 1, buf ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+
+    if (tile == 0) {
+      // Q fragments, scaled and re-rounded as upstream's in-place q /= sqrt(d).
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+        int row = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        int chunk = ks * 2 + (lane >> 4);
+        ldmatrix_x4(qf[ks], reinterpret_cast<uint8_t *>(sm.q) + qkv_chunk_offset(row, chunk));
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+          qf[ks][r] = pack_bf16x2(__fdiv_rn(bf16_lo(qf[ks][r]), args.q_divisor),
+                                  __fdiv_rn(bf16_hi(qf[ks][r]), args.q_divisor));
+      }
+    }
+
+    // S = Q K^T for 64 keys: 8 n-tiles of 8 keys.
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+      uint32_t kf[4];
+      int row = j * 8 + (lane & 7);
+      ldmatrix_x4(kf, reinterpret_cast<uint8_t *>(sm.k[buf]) + qkv_chunk_offset(row, lane >> 3));
+      mma_bf16(s[j], qf[0], kf[0], kf[1]);
+      mma_bf16(s[j], qf[1], kf[2], kf[3]);
+    }
+
+    // Ordered rounding: bf16(s) -> +mask -> bf16 -> +bias -> bf16.
+    const int k0 = tile * kBK;
+    const __nv_bfloat16 *brow0 = sm.bias[buf] + (warp * 16 + g) * kBiasLd;
+    const __nv_bfloat16 *brow1 = brow0 + 8 * kBiasLd;
+    float tile_max[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int kl = j * 8 + 2 * t;
+      const float mb0 = mask_bias[k0 + kl], mb1 = mask_bias[k0 + kl + 1];
+      const uint32_t b0 = *reinterpret_cast<const uint32_t *>(brow0 + kl);
+      const uint32_t b1 = *reinterpret_cast<const uint32_t *>(brow1 + kl);
+      // Keys past n (last tile only) are removed whatever the padding holds.
+      const bool live0 = k0 + kl < n, live1 = k0 + kl + 1 < n;
+      s[j][0] = live0 ? bf16r(bf16r(bf16r(s[j][0]) + mb0) + bf16_lo(b0)) : -INFINITY;
+      s[j][1] = live1 ? bf16r(bf16r(bf16r(s[j][1]) + mb1) + bf16_hi(b0)) : -INFINITY;
+      s[j][2] = live0 ? bf16r(bf16r(bf16r(s[j][2]) + mb0) + bf16_lo(b1)) : -INFINITY;
+      s[j][3] = live1 ? bf16r(bf16r(bf16r(s[j][3]) + mb1) + bf16_hi(b1)) : -INFINITY;
+      tile_max[0] = fmaxf(tile_max[0], fmaxf(s[j][0], s[j][1]));
+      tile_max[1] = fmaxf(tile_max[1], fmaxf(s[j][2], s[j][3]));
+    }
+    float alpha[2], m_scaled[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      tile_max[r] = fmaxf(tile_max[r], __shfl_xor_sync(0xffffffffu, tile_max[r], 1));
+      tile_max[r] = fmaxf(tile_max[r], __shfl_xor_sync(0xffffffffu, tile_max[r], 2));
+      const float m_new = fmaxf(m_run[r], tile_max[r]);
+      alpha[r] = fast_exp2((m_run[r] - m_new) * kLog2e);
+      m_run[r] = m_new;
+      m_scaled[r] = m_new * kLog2e;
+      l_run[r] *= alpha[r];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      o_acc[i][0] *= alpha[0], o_acc[i][1] *= alpha[0];
+      o_acc[i][2] *= alpha[1], o_acc[i][3] *= alpha[1];
+    }
+    // P = exp(t - m) in bf16 as the A operand of P V.
+    uint32_t pf[4][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float p0 = fast_exp2(fmaf(s[j][0], kLog2e, -m_scaled[0]));
+      float p1 = fast_exp2(fmaf(s[j][1], kLog2e, -m_scaled[0]));
+      float p2 = fast_exp2(fmaf(s[j][2], kLog2e, -m_scaled[1]));
+      float p3 = fast_exp2(fmaf(s[j][3], kLog2e, -m_scaled[1]));
+      l_run[0] += p0 + p1;
+      l_run[1] += p2 + p3;
+      const int kk = j >> 1, hi = j & 1;
+      pf[kk][hi * 2 + 0] = pack_bf16x2(p0, p1);
+      pf[kk][hi * 2 + 1] = pack_bf16x2(p2, p3);
+    }
+    // O += P V: 4 k-steps of 16 keys x 4 n-tiles of 8 head channels.
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t a[4] = {pf[kk][0], pf[kk][1], pf[kk][2], pf[kk][3]};
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        uint32_t vf[4];
+        int row = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        int chunk = np * 2 + (lane >> 4);
+        ldmatrix_x4_trans(vf, reinterpret_cast<uint8_t *>(sm.v[buf]) + qkv_chunk_offset(row, chunk));
+        mma_bf16(o_acc[np * 2 + 0], a, vf[0], vf[1]);
+        mma_bf16(o_acc[np * 2 + 1], a, vf[2], vf[3]);
+      }
+    }
+    __syncthreads();
+  }
+
+  // Normalise, round, gate, store.
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 1);
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 2);
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int qi = q0 + warp * 16 + g + r * 8;
+    if (qi >= n) continue;
+    const float inv = 1.f / l_run[r];
+    const int64_t pair = outer * args.so + int64_t(qi) * args.si;
+    const __nv_bfloat16 *grow = args.g + pair * args.ld + col0;
+    __nv_bfloat16 *orow = args.out + pair * args.out_ld + col0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int d = i * 8 + 2 * t;
+      const uint32_t gv = *reinterpret_cast<const uint32_t *>(grow + d);
+      float o0 = bf16r(o_acc[i][r * 2 + 0] * inv), o1 = bf16r(o_acc[i][r * 2 + 1] * inv);
+      float g0 = bf16r(sigmoidf_fast(bf16_lo(gv))), g1 = bf16r(sigmoidf_fast(bf16_hi(gv)));
+      *reinterpret_cast<uint32_t *>(orow + d) = pack_bf16x2(o0 * g0, o1 * g1);
+    }
+  }
+}
+
+// Bias planes from the pair-major projection: natural[h][r][s] = tb[r*n + s][h]
+// (starting node) or transposed[h][s][r] (ending node), rows padded to `ld`.
+__global__ void bias_planes_kernel(const __nv_bfloat16 *tb, int64_t tb_ld, int heads, int n, int transpose,
+                                   __nv_bfloat16 *out, int64_t ld) {
+  __shared__ __nv_bfloat16 tile[32][33];
+  const int r0 = blockIdx.y * 32, s0 = blockIdx.x * 32, h = blockIdx.z;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+  for (int y = ty; y < 32; y += 8) {
+    int r = r0 + y, s = s0 + tx;
+    tile[y][tx] = (r < n && s < n) ? tb[(int64_t(r) * n + s) * tb_ld + h] : __float2bfloat16_rn(0.f);
+  }
+  __syncthreads();
+  __nv_bfloat16 *plane = out + int64_t(h) * n * ld;
+  for (int y = ty; y < 32; y += 8) {
+    if (!transpose) {
+      int r = r0 + y, s = s0 + tx;
+      if (r < n && s < n) plane[int64_t(r) * ld + s] = tile[y][tx];
+    } else {
+      int row = s0 + y, col = r0 + tx;  // out[s][r]
+      if (row < n && col < n) plane[int64_t(row) * ld + col] = tile[tx][y];
+    }
+  }
+}
+
+}  // namespace
+}  // namespace bl
+
+using namespace bl;
+
+extern "C" int bl_triangle_bias_planes(const void *tb, int64_t tb_ld, int64_t heads, int64_t n, int transpose,
+                                       void *out, int64_t ld, void *stream) {
+  BL_REQUIRE(n >= 0 && heads > 0 && heads <= 64, "bl_triangle_bias_planes: bad shape");
+  if (n == 0) return BL_OK;
+  BL_REQUIRE(tb && out, "bl_triangle_bias_planes: null pointer");
+  BL_REQUIRE(ld >= n && tb_ld >= heads, "bl_triangle_bias_planes: bad leading dimension");
+  dim3 grid((n + 31) / 32, (n + 31) / 32, heads);
+  bias_planes_kernel<<<grid, 256, 0, as_stream(stream)>>>(static_cast<const __nv_bfloat16 *>(tb), tb_ld, int(heads),
+                                                         int(n), transpose, static_cast<__nv_bfloat16 *>(out), ld);
+  BL_LAUNCH_CHECK();
+  return BL_OK;
+}
+
+extern "C" int bl_triangle_attention(const void *q, const void *k, const void *v, const void *g, int64_t ld,
+                                     int64_t so, int64_t si, const void *bias, int64_t bias_ld, int64_t bias_hs,
+                                     const float *mask, int64_t ms_o, int64_t ms_k, float inf, int64_t heads,
+                                     int64_t head_dim, int64_t n, void *out, int64_t out_ld, void *stream) {
+  BL_REQUIRE(head_dim == kD, "bl_triangle_attention: head_dim must be 32");
+  BL_REQUIRE(n >= 0 && heads > 0 && heads <= 65535, "bl_triangle_attention: bad shape");
+  if (n == 0) return BL_OK;
+  BL_REQUIRE(n <= 65535, "bl_triangle_attention: at most 65535 tokens");
+  BL_REQUIRE(q && k && v && g && bias && mask && out, "bl_triangle_attention: null pointer");
+  BL_REQUIRE(ld % 8 == 0 && out_ld % 2 == 0 && bias_ld % 8 == 0 && bias_ld >= n,
+             "bl_triangle_attention: leading dimensions must keep 16-byte rows");
+  BL_REQUIRE(aligned_to(q, 16) && aligned_to(k, 16) && aligned_to(v, 16) && aligned_to(bias, 16) &&
+                 aligned_to(g, 4) && aligned_to(out, 4),
+             "bl_triangle_attention: misaligned pointer");
+  BL_REQUIRE(bias_hs % 8 == 0, "bl_triangle_attention: bias head stride must be a multiple of 8");
+  FlashArgs args;
+  args.q = static_cast<const __nv_bfloat16 *>(q);
+  args.k = static_cast<const __nv_bfloat16 *>(k);
+  args.v = static_cast<const __nv_bfloat16 *>(v);
+  args.g = static_cast<const __nv_bfloat16 *>(g);
+  args.ld = ld, args.so = so, args.si = si;
+  args.bias = static_cast<const __nv_bfloat16 *>(bias);
+  args.bias_ld = bias_ld, args.bias_hs = bias_hs;
+  args.mask = mask, args.ms_o = ms_o, args.ms_k = ms_k;
+  args.inf = inf;
+  args.q_divisor = sqrtf(float(head_dim));
+  args.out = static_cast<__nv_bfloat16 *>(out);
+  args.out_ld = out_ld;
+  args.n = int(n);
+  const int n_tiles = int((n + kBK - 1) / kBK);
+  const size_t smem = sizeof(Smem) + size_t(n_tiles) * kBK * sizeof(float);
+  BL_REQUIRE(smem <= 227 * 1024, "bl_triangle_attention: too many tokens for the mask buffer");
+  BL_CUDA(ensure_smem_limit(reinterpret_cast<const void *>(tri_flash_kernel), int(227 * 1024)));
+  dim3 grid(unsigned((n + kBQ - 1) / kBQ), unsigned(n), unsigned(heads));
+  tri_flash_kernel<<<grid, kThreads, smem, as_stream(stream)>>>(args);
+  BL_LAUNCH_CHECK();
+  return BL_OK;
+}

@@ -1,0 +1,205 @@
+"""Standalone modules with upstream Boltz-2 constructors and parameter names.
+
+They let the B200 path run without the upstream package installed (tests,
+benchmarks, other hosts) and load upstream ``state_dict``s unchanged.  Their
+forwards are the kernel-backed functions of :mod:`boltz_lumi_b200.forwards`;
+they are inference-only and raise rather than fall back to eager code.
+"""
+
+import math
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from . import forwards, kernels
+
+
+def _inference_only(module):
+    if module.training or torch.is_grad_enabled():
+        raise RuntimeError(f"{type(module).__name__}: the B200 kernels are inference-only; "
+                           "use torch.inference_mode() and module.eval()")
+
+
+class LayerNorm(nn.LayerNorm):
+    """LayerNorm exposing ``c_in`` like the triangle-attention variant upstream."""
+
+    def __init__(self, c_in, eps=1e-5, elementwise_affine=True, bias=True):
+        super().__init__(c_in, eps=eps, elementwise_affine=elementwise_affine, bias=bias)
+        self.c_in = (c_in,)
+
+
+class Attention(nn.Module):
+    """Parameter container of the gated triangle attention (``mha``)."""
+
+    def __init__(self, c_q, c_k, c_v, c_hidden, no_heads):
+        super().__init__()
+        self.c_q, self.c_hidden, self.no_heads = c_q, c_hidden, no_heads
+        self.linear_q = nn.Linear(c_q, c_hidden * no_heads, bias=False)
+        self.linear_k = nn.Linear(c_k, c_hidden * no_heads, bias=False)
+        self.linear_v = nn.Linear(c_v, c_hidden * no_heads, bias=False)
+        self.linear_o = nn.Linear(c_hidden * no_heads, c_q)
+        self.linear_g = nn.Linear(c_q, c_hidden * no_heads)
+
+
+class TriangleAttention(nn.Module):
+    starting = True
+
+    def __init__(self, c_in, c_hidden, no_heads, starting=None, inf=1e9):
+        super().__init__()
+        if starting is not None:
+            self.starting = starting
+        self.c_in, self.c_hidden, self.no_heads, self.inf = c_in, c_hidden, no_heads, inf
+        self.layer_norm = LayerNorm(c_in)
+        self.linear = nn.Linear(c_in, no_heads, bias=False)
+        self.mha = Attention(c_in, c_in, c_in, c_hidden, no_heads)
+
+    def forward(self, x, mask=None, chunk_size=None, use_kernels=False):
+        _inference_only(self)
+        return forwards.triangle_attention_forward(self, x, mask, chunk_size, use_kernels)
+
+
+class TriangleAttentionEndingNode(TriangleAttention):
+    starting = False
+
+
+class _TriangleMultiplication(nn.Module):
+    outgoing = True
+
+    def __init__(self, dim=128):
+        super().__init__()
+        self.norm_in = nn.LayerNorm(dim, eps=1e-5)
+        self.p_in = nn.Linear(dim, 2 * dim, bias=False)
+        self.g_in = nn.Linear(dim, 2 * dim, bias=False)
+        self.norm_out = nn.LayerNorm(dim)
+        self.p_out = nn.Linear(dim, dim, bias=False)
+        self.g_out = nn.Linear(dim, dim, bias=False)
+
+    def forward(self, x, mask, use_kernels=False):
+        _inference_only(self)
+        return forwards.triangle_multiplication_forward(self, x, mask, use_kernels)
+
+
+class TriangleMultiplicationOutgoing(_TriangleMultiplication):
+    outgoing = True
+
+
+class TriangleMultiplicationIncoming(_TriangleMultiplication):
+    outgoing = False
+
+
+class Transition(nn.Module):
+    def __init__(self, dim=128, hidden=512, out_dim=None):
+        super().__init__()
+        out_dim = out_dim or dim
+        self.norm = nn.LayerNorm(dim, eps=1e-5)
+        self.fc1 = nn.Linear(dim, hidden, bias=False)
+        self.fc2 = nn.Linear(dim, hidden, bias=False)
+        self.fc3 = nn.Linear(hidden, out_dim, bias=False)
+        self.silu = nn.SiLU()
+        self.hidden = hidden
+
+    def forward(self, x, chunk_size=None):
+        _inference_only(self)
+        return forwards.transition_forward(self, x, chunk_size)
+
+
+class AdaLN(nn.Module):
+    def __init__(self, dim, dim_single_cond):
+        super().__init__()
+        self.a_norm = nn.LayerNorm(dim, elementwise_affine=False, bias=False)
+        self.s_norm = nn.LayerNorm(dim_single_cond, bias=False)
+        self.s_scale = nn.Linear(dim_single_cond, dim)
+        self.s_bias = nn.Linear(dim_single_cond, dim, bias=False)
+
+    def forward(self, a, s):
+        _inference_only(self)
+        return forwards.adaln_forward(self, a, s)
+
+
+class ConditionedTransitionBlock(nn.Module):
+    def __init__(self, dim_single, dim_single_cond, expansion_factor=2):
+        super().__init__()
+        self.adaln = AdaLN(dim_single, dim_single_cond)
+        inner = int(dim_single * expansion_factor)
+        self.swish_gate = nn.Sequential(nn.Linear(dim_single, inner * 2, bias=False))
+        self.a_to_b = nn.Linear(dim_single, inner, bias=False)
+        self.b_to_a = nn.Linear(inner, dim_single, bias=False)
+        self.output_projection = nn.Sequential(nn.Linear(dim_single_cond, dim_single), nn.Sigmoid())
+
+    def forward(self, a, s):
+        _inference_only(self)
+        return forwards.conditioned_transition_forward(self, a, s)
+
+
+class AttentionPairBias(nn.Module):
+    """fp32 single-track attention with pair bias (upstream attentionv2)."""
+
+    def __init__(self, c_s, c_z=None, num_heads=None, inf=1e6, compute_pair_bias=True):
+        super().__init__()
+        self.c_s, self.num_heads, self.head_dim, self.inf = c_s, num_heads, c_s // num_heads, inf
+        self.compute_pair_bias = compute_pair_bias
+        self.proj_q = nn.Linear(c_s, c_s)
+        self.proj_k = nn.Linear(c_s, c_s, bias=False)
+        self.proj_v = nn.Linear(c_s, c_s, bias=False)
+        self.proj_g = nn.Linear(c_s, c_s, bias=False)
+        if compute_pair_bias:
+            self.proj_z = nn.Sequential(nn.LayerNorm(c_z), nn.Linear(c_z, num_heads, bias=False))
+        self.proj_o = nn.Linear(c_s, c_s, bias=False)
+
+    def forward(self, s, z, mask, k_in):
+        _inference_only(self)
+        b = s.shape[0]
+        q = F.linear(s, self.proj_q.weight, self.proj_q.bias).view(b, -1, self.num_heads, self.head_dim)
+        k = F.linear(k_in, self.proj_k.weight).view(b, -1, self.num_heads, self.head_dim)
+        v = F.linear(k_in, self.proj_v.weight).view(b, -1, self.num_heads, self.head_dim)
+        if self.compute_pair_bias:
+            ln, lin = self.proj_z[0], self.proj_z[1]
+            zn = kernels.layer_norm(z.float().contiguous(), ln.weight, ln.bias, ln.eps, out_dtype=torch.float32)
+            bias = F.linear(zn, lin.weight).permute(0, 3, 1, 2)
+        else:
+            bias = z
+        g = torch.sigmoid(F.linear(s, self.proj_g.weight))
+        attn = torch.einsum("bihd,bjhd->bhij", q, k) / math.sqrt(self.head_dim) + bias
+        attn = attn + (1 - mask[:, None, None].float()) * -self.inf
+        o = torch.einsum("bhij,bjhd->bihd", attn.softmax(dim=-1), v).reshape(b, -1, self.c_s)
+        return F.linear(g * o, self.proj_o.weight)
+
+
+class _FP32Transition(Transition):
+    """Single-track transition: upstream runs it in fp32 without autocast."""
+
+    def forward(self, x, chunk_size=None):
+        _inference_only(self)
+        xn = kernels.layer_norm(x.contiguous(), self.norm.weight, self.norm.bias, self.norm.eps,
+                                out_dtype=torch.float32)
+        h = F.silu(F.linear(xn, self.fc1.weight)) * F.linear(xn, self.fc2.weight)
+        return F.linear(h, self.fc3.weight)
+
+
+class PairformerLayer(nn.Module):
+    """One Boltz-2 Pairformer block; pair updates are added to z in fp32."""
+
+    def __init__(self, token_s=384, token_z=128, num_heads=16, pairwise_head_width=32, pairwise_num_heads=4):
+        super().__init__()
+        self.pre_norm_s = nn.LayerNorm(token_s)
+        self.attention = AttentionPairBias(token_s, token_z, num_heads)
+        self.tri_mul_out = TriangleMultiplicationOutgoing(token_z)
+        self.tri_mul_in = TriangleMultiplicationIncoming(token_z)
+        self.tri_att_start = TriangleAttention(token_z, pairwise_head_width, pairwise_num_heads)
+        self.tri_att_end = TriangleAttentionEndingNode(token_z, pairwise_head_width, pairwise_num_heads)
+        self.transition_s = _FP32Transition(token_s, token_s * 4)
+        self.transition_z = Transition(token_z, token_z * 4)
+
+    def forward(self, s, z, mask, pair_mask):
+        _inference_only(self)
+        z = z.add_(self.tri_mul_out(z, pair_mask))
+        z = z.add_(self.tri_mul_in(z, pair_mask))
+        z = z.add_(self.tri_att_start(z, pair_mask))
+        z = z.add_(self.tri_att_end(z, pair_mask))
+        z = z.add_(self.transition_z(z))
+        s_normed = kernels.layer_norm(s.contiguous(), self.pre_norm_s.weight, self.pre_norm_s.bias,
+                                      self.pre_norm_s.eps, out_dtype=torch.float32)
+        s = s + self.attention(s_normed, z, mask, s_normed)
+        s = s + self.transition_s(s)
+        return s, z

@@ -149,6 +149,62 @@ BL_API int bl_batched_gemm(const void *a, int a_mn_major, int64_t a_ld, int64_t 
                            int64_t c_ld, int64_t c_batch_stride, int64_t batch, int64_t m, int64_t n,
                            int64_t k, const float *bias, void *stream);
 
+/*
+ * LayerNorm over 128 channel planes (bf16 [128][n][ld], the per-channel
+ * matmul output of the triangle multiplication) into pair rows [n*n, 128].
+ * Replaces the channel-first norm call of multiplication.py:124-133.
+ */
+BL_API int bl_layernorm_planes(const void *planes, int64_t n, int64_t ld, const float *weight,
+                               const float *bias, float eps, void *out, int out_dtype, void *stream);
+
+/*
+ * Gate + mask the joint p|g projection (bf16 rows of pg_ld >= 512 elements:
+ * p in columns 0..255, g in 256..511) into natural channel-first planes
+ * a, b: bf16 [128][n][plane_ld], a[c][r][s] = bf16(gate(p, g)[r, s, c] * mask[r, s]).
+ * Replaces the gate/pack/split + layout-copy stage of multiplication.py:103-119;
+ * the outgoing and incoming products then read the same planes K-major or
+ * MN-major (bl_batched_gemm) instead of transposed copies.
+ */
+BL_API int bl_trimul_pack_planes(const void *pg, int64_t pg_ld, const float *mask, int64_t n,
+                                 int64_t plane_ld, void *a_planes, void *b_planes, void *stream);
+
+/*
+ * Pair-transition activation on the joint fc1|fc2 projection:
+ *   out[r][c] = bf16(bf16(silu(x[r][c])) * x[r][width + c]).
+ * Replaces kernels/pair_hip.cu:42 `pair_silu_mul` on separate fc1/fc2
+ * outputs (pair_transition.py:157-165).
+ */
+BL_API int bl_swiglu_rows(const void *x, int64_t x_ld, int64_t rows, int64_t width, void *out,
+                          int64_t out_ld, void *stream);
+
+/*
+ * Triangle-bias planes from the pair-major projection tb (bf16, head h in
+ * column h of rows of tb_ld): out[h][r][s] = tb[r*n + s][h], or the transpose
+ * out[h][s][r] for the ending node; rows padded to ld (>= n).
+ * Replaces the permute_final_dims of upstream TriangleAttention.forward that
+ * feeds tri_bias into triangle.py:32.
+ */
+BL_API int bl_triangle_bias_planes(const void *tb, int64_t tb_ld, int64_t heads, int64_t n,
+                                   int transpose, void *out, int64_t ld, void *stream);
+
+/*
+ * Flash triangle attention with fused output gate (bf16):
+ *   out(a, b) = bf16(bf16(softmax_c(bf16(bf16(q_s . k + inf*(mask-1)) + bias)) v)
+ *                    * bf16(sigmoid(g)))
+ * Replaces triangle.py:139 `ordered_triangle_forward` (q k^T, ordered bias
+ * softmax, p v) and the gate of upstream Attention._wrap_up.  q, k, v, g:
+ * bf16 pair rows of ld elements, head h at columns h*32..h*32+31, pair row of
+ * (outer a, inner b) = a*so + b*si (starting node: so = n, si = 1; ending
+ * node: so = 1, si = n).  bias(h, b, c) at bias + h*bias_hs + b*bias_ld + c.
+ * mask(a, c) at mask + a*ms_o + c*ms_k (fp32).  out rows of out_ld elements
+ * at the same pair rows.  head_dim must be 32.
+ */
+BL_API int bl_triangle_attention(const void *q, const void *k, const void *v, const void *g, int64_t ld,
+                                 int64_t so, int64_t si, const void *bias, int64_t bias_ld,
+                                 int64_t bias_hs, const float *mask, int64_t ms_o, int64_t ms_k,
+                                 float inf, int64_t heads, int64_t head_dim, int64_t n, void *out,
+                                 int64_t out_ld, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -125,8 +125,13 @@ class TriangleAttention(nn.Module):
         self.linear = nn.Linear(c_in, no_heads, bias=False)
         self.mha = Attention(c_in, c_in, c_in, c_hidden, no_heads)
 
-    def forward(self, x, mask=None, chunk_size=None, bf16=True, row_chunk=64):
-        """x: [B, N, N, C] fp32; mask: [B, N, N].  Returns the bf16-valued update."""
+    def forward(self, x, mask=None, chunk_size=None, bf16=True, row_chunk=64, rows=None):
+        """x: [B, N, N, C] fp32; mask: [B, N, N].  Returns the bf16-valued update.
+
+        ``rows`` limits the computation to the first outer rows (of z, or of z
+        transposed for the ending node); the CPU-baseline timing uses it to
+        extrapolate from a bounded sample.
+        """
         if mask is None:
             mask = x.new_ones(x.shape[:-1])
         if not self.starting:
@@ -138,9 +143,11 @@ class TriangleAttention(nn.Module):
         # Row chunking is exact: rows of the pair tensor attend independently
         # (upstream chunk_layer, triangle.py:81-86); it only bounds CPU memory.
         outs = []
-        for i0 in range(0, x.shape[-3], row_chunk):
-            xs = x[..., i0:i0 + row_chunk, :, :]
-            outs.append(self.mha(xs, xs, tri_bias, mask_bias[..., i0:i0 + row_chunk, :, :, :], bf16))
+        limit = x.shape[-3] if rows is None else min(rows, x.shape[-3])
+        for i0 in range(0, limit, row_chunk):
+            i1 = min(i0 + row_chunk, limit)
+            xs = x[..., i0:i1, :, :]
+            outs.append(self.mha(xs, xs, tri_bias, mask_bias[..., i0:i1, :, :, :], bf16))
         out = torch.cat(outs, dim=-3)
         if not self.starting:
             out = out.transpose(-2, -3)

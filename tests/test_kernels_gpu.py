@@ -40,7 +40,7 @@ def test_layer_norm_rows(cols, in_dtype, out_dtype):
     if out_dtype == torch.float32:
         assert_close(actual, expected, atol=1e-5)
     else:
-        assert_close(actual.float(), numerics.bf16_round(expected), atol=1e-6, rtol=BF16_ULP)
+        assert_close(actual.float(), numerics.bf16_round(expected), atol=1e-6, rtol=2 * BF16_ULP)
 
 
 @pytest.mark.parametrize("m", [1, 17, 1000, 4099])
@@ -54,7 +54,7 @@ def test_norm_channel_first(m):
     assert_close(actual, expected, atol=1e-5)
     actual = kernels.norm(x.bfloat16().cuda(), w.cuda(), b.cuda(), 1e-5, channel_first=True, bf16_output=True)
     expected = torch.nn.functional.layer_norm(x.bfloat16().float().t(), (128,), w, b, 1e-5)
-    assert_close(actual.float(), numerics.bf16_round(expected), atol=1e-6, rtol=BF16_ULP)
+    assert_close(actual.float(), numerics.bf16_round(expected), atol=1e-6, rtol=2 * BF16_ULP)
 
 
 def test_norm_without_affine_and_empty():
