@@ -35,7 +35,10 @@ SIGNATURES = {
     "bl_triangle_softmax": [_p, c_int, c_int64, c_int64, c_int64, c_int64, _i64p, _p, _i64p, _p, _i64p, _p, _p],
     "bl_batched_gemm": [_p, c_int, c_int64, c_int64, _p, c_int, c_int64, c_int64, _p, c_int64, c_int64,
                         c_int64, c_int64, c_int64, c_int64, _p, _p],
+    "bl_linear_fused": [_p, c_int64, _p, c_int64, c_int64, _p, c_int64, c_int64, c_int64, c_int64, _p, c_int, _p,
+                        c_int64, _p, c_int64, _p],
     "bl_layernorm_planes": [_p, c_int64, c_int64, _p, _p, c_float, _p, c_int, _p],
+    "bl_layernorm_heads": [_p, c_int64, _p, _p, c_float, _p, c_int64, c_int, _p, _p, c_int64, _p],
     "bl_trimul_pack_planes": [_p, c_int64, _p, c_int64, c_int64, _p, _p, _p],
     "bl_swiglu_rows": [_p, c_int64, c_int64, c_int64, _p, c_int64, _p],
     "bl_triangle_bias_planes": [_p, c_int64, c_int64, c_int64, c_int, _p, c_int64, _p],

@@ -1,19 +1,27 @@
 // Batched bf16 GEMM on tcgen05 tensor cores with TMA-fed operands.
 //
-//   C[b](m, n) = sum_k A[b](m, k) * B[b](n, k)  (+ bias[n]),  fp32 accumulate, bf16 out
+//   acc[b](m, n) = sum_k A[b](m, k) * B[b](n, k)  (+ bias[n]),  fp32 accumulate
 //
 // A and B may each be K-major or MN-major in global memory; the MN-major form
 // lets the incoming triangle multiplication (O[i,j,c] = sum_k a[k,i,c] b[k,j,c])
-// read its channel planes without a transpose pass.  This kernel is the
-// tensor-core replacement of the reference's torch.bmm / torch.matmul calls
-// (multiplication.py:122, triangle.py:194,208).
+// read its channel planes without a transpose pass.  This kernel replaces the
+// reference's torch.bmm / torch.matmul / F.linear calls (multiplication.py:122,
+// triangle.py:194,208, pair_transition.py:158-165) and fuses what follows them:
+//
+//   EPI_STORE          C = bf16(acc + bias)
+//   EPI_RESIDUAL       Z += bf16(acc + bias)                 (fp32 Z, the pair tensor)
+//   EPI_GATE_STORE     C[:, c] = bf16(bf16(acc[c]) * bf16(sigmoid(bf16(acc[w + c]))))
+//   EPI_GATE_RESIDUAL  Z[:, c] += that value                  (w = BN / 2)
+// The gate forms are the output gate of the triangle multiplication
+// (multiplication.py:135-137): p_out and g_out computed as one GEMM.
 //
 // Persistent, warp-specialised CTA (192 threads, one per SM):
 //   warp 0      TMA producer over a STAGES-deep shared-memory ring
 //   warp 1      TMEM allocation + single-thread tcgen05.mma issue
-//   warps 2..5  epilogue: tcgen05.ld -> bf16 -> swizzled staging -> TMA store
+//   warps 2..5  epilogue: tcgen05.ld -> math -> swizzled staging -> TMA store
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
-// of tile t overlaps the main loop of tile t+1.
+// of tile t overlaps the main loop of tile t+1.  Residual epilogues TMA-load
+// the fp32 Z tile while the tile's MMAs run and TMA-store it back.
 #include "tc.cuh"
 
 namespace bl {
@@ -46,42 +54,57 @@ bool encode_tmap(CUtensorMap *map, CUtensorMapDataType type, int rank, const voi
 
 namespace {
 
+enum Epilogue { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_GATE_STORE = 2, EPI_GATE_RESIDUAL = 3 };
+
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kThreads = 192;
-constexpr int kStagingBytes = 4096;  // 32 rows x 64 bf16 per buffer
+constexpr int kStagingBytes = 4096;  // bf16 store: 32 rows x 64 bf16; residual: 32 rows x 32 fp32
 
 struct GemmArgs {
   int m, n, k, batch;
   int tiles_m, tiles_n;
+  int k_split;  // K blocks < k_split come from tma_a, the rest from tma_a2 (K-concatenated operands)
   const float *bias;
   unsigned int *status;
 };
 
-template <int BN> struct GemmShape {
+template <int BN, int EPI> struct GemmShape {
+  static constexpr bool kResidual = EPI == EPI_RESIDUAL || EPI == EPI_GATE_RESIDUAL;
+  static constexpr bool kGate = EPI == EPI_GATE_STORE || EPI == EPI_GATE_RESIDUAL;
+  static constexpr int kOutWidth = kGate ? BN / 2 : BN;  // output columns per tile
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = BN == 256 ? 3 : 5;
+  static constexpr int kStages = kResidual ? 3 : (BN == 256 ? 3 : 5);
   static constexpr int kRingBytes = kStages * kStageBytes;
-  static constexpr int kStagingTotal = 4 * 2 * kStagingBytes;
+  // Residual: every 32-column fp32 chunk of the warp's 32 rows is resident at once.
+  static constexpr int kStagingPerWarp = kResidual ? (kOutWidth / 32) * kStagingBytes : 2 * kStagingBytes;
+  static constexpr int kStagingTotal = 4 * kStagingPerWarp;
   static constexpr int kBarrierOffset = kRingBytes + kStagingTotal;
   static constexpr int kSmemBytes = kBarrierOffset + 256 + 1024;  // barriers + alignment slack
   static constexpr uint32_t kTmemCols = 2 * BN;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
-template <bool A_MN, bool B_MN, int BN>
+__device__ __forceinline__ float gate_pair(float p, float g) {
+  return bf16r(bf16r(p) * bf16r(sigmoidf_fast(bf16r(g))));
+}
+
+template <bool A_MN, bool B_MN, int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                     const __grid_constant__ CUtensorMap tma_c, const GemmArgs args) {
-  using S = GemmShape<BN>;
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_a2,
+                     const __grid_constant__ CUtensorMap tma_b, const __grid_constant__ CUtensorMap tma_c,
+                     const GemmArgs args) {
+  using S = GemmShape<BN, EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + S::kBarrierOffset);
   uint64_t *empty = full + S::kStages;
   uint64_t *acc_full = empty + S::kStages;
   uint64_t *acc_empty = acc_full + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+  uint64_t *z_full = acc_empty + 2;  // one per epilogue warp
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(z_full + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_per_batch = args.tiles_m * args.tiles_n;
@@ -97,8 +120,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::mbar_init(&acc_full[b], 1);
       tc::mbar_init(&acc_empty[b], 4);
     }
+    for (int w = 0; w < 4; ++w) tc::mbar_init(&z_full[w], 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tma_a);
+    tc::prefetch_tmap(&tma_a2);
     tc::prefetch_tmap(&tma_b);
     tc::prefetch_tmap(&tma_c);
   }
@@ -128,11 +153,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t *sb = sa + S::kABytes;
           tc::mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
           const int k0 = kb * kBK;
+          const CUtensorMap *map_a = kb < args.k_split ? &tma_a : &tma_a2;
+          const int ka = kb < args.k_split ? k0 : k0 - args.k_split * kBK;
           if constexpr (A_MN) {
-            tc::tma_load_3d(sa, &tma_a, &full[stage], m0, k0, b);
-            tc::tma_load_3d(sa + 8192, &tma_a, &full[stage], m0 + 64, k0, b);
+            tc::tma_load_3d(sa, map_a, &full[stage], m0, ka, b);
+            tc::tma_load_3d(sa + 8192, map_a, &full[stage], m0 + 64, ka, b);
           } else {
-            tc::tma_load_3d(sa, &tma_a, &full[stage], k0, m0, b);
+            tc::tma_load_3d(sa, map_a, &full[stage], ka, m0, b);
           }
           if constexpr (B_MN) {
 #pragma unroll
@@ -180,52 +207,119 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // Epilogue warps 2..5 own TMEM lane quarters (warp % 4).
     const int quarter = warp & 3;
-    uint8_t *staging = smem + S::kRingBytes + quarter * 2 * kStagingBytes;
+    uint8_t *staging = smem + S::kRingBytes + quarter * S::kStagingPerWarp;
     int acc = 0;
-    uint32_t acc_phase = 0;
+    uint32_t acc_phase = 0, z_phase = 0;
     int chunk_count = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
       const int b = tile / tiles_per_batch, rem = tile % tiles_per_batch;
       const int m0 = (rem / args.tiles_n) * kBM, n0 = (rem % args.tiles_n) * BN;
+      const int row0 = m0 + quarter * 32;
+      if constexpr (S::kResidual) {
+        // Fetch this warp's fp32 Z rows while the tile's MMAs run (the previous
+        // tile's stores must have finished reading the staging first).
+        if (lane == 0) {
+          tc::bulk_wait_read<0>();
+          tc::mbar_arrive_expect_tx(&z_full[quarter], S::kOutWidth / 32 * kStagingBytes);
+#pragma unroll
+          for (int cc = 0; cc < S::kOutWidth / 32; ++cc)
+            tc::tma_load_2d(staging + cc * kStagingBytes, &tma_c, &z_full[quarter], cc * 32, row0);
+        }
+      }
       if (!tc::mbar_wait(&acc_full[acc], acc_phase, args.status, 0x104)) break;
       tc::tc_fence_after();
+      const uint32_t tbase = tc::tmem_addr(tmem_base, quarter * 32, acc * BN);
+      if constexpr (S::kResidual) {
+        if (!tc::mbar_wait(&z_full[quarter], z_phase, args.status, 0x105)) break;
+        z_phase ^= 1u;
 #pragma unroll 1
-      for (int cc = 0; cc < BN / 64; ++cc) {
-        uint32_t r0[32], r1[32];
-        const uint32_t taddr = tc::tmem_addr(tmem_base, quarter * 32, acc * BN + cc * 64);
-        tc::tmem_ld_32x32b_x32(taddr, r0);
-        tc::tmem_ld_32x32b_x32(taddr + 32, r1);
-        tc::tmem_ld_wait();
-        uint32_t packed[32];
+        for (int cc = 0; cc < S::kOutWidth / 32; ++cc) {
+          uint32_t r[32];
+          tc::tmem_ld_32x32b_x32(tbase + cc * 32, r);
+          float out[32];
+          if constexpr (S::kGate) {
+            uint32_t gr[32];
+            tc::tmem_ld_32x32b_x32(tbase + S::kOutWidth + cc * 32, gr);
+            tc::tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float v0 = __uint_as_float(r0[2 * j]), v1 = __uint_as_float(r0[2 * j + 1]);
-          float w0 = __uint_as_float(r1[2 * j]), w1 = __uint_as_float(r1[2 * j + 1]);
-          if (args.bias) {
-            const int c = n0 + cc * 64 + 2 * j;
-            v0 += c < args.n ? args.bias[c] : 0.f;
-            v1 += c + 1 < args.n ? args.bias[c + 1] : 0.f;
-            w0 += c + 32 < args.n ? args.bias[c + 32] : 0.f;
-            w1 += c + 33 < args.n ? args.bias[c + 33] : 0.f;
+            for (int j = 0; j < 32; ++j) out[j] = gate_pair(__uint_as_float(r[j]), __uint_as_float(gr[j]));
+          } else {
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int c = n0 + cc * 32 + j;
+              out[j] = bf16r(__uint_as_float(r[j]) + (args.bias && c < args.n ? args.bias[c] : 0.f));
+            }
           }
-          packed[j] = pack_bf16x2(v0, v1);
-          packed[16 + j] = pack_bf16x2(w0, w1);
-        }
-        uint8_t *buf = staging + (chunk_count & 1) * kStagingBytes;
-        if (lane == 0) tc::bulk_wait_read<1>();
-        __syncwarp();
+          uint8_t *buf = staging + cc * kStagingBytes;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          uint4 v = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-          *reinterpret_cast<uint4 *>(buf + lane * 128 + ((j ^ (lane & 7)) * 16)) = v;
+          for (int j = 0; j < 8; ++j) {
+            float4 *p = reinterpret_cast<float4 *>(buf + lane * 128 + ((j ^ (lane & 7)) * 16));
+            float4 zv = *p;
+            zv.x += out[4 * j], zv.y += out[4 * j + 1], zv.z += out[4 * j + 2], zv.w += out[4 * j + 3];
+            *p = zv;
+          }
         }
         tc::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tc::tma_store_3d(&tma_c, buf, n0 + cc * 64, m0 + quarter * 32, b);
+#pragma unroll
+          for (int cc = 0; cc < S::kOutWidth / 32; ++cc)
+            tc::tma_store_2d(&tma_c, staging + cc * kStagingBytes, cc * 32, row0);
           tc::bulk_commit();
         }
-        ++chunk_count;
+      } else {
+#pragma unroll 1
+        for (int cc = 0; cc < S::kOutWidth / 64; ++cc) {
+          uint32_t r0[32], r1[32];
+          tc::tmem_ld_32x32b_x32(tbase + cc * 64, r0);
+          tc::tmem_ld_32x32b_x32(tbase + cc * 64 + 32, r1);
+          uint32_t packed[32];
+          if constexpr (S::kGate) {
+            uint32_t g0[32], g1[32];
+            tc::tmem_ld_32x32b_x32(tbase + S::kOutWidth + cc * 64, g0);
+            tc::tmem_ld_32x32b_x32(tbase + S::kOutWidth + cc * 64 + 32, g1);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              packed[j] = pack_bf16x2(gate_pair(__uint_as_float(r0[2 * j]), __uint_as_float(g0[2 * j])),
+                                      gate_pair(__uint_as_float(r0[2 * j + 1]), __uint_as_float(g0[2 * j + 1])));
+              packed[16 + j] = pack_bf16x2(gate_pair(__uint_as_float(r1[2 * j]), __uint_as_float(g1[2 * j])),
+                                           gate_pair(__uint_as_float(r1[2 * j + 1]), __uint_as_float(g1[2 * j + 1])));
+            }
+          } else {
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float v0 = __uint_as_float(r0[2 * j]), v1 = __uint_as_float(r0[2 * j + 1]);
+              float w0 = __uint_as_float(r1[2 * j]), w1 = __uint_as_float(r1[2 * j + 1]);
+              if (args.bias) {
+                const int c = n0 + cc * 64 + 2 * j;
+                v0 += c < args.n ? args.bias[c] : 0.f;
+                v1 += c + 1 < args.n ? args.bias[c + 1] : 0.f;
+                w0 += c + 32 < args.n ? args.bias[c + 32] : 0.f;
+                w1 += c + 33 < args.n ? args.bias[c + 33] : 0.f;
+              }
+              packed[j] = pack_bf16x2(v0, v1);
+              packed[16 + j] = pack_bf16x2(w0, w1);
+            }
+          }
+          uint8_t *buf = staging + (chunk_count & 1) * kStagingBytes;
+          if (lane == 0) tc::bulk_wait_read<1>();
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint4 v = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+            *reinterpret_cast<uint4 *>(buf + lane * 128 + ((j ^ (lane & 7)) * 16)) = v;
+          }
+          tc::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tc::tma_store_3d(&tma_c, buf, (S::kGate ? 0 : n0) + cc * 64, row0, b);
+            tc::bulk_commit();
+          }
+          ++chunk_count;
+        }
       }
       tc::tc_fence_before();
       __syncwarp();
@@ -242,15 +336,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <bool A_MN, bool B_MN, int BN>
-int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tcm, const GemmArgs &args,
-                cudaStream_t stream) {
-  using S = GemmShape<BN>;
-  auto kernel = gemm_bf16_kernel<A_MN, B_MN, BN>;
+template <bool A_MN, bool B_MN, int BN, int EPI>
+int launch_gemm(const CUtensorMap &ta, const CUtensorMap &ta2, const CUtensorMap &tb, const CUtensorMap &tcm,
+                const GemmArgs &args, cudaStream_t stream) {
+  using S = GemmShape<BN, EPI>;
+  auto kernel = gemm_bf16_kernel<A_MN, B_MN, BN, EPI>;
   BL_CUDA(ensure_smem_limit(reinterpret_cast<const void *>(kernel), S::kSmemBytes));
   int total = args.tiles_m * args.tiles_n * args.batch;
   int grid = total < num_sms() ? total : num_sms();
-  kernel<<<grid, kThreads, S::kSmemBytes, stream>>>(ta, tb, tcm, args);
+  kernel<<<grid, kThreads, S::kSmemBytes, stream>>>(ta, ta2, tb, tcm, args);
   BL_LAUNCH_CHECK();
   return BL_OK;
 }
@@ -276,6 +370,15 @@ static bool operand_map(CUtensorMap *map, const void *ptr, bool mn_major, int64_
   strides[1] = uint64_t(batch_stride) * 2;
   return encode_tmap(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ptr, dims, strides, box,
                      CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <int BN, int EPI>
+static int dispatch_majors(bool a_mn, bool b_mn, const CUtensorMap &ta, const CUtensorMap &tb,
+                           const CUtensorMap &tcm, const GemmArgs &args, cudaStream_t stream) {
+  if (a_mn && b_mn) return launch_gemm<true, true, BN, EPI>(ta, ta, tb, tcm, args, stream);
+  if (a_mn) return launch_gemm<true, false, BN, EPI>(ta, ta, tb, tcm, args, stream);
+  if (b_mn) return launch_gemm<false, true, BN, EPI>(ta, ta, tb, tcm, args, stream);
+  return launch_gemm<false, false, BN, EPI>(ta, ta, tb, tcm, args, stream);
 }
 
 int batched_gemm_bf16(const void *a, bool a_mn, int64_t a_ld, int64_t a_bs, const void *b, bool b_mn, int64_t b_ld,
@@ -314,19 +417,71 @@ int batched_gemm_bf16(const void *a, bool a_mn, int64_t a_ld, int64_t a_bs, cons
   args.m = int(m), args.n = int(n), args.k = int(k), args.batch = int(batch);
   args.tiles_m = int((m + kBM - 1) / kBM);
   args.tiles_n = int((n + bn - 1) / bn);
+  args.k_split = int((k + kBK - 1) / kBK);
   args.bias = bias;
   args.status = device_status_ptr();
   BL_REQUIRE(args.status, "gemm: device status word unavailable");
-  if (bn == 256) {
-    if (a_mn && b_mn) return launch_gemm<true, true, 256>(ta, tb, tcm, args, stream);
-    if (a_mn) return launch_gemm<true, false, 256>(ta, tb, tcm, args, stream);
-    if (b_mn) return launch_gemm<false, true, 256>(ta, tb, tcm, args, stream);
-    return launch_gemm<false, false, 256>(ta, tb, tcm, args, stream);
+  if (bn == 256) return dispatch_majors<256, EPI_STORE>(a_mn, b_mn, ta, tb, tcm, args, stream);
+  return dispatch_majors<128, EPI_STORE>(a_mn, b_mn, ta, tb, tcm, args, stream);
+}
+
+// Linear layer over pair rows with a fused epilogue (single N tile per row block).
+int linear_fused(const void *a, int64_t a_ld, const void *a2, int64_t a2_ld, int64_t k1, const void *w,
+                 int64_t w_ld, int64_t m, int64_t n, int64_t k, const float *bias, int gate, float *z, int64_t z_ld,
+                 void *out, int64_t out_ld, cudaStream_t stream) {
+  BL_REQUIRE(m >= 0 && k > 0, "linear: bad shape");
+  if (m == 0) return BL_OK;
+  BL_REQUIRE(a && w && (z || out) && !(z && out), "linear: exactly one of z (residual) and out must be given");
+  if (!a2) k1 = k;
+  BL_REQUIRE(k1 > 0 && k1 <= k && k1 % kBK == 0 || k1 == k, "linear: the A split must fall on a 64-column boundary");
+  BL_REQUIRE(gate ? n == 256 : n == 128, "linear: n must be 128 (or 256 = p|g with gate)");
+  BL_REQUIRE(!(gate && bias), "linear: the gate form takes no bias");
+  BL_REQUIRE(aligned_to(a, 16) && aligned_to(w, 16) && a_ld % 8 == 0 && w_ld % 8 == 0 && a_ld >= k && w_ld >= k,
+             "linear: operands must have 16-byte aligned rows");
+  BL_REQUIRE(m < (1ll << 31) && k < (1ll << 31), "linear: shape too large");
+  const int width = gate ? int(n / 2) : int(n);
+  CUtensorMap ta, ta2, tb, tcm;
+  BL_REQUIRE(a_ld >= k1, "linear: A leading dimension too small");
+  BL_REQUIRE(operand_map(&ta, a, false, m, k1, a_ld, a_ld * m, 1, kBM), "linear: cannot encode the A tensor map");
+  if (a2) {
+    BL_REQUIRE(aligned_to(a2, 16) && a2_ld % 8 == 0 && a2_ld >= k - k1, "linear: second A operand misaligned");
+    BL_REQUIRE(operand_map(&ta2, a2, false, m, k - k1, a2_ld, a2_ld * m, 1, kBM),
+               "linear: cannot encode the second A tensor map");
+  } else {
+    ta2 = ta;
   }
-  if (a_mn && b_mn) return launch_gemm<true, true, 128>(ta, tb, tcm, args, stream);
-  if (a_mn) return launch_gemm<true, false, 128>(ta, tb, tcm, args, stream);
-  if (b_mn) return launch_gemm<false, true, 128>(ta, tb, tcm, args, stream);
-  return launch_gemm<false, false, 128>(ta, tb, tcm, args, stream);
+  BL_REQUIRE(operand_map(&tb, w, false, n, k, w_ld, w_ld * n, 1, int(n)), "linear: cannot encode the W tensor map");
+  if (z) {
+    BL_REQUIRE(aligned_to(z, 16) && z_ld % 4 == 0 && z_ld >= width, "linear: z rows must be 16-byte aligned");
+    uint64_t dims[2] = {uint64_t(width), uint64_t(m)};
+    uint64_t strides[1] = {uint64_t(z_ld) * 4};
+    uint32_t box[2] = {32, 32};
+    BL_REQUIRE(encode_tmap(&tcm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, z, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B),
+               "linear: cannot encode the Z tensor map");
+  } else {
+    BL_REQUIRE(aligned_to(out, 16) && out_ld % 8 == 0 && out_ld >= width, "linear: out rows must be 16-byte aligned");
+    uint64_t dims[3] = {uint64_t(width), uint64_t(m), 1};
+    uint64_t strides[2] = {uint64_t(out_ld) * 2, uint64_t(out_ld) * 2 * uint64_t(m)};
+    uint32_t box[3] = {64, 32, 1};
+    BL_REQUIRE(encode_tmap(&tcm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B),
+               "linear: cannot encode the output tensor map");
+  }
+  GemmArgs args;
+  args.m = int(m), args.n = int(n), args.k = int(k), args.batch = 1;
+  args.tiles_m = int((m + kBM - 1) / kBM);
+  args.tiles_n = 1;
+  args.k_split = int(a2 ? k1 / kBK : (k + kBK - 1) / kBK);
+  args.bias = bias;
+  args.status = device_status_ptr();
+  BL_REQUIRE(args.status, "linear: device status word unavailable");
+  if (gate) {
+    if (z) return launch_gemm<false, false, 256, EPI_GATE_RESIDUAL>(ta, ta2, tb, tcm, args, stream);
+    return launch_gemm<false, false, 256, EPI_GATE_STORE>(ta, ta2, tb, tcm, args, stream);
+  }
+  if (z) return launch_gemm<false, false, 128, EPI_RESIDUAL>(ta, ta2, tb, tcm, args, stream);
+  return launch_gemm<false, false, 128, EPI_STORE>(ta, ta2, tb, tcm, args, stream);
 }
 
 }  // namespace bl
@@ -337,4 +492,11 @@ extern "C" int bl_batched_gemm(const void *a, int a_mn_major, int64_t a_ld, int6
                                const float *bias, void *stream) {
   return bl::batched_gemm_bf16(a, a_mn_major != 0, a_ld, a_batch_stride, b, b_mn_major != 0, b_ld, b_batch_stride, c,
                                c_ld, c_batch_stride, batch, m, n, k, bias, bl::as_stream(stream));
+}
+
+extern "C" int bl_linear_fused(const void *a, int64_t a_ld, const void *a2, int64_t a2_ld, int64_t k1, const void *w,
+                               int64_t w_ld, int64_t m, int64_t n, int64_t k, const float *bias, int gate, float *z,
+                               int64_t z_ld, void *out, int64_t out_ld, void *stream) {
+  return bl::linear_fused(a, a_ld, a2, a2_ld, k1, w, w_ld, m, n, k, bias, gate, z, z_ld, out, out_ld,
+                          bl::as_stream(stream));
 }

@@ -13,9 +13,14 @@
 // (pair row of (outer, inner) = outer * so + inner * si) and a transposed bias
 // plane, so no transposed copy of z or of q/k/v is made.
 //
-// Head dim 32 makes the core exp/ALU-bound rather than tensor-bound, so this
-// version keeps the two small contractions on mma.sync m16n8k16 (bf16 in,
-// fp32 accumulate) and spends its issue slots on the softmax.
+// Cost model: head dim 32 makes the core exp/ALU-bound (N^3 H exponentials vs
+// 4 N^3 H d flops), so the two small contractions stay on mma.sync m16n8k16 and
+// the score pipeline runs on packed bf16x2 arithmetic -- the rounding points
+// upstream imposes are bf16 anyway:
+//   cvt.rn.bf16x2 (s) -> add (mask) -> add (bias) -> max -> sub (max)
+//   -> mul/fma by log2(e) (two-term constant, unbiased) -> ex2.bf16x2 = P
+// P feeds the P.V mma directly, and the row sums come from one extra mma
+// against a ones fragment, so no per-element fp32 adds remain.
 #include "common.cuh"
 
 namespace bl {
@@ -74,11 +79,58 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// Packed bf16x2 arithmetic (each result rounded once to nearest-even).
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t add_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t sub_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t fma_bf16x2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+__device__ __forceinline__ uint32_t max_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t ex2_bf16x2(uint32_t a) {
+  uint32_t r;
+  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(r) : "r"(a));
+  return r;
+}
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+__device__ __forceinline__ uint32_t splat_lo(uint32_t v) { return (v & 0xffffu) | (v << 16); }
+__device__ __forceinline__ uint32_t splat_hi(uint32_t v) { return (v >> 16) | (v & 0xffff0000u); }
+
+constexpr uint32_t kOnes = 0x3F803F80u;      // bf16x2 (1, 1)
+constexpr uint32_t kNegInf = 0xFF80FF80u;    // bf16x2 (-inf, -inf): max identity
+// Padding keys get -1e30 rather than -inf so (t - m) log2(e) stays finite in
+// the two-term fma (inf - inf would give NaN); ex2 of it is exactly 0.
+constexpr uint32_t kNegPad = 0xF14AF14Au;    // bf16x2 (-1.0003e30, -1.0003e30)
+// log2(e) as an unbiased two-term bf16 constant: c1 = bf16(log2 e), c2 = bf16(log2 e - c1).
+constexpr uint32_t kLog2eHi = 0x3FB93FB9u;   // 1.4453125
+constexpr uint32_t kLog2eLo = 0xBB2CBB2Cu;   // -0.00262451171875
 
 // [rows][32] bf16 tile, 4 chunks of 16 B per row, chunk c of row r stored at
 // c ^ ((r >> 1) & 3): conflict-free for ldmatrix row groups of 8.
@@ -91,13 +143,13 @@ struct Smem {
   alignas(128) __nv_bfloat16 k[2][kBK * kD];
   alignas(128) __nv_bfloat16 v[2][kBK * kD];
   alignas(128) __nv_bfloat16 bias[2][kBQ * kBiasLd];
-  // followed by the per-key mask bias of this outer row (n floats, dynamic)
+  // followed by the per-key mask bias of this outer row (bf16, dynamic)
 };
 
 __global__ void __launch_bounds__(kThreads, 2) tri_flash_kernel(const FlashArgs args) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
-  float *mask_bias = reinterpret_cast<float *>(smem_raw + sizeof(Smem));
+  __nv_bfloat16 *mask_bias = reinterpret_cast<__nv_bfloat16 *>(smem_raw + sizeof(Smem));
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n = args.n;
@@ -106,16 +158,18 @@ __global__ void __launch_bounds__(kThreads, 2) tri_flash_kernel(const FlashArgs 
   const int h = blockIdx.z;
   const int col0 = h * kD;
 
-  // Per-key additive mask of this outer row; padding keys get -inf.
+  // Per-key additive mask of this outer row.  inf * (mask - 1) is added to the
+  // bf16 score; for mask in {0, 1} adding its bf16 value rounds identically.
+  // Padding keys are removed separately (last tile).
   const int n_tiles = (n + kBK - 1) / kBK;
   for (int key = tid; key < n_tiles * kBK; key += kThreads)
-    mask_bias[key] = key < n ? args.inf * (args.mask[outer * args.ms_o + int64_t(key) * args.ms_k] - 1.f) : -INFINITY;
+    mask_bias[key] = __float2bfloat16_rn(
+        key < n ? args.inf * (args.mask[outer * args.ms_o + int64_t(key) * args.ms_k] - 1.f) : 0.f);
 
   auto row_ptr = [&](const __nv_bfloat16 *base, int inner) {
     return base + (outer * args.so + int64_t(inner) * args.si) * args.ld + col0;
   };
 
-  // Q tile (128 rows x 4 chunks).
   for (int c = tid; c < kBQ * 4; c += kThreads) {
     int row = c >> 2, chunk = c & 3;
     int qi = q0 + row;
@@ -125,7 +179,7 @@ __global__ void __launch_bounds__(kThreads, 2) tri_flash_kernel(const FlashArgs 
   }
   auto load_tile = [&](int tile, int buf) {
     const int k0 = tile * kBK;
-    {  // K and V: 64 rows x 4 chunks each, one chunk per thread per operand
+    {
       int row = tid >> 2, chunk = tid & 3;
       int key = k0 + row;
       bool valid = key < n;
@@ -134,7 +188,6 @@ __global__ void __launch_bounds__(kThreads, 2) tri_flash_kernel(const FlashArgs 
       cp_async16(reinterpret_cast<uint8_t *>(sm.k[buf]) + qkv_chunk_offset(row, chunk), ks, valid);
       cp_async16(reinterpret_cast<uint8_t *>(sm.v[buf]) + qkv_chunk_offset(row, chunk), vs, valid);
     }
-    // Bias: 128 query rows x 8 chunks of 8 keys.
     const __nv_bfloat16 *bias_h = args.bias + int64_t(h) * args.bias_hs;
     for (int c = tid; c < kBQ * 8; c += kThreads) {
       int row = c >> 3, chunk = c & 7;
@@ -148,16 +201,17 @@ __global__ void __launch_bounds__(kThreads, 2) tri_flash_kernel(const FlashArgs 
   load_tile(0, 0);
   cp_async_commit();
 
-  // Per-thread state: rows g = lane/4 and g+8 of this warp's 16 queries.
   const int g = lane >> 2, t = lane & 3;
   float o_acc[4][4];
+  float l_acc[4];  // row sums from the ones-fragment mma: [0] row g, [2] row g + 8
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < 4; ++i) {
+    l_acc[i] = 0.f;
 #pragma unroll
     for (int j = 0; j < 4; ++j) o_acc[i][j] = 0.f;
-  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  }
+  uint32_t m_run = kNegInf;  // running max, bf16x2 (row g, row g + 8)
   uint32_t qf[2][4];
-  constexpr float kLog2e = 1.4426950408889634f;
 
   for (int tile = 0; tile < n_tiles; ++tile) {
     const int buf = tile & 1;
@@ -180,69 +234,70 @@ __global__ void __launch_bounds__(kThreads, 2) tri_flash_kernel(const FlashArgs 
       }
     }
 
-    // S = Q K^T for 64 keys: 8 n-tiles of 8 keys.
-    float s[8][4];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-      uint32_t kf[4];
-      int row = j * 8 + (lane & 7);
-      ldmatrix_x4(kf, reinterpret_cast<uint8_t *>(sm.k[buf]) + qkv_chunk_offset(row, lane >> 3));
-      mma_bf16(s[j], qf[0], kf[0], kf[1]);
-      mma_bf16(s[j], qf[1], kf[2], kf[3]);
-    }
-
-    // Ordered rounding: bf16(s) -> +mask -> bf16 -> +bias -> bf16.
+    // S = Q K^T for 64 keys (8 n-tiles of 8 keys), then the ordered rounding
+    // in bf16x2: sp[j][0] = row g keys (2t, 2t+1), sp[j][1] = row g + 8.
     const int k0 = tile * kBK;
     const __nv_bfloat16 *brow0 = sm.bias[buf] + (warp * 16 + g) * kBiasLd;
     const __nv_bfloat16 *brow1 = brow0 + 8 * kBiasLd;
-    float tile_max[2] = {-INFINITY, -INFINITY};
+    uint32_t sp[8][2];
+    uint32_t tmax0 = kNegInf, tmax1 = kNegInf;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
+      float s[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t kf[4];
+      ldmatrix_x4(kf, reinterpret_cast<uint8_t *>(sm.k[buf]) + qkv_chunk_offset(j * 8 + (lane & 7), lane >> 3));
+      mma_bf16(s, qf[0], kf[0], kf[1]);
+      mma_bf16(s, qf[1], kf[2], kf[3]);
       const int kl = j * 8 + 2 * t;
-      const float mb0 = mask_bias[k0 + kl], mb1 = mask_bias[k0 + kl + 1];
+      const uint32_t mb = *reinterpret_cast<const uint32_t *>(mask_bias + k0 + kl);
       const uint32_t b0 = *reinterpret_cast<const uint32_t *>(brow0 + kl);
       const uint32_t b1 = *reinterpret_cast<const uint32_t *>(brow1 + kl);
-      // Keys past n (last tile only) are removed whatever the padding holds.
-      const bool live0 = k0 + kl < n, live1 = k0 + kl + 1 < n;
-      s[j][0] = live0 ? bf16r(bf16r(bf16r(s[j][0]) + mb0) + bf16_lo(b0)) : -INFINITY;
-      s[j][1] = live1 ? bf16r(bf16r(bf16r(s[j][1]) + mb1) + bf16_hi(b0)) : -INFINITY;
-      s[j][2] = live0 ? bf16r(bf16r(bf16r(s[j][2]) + mb0) + bf16_lo(b1)) : -INFINITY;
-      s[j][3] = live1 ? bf16r(bf16r(bf16r(s[j][3]) + mb1) + bf16_hi(b1)) : -INFINITY;
-      tile_max[0] = fmaxf(tile_max[0], fmaxf(s[j][0], s[j][1]));
-      tile_max[1] = fmaxf(tile_max[1], fmaxf(s[j][2], s[j][3]));
+      sp[j][0] = add_bf16x2(add_bf16x2(cvt_bf16x2(s[0], s[1]), mb), b0);
+      sp[j][1] = add_bf16x2(add_bf16x2(cvt_bf16x2(s[2], s[3]), mb), b1);
     }
-    float alpha[2], m_scaled[2];
+    if (k0 + kBK > n) {  // last tile: keys past n contribute nothing
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      tile_max[r] = fmaxf(tile_max[r], __shfl_xor_sync(0xffffffffu, tile_max[r], 1));
-      tile_max[r] = fmaxf(tile_max[r], __shfl_xor_sync(0xffffffffu, tile_max[r], 2));
-      const float m_new = fmaxf(m_run[r], tile_max[r]);
-      alpha[r] = fast_exp2((m_run[r] - m_new) * kLog2e);
-      m_run[r] = m_new;
-      m_scaled[r] = m_new * kLog2e;
-      l_run[r] *= alpha[r];
+      for (int j = 0; j < 8; ++j) {
+        const int key = k0 + j * 8 + 2 * t;
+        const uint32_t keep = (key < n ? 0x0000ffffu : 0u) | (key + 1 < n ? 0xffff0000u : 0u);
+        sp[j][0] = (sp[j][0] & keep) | (kNegPad & ~keep);
+        sp[j][1] = (sp[j][1] & keep) | (kNegPad & ~keep);
+      }
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      o_acc[i][0] *= alpha[0], o_acc[i][1] *= alpha[0];
-      o_acc[i][2] *= alpha[1], o_acc[i][3] *= alpha[1];
+    for (int j = 0; j < 8; ++j) {
+      tmax0 = max_bf16x2(tmax0, sp[j][0]);
+      tmax1 = max_bf16x2(tmax1, sp[j][1]);
     }
-    // P = exp(t - m) in bf16 as the A operand of P V.
+    // Row maxima packed as (row g, row g + 8), reduced over the 4-thread quad.
+    uint32_t rmax = max_bf16x2((tmax0 & 0xffffu) | (tmax1 << 16), (tmax0 >> 16) | (tmax1 & 0xffff0000u));
+    rmax = max_bf16x2(rmax, __shfl_xor_sync(0xffffffffu, rmax, 1));
+    rmax = max_bf16x2(rmax, __shfl_xor_sync(0xffffffffu, rmax, 2));
+    const uint32_t m_new = max_bf16x2(m_run, rmax);
+    if (m_new != m_run) {
+      const float alpha0 = fast_exp2((bf16_lo(m_run) - bf16_lo(m_new)) * 1.4426950408889634f);
+      const float alpha1 = fast_exp2((bf16_hi(m_run) - bf16_hi(m_new)) * 1.4426950408889634f);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        o_acc[i][0] *= alpha0, o_acc[i][1] *= alpha0;
+        o_acc[i][2] *= alpha1, o_acc[i][3] *= alpha1;
+      }
+      l_acc[0] *= alpha0, l_acc[1] *= alpha0, l_acc[2] *= alpha1, l_acc[3] *= alpha1;
+      m_run = m_new;
+    }
+    const uint32_t m0 = splat_lo(m_run), m1 = splat_hi(m_run);
+    // P = exp2((t - m) log2 e) in bf16x2, laid out as the A fragments of P.V.
     uint32_t pf[4][4];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      float p0 = fast_exp2(fmaf(s[j][0], kLog2e, -m_scaled[0]));
-      float p1 = fast_exp2(fmaf(s[j][1], kLog2e, -m_scaled[0]));
-      float p2 = fast_exp2(fmaf(s[j][2], kLog2e, -m_scaled[1]));
-      float p3 = fast_exp2(fmaf(s[j][3], kLog2e, -m_scaled[1]));
-      l_run[0] += p0 + p1;
-      l_run[1] += p2 + p3;
+      uint32_t x0 = sub_bf16x2(sp[j][0], m0), x1 = sub_bf16x2(sp[j][1], m1);
+      x0 = fma_bf16x2(x0, kLog2eLo, mul_bf16x2(x0, kLog2eHi));
+      x1 = fma_bf16x2(x1, kLog2eLo, mul_bf16x2(x1, kLog2eHi));
       const int kk = j >> 1, hi = j & 1;
-      pf[kk][hi * 2 + 0] = pack_bf16x2(p0, p1);
-      pf[kk][hi * 2 + 1] = pack_bf16x2(p2, p3);
+      pf[kk][hi * 2 + 0] = ex2_bf16x2(x0);
+      pf[kk][hi * 2 + 1] = ex2_bf16x2(x1);
     }
-    // O += P V: 4 k-steps of 16 keys x 4 n-tiles of 8 head channels.
+    // O += P V (4 k-steps of 16 keys x 4 n-tiles of 8 channels); l += P 1.
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
       uint32_t a[4] = {pf[kk][0], pf[kk][1], pf[kk][2], pf[kk][3]};
@@ -255,6 +310,7 @@ __global__ void __launch_bounds__(kThreads, 2) tri_flash_kernel(const FlashArgs 
         mma_bf16(o_acc[np * 2 + 0], a, vf[0], vf[1]);
         mma_bf16(o_acc[np * 2 + 1], a, vf[2], vf[3]);
       }
+      mma_bf16(l_acc, a, kOnes, kOnes);
     }
     __syncthreads();
   }
@@ -262,14 +318,9 @@ __global__ void __launch_bounds__(kThreads, 2) tri_flash_kernel(const FlashArgs 
   // Normalise, round, gate, store.
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
-    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 1);
-    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 2);
-  }
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
     const int qi = q0 + warp * 16 + g + r * 8;
     if (qi >= n) continue;
-    const float inv = 1.f / l_run[r];
+    const float inv = 1.f / l_acc[r * 2];
     const int64_t pair = outer * args.so + int64_t(qi) * args.si;
     const __nv_bfloat16 *grow = args.g + pair * args.ld + col0;
     __nv_bfloat16 *orow = args.out + pair * args.out_ld + col0;
@@ -285,7 +336,8 @@ __global__ void __launch_bounds__(kThreads, 2) tri_flash_kernel(const FlashArgs 
 }
 
 // Bias planes from the pair-major projection: natural[h][r][s] = tb[r*n + s][h]
-// (starting node) or transposed[h][s][r] (ending node), rows padded to `ld`.
+// (starting node) or transposed[h][s][r] (ending node), rows padded to `ld`
+// with zeros.
 __global__ void bias_planes_kernel(const __nv_bfloat16 *tb, int64_t tb_ld, int heads, int n, int transpose,
                                    __nv_bfloat16 *out, int64_t ld) {
   __shared__ __nv_bfloat16 tile[32][33];
@@ -300,10 +352,10 @@ __global__ void bias_planes_kernel(const __nv_bfloat16 *tb, int64_t tb_ld, int h
   for (int y = ty; y < 32; y += 8) {
     if (!transpose) {
       int r = r0 + y, s = s0 + tx;
-      if (r < n && s < n) plane[int64_t(r) * ld + s] = tile[y][tx];
+      if (r < n && s < ld) plane[int64_t(r) * ld + s] = tile[y][tx];
     } else {
       int row = s0 + y, col = r0 + tx;  // out[s][r]
-      if (row < n && col < n) plane[int64_t(row) * ld + col] = tile[tx][y];
+      if (row < n && col < ld) plane[int64_t(row) * ld + col] = tile[tx][y];
     }
   }
 }
@@ -318,7 +370,7 @@ extern "C" int bl_triangle_bias_planes(const void *tb, int64_t tb_ld, int64_t he
   BL_REQUIRE(n >= 0 && heads > 0 && heads <= 64, "bl_triangle_bias_planes: bad shape");
   if (n == 0) return BL_OK;
   BL_REQUIRE(tb && out, "bl_triangle_bias_planes: null pointer");
-  BL_REQUIRE(ld >= n && tb_ld >= heads, "bl_triangle_bias_planes: bad leading dimension");
+  BL_REQUIRE(ld >= n && ld <= (n + 31) / 32 * 32 && tb_ld >= heads, "bl_triangle_bias_planes: bad leading dimension");
   dim3 grid((n + 31) / 32, (n + 31) / 32, heads);
   bias_planes_kernel<<<grid, 256, 0, as_stream(stream)>>>(static_cast<const __nv_bfloat16 *>(tb), tb_ld, int(heads),
                                                          int(n), transpose, static_cast<__nv_bfloat16 *>(out), ld);
@@ -356,7 +408,7 @@ extern "C" int bl_triangle_attention(const void *q, const void *k, const void *v
   args.out_ld = out_ld;
   args.n = int(n);
   const int n_tiles = int((n + kBK - 1) / kBK);
-  const size_t smem = sizeof(Smem) + size_t(n_tiles) * kBK * sizeof(float);
+  const size_t smem = sizeof(Smem) + size_t(n_tiles) * kBK * sizeof(__nv_bfloat16);
   BL_REQUIRE(smem <= 227 * 1024, "bl_triangle_attention: too many tokens for the mask buffer");
   BL_CUDA(ensure_smem_limit(reinterpret_cast<const void *>(tri_flash_kernel), int(227 * 1024)));
   dim3 grid(unsigned((n + kBQ - 1) / kBQ), unsigned(n), unsigned(heads));

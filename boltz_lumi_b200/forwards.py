@@ -9,6 +9,11 @@ Numerics follow upstream's eager path under bf16 autocast for the trunk
 (TriangleAttention, TriangleMultiplication, Transition) and plain fp32 for the
 diffusion AdaLN / ConditionedTransitionBlock.  All compute runs in the sm_100a
 kernels of ``libboltz_b200.so``; there is no CPU path.
+
+The trunk forwards return the bf16 update like upstream.  Given
+``residual=z`` (an fp32 pair tensor of the same shape) they instead add the
+update into ``z`` inside the last GEMM's epilogue and return ``z``: this is
+how the Pairformer block applies ``z = z + op(z)`` without a separate pass.
 """
 
 import torch
@@ -45,15 +50,34 @@ def _check_pair_input(x, mask, c=128):
         raise RuntimeError("pair mask must be [B, N, N]")
 
 
+def _check_residual(residual, x):
+    if residual is None:
+        return
+    if residual.dtype != torch.float32 or not residual.is_contiguous() or residual.shape != x.shape:
+        raise RuntimeError("residual must be a contiguous fp32 tensor shaped like the input")
+
+
+def _f32(t):
+    return None if t is None else t.float().contiguous()
+
+
 def _layer_norm_bf16(x2d, norm):
-    return kernels.layer_norm(x2d, norm.weight.float().contiguous() if norm.weight is not None else None,
-                              norm.bias.float().contiguous() if getattr(norm, "bias", None) is not None else None,
-                              norm.eps, out_dtype=_BF16)
+    return kernels.layer_norm(x2d, _f32(norm.weight), _f32(getattr(norm, "bias", None)), norm.eps, out_dtype=_BF16)
 
 
 def _linear_bf16(x2d, weight_bf16, bias=None):
     """Autocast linear on tcgen05: bf16 operands, fp32 accumulation, bf16 result."""
     return kernels.bmm(x2d.unsqueeze(0), weight_bf16.unsqueeze(0), bias=bias).squeeze(0)
+
+
+def _linear_out(a, w, rows, k, stream, bias=None, a2=None, k1=None, gate=False, residual=None, out=None):
+    """bl_linear_fused: residual (fp32 rows += y) or out (bf16 rows = y)."""
+    n = w.shape[0]
+    call("bl_linear_fused", a.data_ptr(), a.stride(0), None if a2 is None else a2.data_ptr(),
+         0 if a2 is None else a2.stride(0), k if k1 is None else k1, w.data_ptr(), w.stride(0), rows, n, k,
+         None if bias is None else bias.data_ptr(), int(gate),
+         None if residual is None else residual.data_ptr(), 0 if residual is None else residual.shape[-1],
+         None if out is None else out.data_ptr(), 0 if out is None else out.shape[-1], stream)
 
 
 # ---------------------------------------------------------------------------
@@ -65,18 +89,11 @@ def _attention_weights(module):
               mha.linear_g.bias, module.linear.weight, mha.linear_o.weight, mha.linear_o.bias)
 
     def build():
-        h = module.linear.weight.shape[0]
-        w = torch.zeros(512 + _pad8(h), mha.linear_q.weight.shape[1], device=mha.linear_q.weight.device,
-                        dtype=torch.float32)
-        w[0:128] = mha.linear_q.weight
-        w[128:256] = mha.linear_k.weight
-        w[256:384] = mha.linear_v.weight
-        w[384:512] = mha.linear_g.weight
-        w[512:512 + h] = module.linear.weight
+        w = torch.cat([mha.linear_q.weight, mha.linear_k.weight, mha.linear_v.weight, mha.linear_g.weight], 0)
         bias = torch.zeros(w.shape[0], device=w.device, dtype=torch.float32)
         bias[384:512] = mha.linear_g.bias
-        return dict(w_in=w.to(_BF16).contiguous(), b_in=bias, w_out=mha.linear_o.weight.to(_BF16).contiguous(),
-                    b_out=mha.linear_o.bias.float().contiguous())
+        return dict(w_in=w.to(_BF16).contiguous(), b_in=bias, w_heads=module.linear.weight.to(_BF16).contiguous(),
+                    w_out=mha.linear_o.weight.to(_BF16).contiguous(), b_out=mha.linear_o.bias.float().contiguous())
 
     return _cached(module, "_bl_attention_weights", params, build)
 
@@ -87,13 +104,14 @@ def _attention_supported(module):
             and mha.linear_q.weight.shape == (128, 128) and mha.linear_q.bias is None)
 
 
-def triangle_attention_forward(self, x, mask=None, chunk_size=None, use_kernels=False):
+def triangle_attention_forward(self, x, mask=None, chunk_size=None, use_kernels=False, residual=None):
     """Upstream ``TriangleAttention.forward(x, mask, chunk_size, use_kernels)``.
 
-    Returns the bf16 update (the caller adds it to z).  Row chunking is
-    irrelevant here: the flash kernel never materialises the scores.
+    Returns the bf16 update (or, with ``residual``, adds it into that fp32 z).
+    Row chunking is irrelevant here: the flash kernel never materialises the scores.
     """
     _check_pair_input(x, mask)
+    _check_residual(residual, x)
     if not _attention_supported(self):
         raise RuntimeError("triangle attention kernels cover c_z = 128, 4 heads x 32 only")
     starting = getattr(self, "starting", True)
@@ -104,23 +122,34 @@ def triangle_attention_forward(self, x, mask=None, chunk_size=None, use_kernels=
     w = _attention_weights(self)
     width = w["w_in"].shape[0]
     n_pad = _pad8(n)
-    out = torch.empty(batch, n, n, 128, device=x.device, dtype=_BF16)
+    out = None if residual is not None else torch.empty(batch, n, n, 128, device=x.device, dtype=_BF16)
     stream = stream_of(x)
+    ln = self.layer_norm
+    rows = n * n
     for b in range(batch):
-        xn = _layer_norm_bf16(x[b].reshape(n * n, 128), self.layer_norm)
-        proj = _linear_bf16(xn, w["w_in"], w["b_in"])  # [n*n, 520]: q | k | v | g | tri-bias
+        xb = x[b].reshape(rows, 128).float().contiguous()
+        xn = torch.empty(rows, 128, device=x.device, dtype=_BF16)
         bias = torch.empty(4, n, n_pad, device=x.device, dtype=_BF16)
-        call("bl_triangle_bias_planes", proj.data_ptr() + 512 * 2, width, 4, n, int(not starting),
-             bias.data_ptr(), n_pad, stream)
-        gated = torch.empty(n * n, 128, device=x.device, dtype=_BF16)
+        # LayerNorm fused with the 128 -> 4 triangle-bias projection, written as
+        # [h][query][key] planes (transposed for the ending node).
+        call("bl_layernorm_heads", xb.data_ptr(), n, _f32(ln.weight).data_ptr(), _f32(ln.bias).data_ptr(),
+             float(ln.eps), w["w_heads"].data_ptr(), 4, int(not starting), xn.data_ptr(), bias.data_ptr(), n_pad,
+             stream)
+        proj = _linear_bf16(xn, w["w_in"], w["b_in"])  # [n*n, 512]: q | k | v | g (+ g bias)
+        del xn
+        gated = torch.empty(rows, 128, device=x.device, dtype=_BF16)
         so, si = (n, 1) if starting else (1, n)
         ms_o, ms_k = (n, 1) if starting else (1, n)
         base = proj.data_ptr()
         call("bl_triangle_attention", base, base + 128 * 2, base + 256 * 2, base + 384 * 2, width, so, si,
              bias.data_ptr(), n_pad, n * n_pad, mask[b].data_ptr(), ms_o, ms_k, float(getattr(self, "inf", 1e9)),
              4, 32, n, gated.data_ptr(), 128, stream)
-        out[b] = _linear_bf16(gated, w["w_out"], w["b_out"]).view(n, n, 128)
-    return out
+        del proj, bias
+        if residual is not None:
+            _linear_out(gated, w["w_out"], rows, 128, stream, bias=w["b_out"], residual=residual[b].view(rows, 128))
+        else:
+            _linear_out(gated, w["w_out"], rows, 128, stream, bias=w["b_out"], out=out[b].view(rows, 128))
+    return residual if residual is not None else out
 
 
 # ---------------------------------------------------------------------------
@@ -130,9 +159,12 @@ def _multiplication_weights(module):
     params = (module.p_in.weight, module.g_in.weight, module.p_out.weight, module.g_out.weight)
 
     def build():
-        return dict(w_in=torch.cat([module.p_in.weight, module.g_in.weight], 0).to(_BF16).contiguous(),
-                    w_pout=module.p_out.weight.to(_BF16).contiguous(),
-                    w_gout=module.g_out.weight.to(_BF16).contiguous())
+        w_in = torch.cat([module.p_in.weight, module.g_in.weight], 0)
+        # Block-diagonal [p_out 0; 0 g_out] over the K-concatenation [LN_out(o) | LN_in(x)].
+        w_out = torch.zeros(256, 256, device=w_in.device, dtype=torch.float32)
+        w_out[:128, :128] = module.p_out.weight
+        w_out[128:, 128:] = module.g_out.weight
+        return dict(w_in=w_in.to(_BF16).contiguous(), w_out=w_out.to(_BF16).contiguous())
 
     return _cached(module, "_bl_multiplication_weights", params, build)
 
@@ -143,10 +175,12 @@ def _is_outgoing(module):
     return type(module).__name__ == "TriangleMultiplicationOutgoing"
 
 
-def triangle_multiplication_forward(self, x, mask, use_kernels=False):
+def triangle_multiplication_forward(self, x, mask, use_kernels=False, residual=None):
     """Upstream ``TriangleMultiplication{Outgoing,Incoming}.forward(x, mask, use_kernels)``
-    (the reference's ``normalized_forward``, multiplication.py:48-137).  Returns bf16."""
+    (the reference's ``normalized_forward``, multiplication.py:48-137).  Returns bf16
+    (or, with ``residual``, adds into that fp32 z)."""
     _check_pair_input(x, mask)
+    _check_residual(residual, x)
     if self.p_in.weight.shape != (256, 128) or self.p_in.bias is not None:
         raise RuntimeError("triangle multiplication kernels cover dim = 128 without projection biases")
     outgoing = _is_outgoing(self)
@@ -154,10 +188,11 @@ def triangle_multiplication_forward(self, x, mask, use_kernels=False):
     mask = mask.float().contiguous()
     w = _multiplication_weights(self)
     n_pad = _pad8(n)
-    out = torch.empty(batch, n, n, 128, device=x.device, dtype=_BF16)
+    rows = n * n
+    out = None if residual is not None else torch.empty(batch, n, n, 128, device=x.device, dtype=_BF16)
     stream = stream_of(x)
     for b in range(batch):
-        xn = _layer_norm_bf16(x[b].reshape(n * n, 128), self.norm_in)
+        xn = _layer_norm_bf16(x[b].reshape(rows, 128), self.norm_in)
         pg = _linear_bf16(xn, w["w_in"])  # [n*n, 512]: p | g
         a = torch.empty(128, n, n_pad, device=x.device, dtype=_BF16)
         bp = torch.empty_like(a)
@@ -172,15 +207,17 @@ def triangle_multiplication_forward(self, x, mask, use_kernels=False):
         call("bl_batched_gemm", a.data_ptr(), mn, n_pad, plane, bp.data_ptr(), mn, n_pad, plane, prod.data_ptr(),
              n_pad, plane, 128, n, n, n, None, stream)
         del a, bp
-        normed = torch.empty(n * n, 128, device=x.device, dtype=_BF16)
-        call("bl_layernorm_planes", prod.data_ptr(), n, n_pad, self.norm_out.weight.float().contiguous().data_ptr(),
-             self.norm_out.bias.float().contiguous().data_ptr(), float(self.norm_out.eps), normed.data_ptr(),
-             _lib.BL_BF16, stream)
+        normed = torch.empty(rows, 128, device=x.device, dtype=_BF16)
+        call("bl_layernorm_planes", prod.data_ptr(), n, n_pad, _f32(self.norm_out.weight).data_ptr(),
+             _f32(self.norm_out.bias).data_ptr(), float(self.norm_out.eps), normed.data_ptr(), _lib.BL_BF16, stream)
         del prod
-        p = _linear_bf16(normed, w["w_pout"])
-        g = _linear_bf16(xn, w["w_gout"])
-        out[b] = kernels.gate(p, g).view(n, n, 128)
-    return out
+        # y = bf16(p_out(normed)) * bf16(sigmoid(g_out(xn))) in one GEMM (K = 256).
+        if residual is not None:
+            _linear_out(normed, w["w_out"], rows, 256, stream, a2=xn, k1=128, gate=True,
+                        residual=residual[b].view(rows, 128))
+        else:
+            _linear_out(normed, w["w_out"], rows, 256, stream, a2=xn, k1=128, gate=True, out=out[b].view(rows, 128))
+    return residual if residual is not None else out
 
 
 # ---------------------------------------------------------------------------
@@ -196,22 +233,36 @@ def _transition_weights(module):
     return _cached(module, "_bl_transition_weights", params, build)
 
 
-def transition_forward(self, x, chunk_size=None):
+def transition_forward(self, x, chunk_size=None, residual=None):
     """Upstream ``Transition.forward(x, chunk_size)`` under bf16 autocast
-    (the reference's pair_transition.py:8-28).  Returns bf16."""
+    (the reference's pair_transition.py:8-28).  Returns bf16 (or adds into ``residual``)."""
     if not x.is_cuda:
         raise RuntimeError("transition kernels need CUDA tensors")
+    _check_residual(residual, x)
     dim, hidden = x.shape[-1], self.fc1.weight.shape[0]
-    if dim % 8 or hidden % 8 or any(f.bias is not None for f in (self.fc1, self.fc2, self.fc3)):
-        raise RuntimeError("transition kernels need bias-free layers with widths that are multiples of 8")
+    out_dim = self.fc3.weight.shape[0]
+    if dim % 8 or hidden % 64 or any(f.bias is not None for f in (self.fc1, self.fc2, self.fc3)):
+        raise RuntimeError("transition kernels need bias-free layers, dim % 8 == 0 and hidden % 64 == 0")
     w = _transition_weights(self)
     rows = x.numel() // dim
+    stream = stream_of(x)
     xn = _layer_norm_bf16(x.reshape(rows, dim).contiguous(), self.norm)
     h12 = _linear_bf16(xn, w["w12"])
+    del xn
     h = torch.empty(rows, hidden, device=x.device, dtype=_BF16)
-    call("bl_swiglu_rows", h12.data_ptr(), 2 * hidden, rows, hidden, h.data_ptr(), hidden, stream_of(x))
+    call("bl_swiglu_rows", h12.data_ptr(), 2 * hidden, rows, hidden, h.data_ptr(), hidden, stream)
     del h12
-    return _linear_bf16(h, w["w3"]).view(*x.shape[:-1], w["w3"].shape[0])
+    if out_dim == 128:
+        if residual is not None:
+            _linear_out(h, w["w3"], rows, hidden, stream, residual=residual.view(rows, out_dim))
+            return residual
+        out = torch.empty(rows, out_dim, device=x.device, dtype=_BF16)
+        _linear_out(h, w["w3"], rows, hidden, stream, out=out)
+        return out.view(*x.shape[:-1], out_dim)
+    y = _linear_bf16(h, w["w3"]).view(*x.shape[:-1], out_dim)
+    if residual is not None:
+        return residual.add_(y)
+    return y
 
 
 # ---------------------------------------------------------------------------
@@ -248,8 +299,8 @@ def normalization_forward(self, x):
     """Upstream triangle ``LayerNorm.forward(x)`` (triangle.py:107-146): fp32
     statistics, bf16 output for the autocast linears that consume it."""
     c = x.shape[-1]
-    return kernels.layer_norm(x.reshape(-1, c), self.weight.float().contiguous(), self.bias.float().contiguous(),
-                              self.eps, out_dtype=_BF16).view(x.shape)
+    return kernels.layer_norm(x.reshape(-1, c), _f32(self.weight), _f32(self.bias), self.eps,
+                              out_dtype=_BF16).view(x.shape)
 
 
 __all__ = [

@@ -192,12 +192,16 @@ class PairformerLayer(nn.Module):
         self.transition_z = Transition(token_z, token_z * 4)
 
     def forward(self, s, z, mask, pair_mask):
+        """Returns (s, z); z (contiguous fp32) is updated in place: each pair op adds
+        its bf16 update inside its last GEMM's epilogue (z = z + op(z) upstream)."""
         _inference_only(self)
-        z = z.add_(self.tri_mul_out(z, pair_mask))
-        z = z.add_(self.tri_mul_in(z, pair_mask))
-        z = z.add_(self.tri_att_start(z, pair_mask))
-        z = z.add_(self.tri_att_end(z, pair_mask))
-        z = z.add_(self.transition_z(z))
+        if z.dtype != torch.float32 or not z.is_contiguous():
+            z = z.float().contiguous()
+        forwards.triangle_multiplication_forward(self.tri_mul_out, z, pair_mask, residual=z)
+        forwards.triangle_multiplication_forward(self.tri_mul_in, z, pair_mask, residual=z)
+        forwards.triangle_attention_forward(self.tri_att_start, z, pair_mask, residual=z)
+        forwards.triangle_attention_forward(self.tri_att_end, z, pair_mask, residual=z)
+        forwards.transition_forward(self.transition_z, z, residual=z)
         s_normed = kernels.layer_norm(s.contiguous(), self.pre_norm_s.weight, self.pre_norm_s.bias,
                                       self.pre_norm_s.eps, out_dtype=torch.float32)
         s = s + self.attention(s_normed, z, mask, s_normed)

@@ -150,12 +150,43 @@ BL_API int bl_batched_gemm(const void *a, int a_mn_major, int64_t a_ld, int64_t 
                            int64_t k, const float *bias, void *stream);
 
 /*
+ * Linear layer over pair rows on tcgen05 with a fused epilogue; one N tile
+ * per row block.  acc = [A | A2] . W^T, where A [m, k1] (row stride a_ld) and
+ * the optional A2 [m, k - k1] (row stride a2_ld) are concatenated along K
+ * (k1 a multiple of 64), W bf16 [n, k] (row stride w_ld).
+ *   gate = 0, n = 128: y = bf16(acc + bias)                          (bias may be NULL)
+ *   gate = 1, n = 256: y[:, c] = bf16(bf16(acc[c]) * bf16(sigmoid(bf16(acc[128 + c]))))
+ * Exactly one of z / out: z (fp32 rows of z_ld) receives z += y, the residual
+ * update of the Pairformer block; out (bf16 rows of out_ld) receives y.
+ * Replaces the output linears of the reference path and the gate that follows
+ * them: linear_o of upstream _wrap_up (triangle.py:104), p_out / g_out and the
+ * K-gate `gate` (multiplication.py:135-137), fc3 (pair_transition.py:165).
+ */
+BL_API int bl_linear_fused(const void *a, int64_t a_ld, const void *a2, int64_t a2_ld, int64_t k1,
+                           const void *w, int64_t w_ld, int64_t m, int64_t n, int64_t k,
+                           const float *bias, int gate, float *z, int64_t z_ld, void *out,
+                           int64_t out_ld, void *stream);
+
+/*
  * LayerNorm over 128 channel planes (bf16 [128][n][ld], the per-channel
  * matmul output of the triangle multiplication) into pair rows [n*n, 128].
  * Replaces the channel-first norm call of multiplication.py:124-133.
  */
 BL_API int bl_layernorm_planes(const void *planes, int64_t n, int64_t ld, const float *weight,
                                const float *bias, float eps, void *out, int out_dtype, void *stream);
+
+/*
+ * LayerNorm of fp32 pair rows x [n*n, 128] to bf16 rows `out`, fused with the
+ * bias-free triangle-bias projection (bf16 weights w_heads [heads][128]):
+ *   bias[h][r][s] = bf16(bf16(ln(x[r*n+s])) . w_heads[h])   (transpose = 0)
+ *   bias[h][s][r] = same                                    (transpose = 1, ending node)
+ * with bias planes of row stride ld.  Replaces the layer_norm fast path
+ * (triangle.py:107-146) plus upstream's `linear` + permute_final_dims that
+ * build tri_bias for triangle.py:32.  heads must be 4.
+ */
+BL_API int bl_layernorm_heads(const float *x, int64_t n, const float *weight, const float *bias, float eps,
+                              const void *w_heads, int64_t heads, int transpose, void *out,
+                              void *bias_planes, int64_t ld, void *stream);
 
 /*
  * Gate + mask the joint p|g projection (bf16 rows of pg_ld >= 512 elements:

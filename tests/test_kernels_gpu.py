@@ -219,3 +219,41 @@ def test_batched_gemm(batch, m, n, k, a_mn, b_mn):
     actual = kernels.bmm(av, bv, bias=None if bias is None else bias.cuda())
     # fp32 accumulation-order differences can flip one bf16 rounding.
     assert_close(actual.float(), expected, atol=1e-3 * k ** 0.5, rtol=2 * BF16_ULP)
+
+
+# ---------------------------------------------------------------------------
+# tcgen05 linear with fused epilogues (residual add into fp32 z, gate pair)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("m", [1, 127, 1000, 4096 + 64])
+@pytest.mark.parametrize("gate", [False, True])
+@pytest.mark.parametrize("residual", [False, True])
+def test_linear_fused(m, gate, residual):
+    from boltz_lumi_b200._lib import call
+
+    g = gen(88)
+    k1, k = (128, 256) if gate else (512, 512)
+    n = 256 if gate else 128
+    a = torch.randn(m, k1, generator=g).bfloat16()
+    a2 = torch.randn(m, k - k1, generator=g).bfloat16() if gate else None
+    w = (torch.randn(n, k, generator=g) / k ** 0.5).bfloat16()
+    bias = None if gate else torch.randn(n, generator=g)
+    full = a.float() if a2 is None else torch.cat([a.float(), a2.float()], 1)
+    acc = full @ w.float().t()
+    if gate:
+        y = numerics.bf16_round(numerics.bf16_round(acc[:, :128]) * numerics.sigmoid_bf16(acc[:, 128:]))
+    else:
+        y = numerics.bf16_round(acc + bias)
+    z0 = torch.randn(m, 128, generator=g)
+    ac, wc = a.cuda(), w.cuda()
+    a2c = a2.cuda() if a2 is not None else None
+    bc = bias.cuda() if bias is not None else None
+    zc = z0.cuda() if residual else None
+    out = None if residual else torch.empty(m, 128, device="cuda", dtype=torch.bfloat16)
+    call("bl_linear_fused", ac.data_ptr(), k1, None if a2c is None else a2c.data_ptr(), k - k1, k1, wc.data_ptr(), k,
+         m, n, k, None if bc is None else bc.data_ptr(), int(gate), None if zc is None else zc.data_ptr(), 128,
+         None if out is None else out.data_ptr(), 128, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    if residual:
+        assert_close(zc.cpu() - z0, y, atol=1e-5, rtol=2 * BF16_ULP)
+    else:
+        assert_close(out.float(), y, atol=1e-5, rtol=2 * BF16_ULP)
