@@ -436,7 +436,7 @@ int linear_fused(const void *a, int64_t a_ld, const void *a2, int64_t a2_ld, int
   BL_REQUIRE(k1 > 0 && k1 <= k && k1 % kBK == 0 || k1 == k, "linear: the A split must fall on a 64-column boundary");
   BL_REQUIRE(gate ? n == 256 : n == 128, "linear: n must be 128 (or 256 = p|g with gate)");
   BL_REQUIRE(!(gate && bias), "linear: the gate form takes no bias");
-  BL_REQUIRE(aligned_to(a, 16) && aligned_to(w, 16) && a_ld % 8 == 0 && w_ld % 8 == 0 && a_ld >= k && w_ld >= k,
+  BL_REQUIRE(aligned_to(a, 16) && aligned_to(w, 16) && a_ld % 8 == 0 && w_ld % 8 == 0 && w_ld >= k,
              "linear: operands must have 16-byte aligned rows");
   BL_REQUIRE(m < (1ll << 31) && k < (1ll << 31), "linear: shape too large");
   const int width = gate ? int(n / 2) : int(n);
