@@ -13,14 +13,15 @@
 // (pair row of (outer, inner) = outer * so + inner * si) and a transposed bias
 // plane, so no transposed copy of z or of q/k/v is made.
 //
-// Cost model: head dim 32 makes the core exp/ALU-bound (N^3 H exponentials vs
-// 4 N^3 H d flops), so the two small contractions stay on mma.sync m16n8k16 and
-// the score pipeline runs on packed bf16x2 arithmetic -- the rounding points
-// upstream imposes are bf16 anyway:
-//   cvt.rn.bf16x2 (s) -> add (mask) -> add (bias) -> max -> sub (max)
-//   -> mul/fma by log2(e) (two-term constant, unbiased) -> ex2.bf16x2 = P
-// P feeds the P.V mma directly, and the row sums come from one extra mma
-// against a ones fragment, so no per-element fp32 adds remain.
+// Cost model: head dim 32 makes the core exp/issue-bound (N^3 H exponentials
+// at 16 MUFU ops/clk/SM vs 4 N^3 H d flops), so the two small contractions
+// stay on mma.sync m16n8k16 and the per-score work is kept minimal:
+//   cvt.rn.bf16x2 (s) -> add.bf16x2 (mask; skipped on key tiles without
+//   masked keys) -> add.bf16x2 (bias, loaded with ldmatrix in fragment
+//   layout) -> max.bf16x2 -> one fp32 FFMA + MUFU.EX2 per score -> cvt = P
+// (measured on B200: packed ex2.bf16x2 costs two MUFU ops, so the exponent
+// runs in fp32, which also keeps t*log2(e) exact).  P feeds the P.V mma
+// directly and the row sums come from one extra mma against a ones fragment.
 #include "common.cuh"
 
 namespace bl {
@@ -32,6 +33,8 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kBQ = kWarps * 16;  // 128 queries per CTA
 constexpr int kBK = 64;           // keys per tile
 constexpr int kBiasLd = kBK + 8;  // padded smem row (144 B): conflict-free fragment reads
+constexpr int kHeadsPerRow = 4;   // heads (grid.x = heads * query tiles)
+constexpr int kMaxTiles = 64;     // key tiles per row: n <= 4096
 
 struct FlashArgs {
   const __nv_bfloat16 *q, *k, *v, *g;
@@ -143,6 +146,7 @@ struct Smem {
   alignas(128) __nv_bfloat16 k[2][kBK * kD];
   alignas(128) __nv_bfloat16 v[2][kBK * kD];
   alignas(128) __nv_bfloat16 bias[2][kBQ * kBiasLd];
+  int tile_masked[kMaxTiles];
   // followed by the per-key mask bias of this outer row (bf16, dynamic)
 };
 
@@ -153,48 +157,55 @@ __global__ void __launch_bounds__(kThreads, 2) tri_flash_kernel(const FlashArgs 
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n = args.n;
-  const int q0 = blockIdx.x * kBQ;
+  // Heads of one query tile are adjacent in the grid: they read the same pair rows.
+  const int h = blockIdx.x % kHeadsPerRow;
+  const int q0 = (blockIdx.x / kHeadsPerRow) * kBQ;
   const int64_t outer = blockIdx.y;
-  const int h = blockIdx.z;
   const int col0 = h * kD;
-
-  // Per-key additive mask of this outer row.  inf * (mask - 1) is added to the
-  // bf16 score; for mask in {0, 1} adding its bf16 value rounds identically.
-  // Padding keys are removed separately (last tile).
   const int n_tiles = (n + kBK - 1) / kBK;
-  for (int key = tid; key < n_tiles * kBK; key += kThreads)
-    mask_bias[key] = __float2bfloat16_rn(
-        key < n ? args.inf * (args.mask[outer * args.ms_o + int64_t(key) * args.ms_k] - 1.f) : 0.f);
 
-  auto row_ptr = [&](const __nv_bfloat16 *base, int inner) {
-    return base + (outer * args.so + int64_t(inner) * args.si) * args.ld + col0;
-  };
+  // Per-key additive mask of this outer row (bf16; for mask in {0, 1} adding it
+  // rounds exactly like adding the fp32 value) and a flag per key tile that
+  // says whether any key of the tile is masked at all.
+  if (tid < kMaxTiles) sm.tile_masked[tid] = 0;
+  __syncthreads();
+  for (int key = tid; key < n_tiles * kBK; key += kThreads) {
+    float mb = key < n ? args.inf * (args.mask[outer * args.ms_o + int64_t(key) * args.ms_k] - 1.f) : 0.f;
+    mask_bias[key] = __float2bfloat16_rn(mb);
+    if (mb != 0.f) atomicOr(&sm.tile_masked[key / kBK], 1);
+  }
+
+  // Per-thread load addresses: K/V row (tid / 4, 16-byte chunk tid % 4) and
+  // four bias chunks (rows tid / 8 + 32 i, chunk tid % 8), advanced per tile.
+  const int kv_row = tid >> 2, kv_chunk = tid & 3;
+  const int64_t kv_base = (outer * args.so + int64_t(kv_row) * args.si) * args.ld + col0 + kv_chunk * 8;
+  const int64_t kv_step = int64_t(kBK) * args.si * args.ld;
+  const int b_row = tid >> 3, b_chunk = tid & 7;
+  const __nv_bfloat16 *bias_base = args.bias + int64_t(h) * args.bias_hs + int64_t(q0 + b_row) * args.bias_ld + b_chunk * 8;
+  const int64_t bias_rows32 = 32 * args.bias_ld;
 
   for (int c = tid; c < kBQ * 4; c += kThreads) {
     int row = c >> 2, chunk = c & 3;
     int qi = q0 + row;
     bool valid = qi < n;
-    const __nv_bfloat16 *src = valid ? row_ptr(args.q, qi) + chunk * 8 : args.q;
+    const __nv_bfloat16 *src =
+        valid ? args.q + (outer * args.so + int64_t(qi) * args.si) * args.ld + col0 + chunk * 8 : args.q;
     cp_async16(reinterpret_cast<uint8_t *>(sm.q) + qkv_chunk_offset(row, chunk), src, valid);
   }
   auto load_tile = [&](int tile, int buf) {
     const int k0 = tile * kBK;
-    {
-      int row = tid >> 2, chunk = tid & 3;
-      int key = k0 + row;
-      bool valid = key < n;
-      const __nv_bfloat16 *ks = valid ? row_ptr(args.k, key) + chunk * 8 : args.k;
-      const __nv_bfloat16 *vs = valid ? row_ptr(args.v, key) + chunk * 8 : args.v;
-      cp_async16(reinterpret_cast<uint8_t *>(sm.k[buf]) + qkv_chunk_offset(row, chunk), ks, valid);
-      cp_async16(reinterpret_cast<uint8_t *>(sm.v[buf]) + qkv_chunk_offset(row, chunk), vs, valid);
-    }
-    const __nv_bfloat16 *bias_h = args.bias + int64_t(h) * args.bias_hs;
-    for (int c = tid; c < kBQ * 8; c += kThreads) {
-      int row = c >> 3, chunk = c & 7;
-      int qi = q0 + row, key = k0 + chunk * 8;
-      bool valid = qi < n && key < args.bias_ld;
-      const __nv_bfloat16 *src = valid ? bias_h + int64_t(qi) * args.bias_ld + key : args.bias;
-      cp_async16(sm.bias[buf] + row * kBiasLd + chunk * 8, src, valid);
+    const bool kv_valid = k0 + kv_row < n;
+    const int64_t off = kv_base + tile * kv_step;
+    cp_async16(reinterpret_cast<uint8_t *>(sm.k[buf]) + qkv_chunk_offset(kv_row, kv_chunk),
+               kv_valid ? args.k + off : args.k, kv_valid);
+    cp_async16(reinterpret_cast<uint8_t *>(sm.v[buf]) + qkv_chunk_offset(kv_row, kv_chunk),
+               kv_valid ? args.v + off : args.v, kv_valid);
+    const bool col_valid = k0 + b_chunk * 8 < args.bias_ld;
+#pragma unroll
+    for (int i = 0; i < kBQ / 32; ++i) {
+      const bool valid = col_valid && q0 + b_row + 32 * i < n;
+      cp_async16(sm.bias[buf] + (b_row + 32 * i) * kBiasLd + b_chunk * 8,
+                 valid ? bias_base + i * bias_rows32 + k0 : args.bias, valid);
     }
   };
 
@@ -210,8 +221,9 @@ __global__ void __launch_bounds__(kThreads, 2) tri_flash_kernel(const FlashArgs 
 #pragma unroll
     for (int j = 0; j < 4; ++j) o_acc[i][j] = 0.f;
   }
-  uint32_t m_run = kNegInf;  // running max, bf16x2 (row g, row g + 8)
+  float m_run0 = -INFINITY, m_run1 = -INFINITY;  // running maxima of rows g, g + 8
   uint32_t qf[2][4];
+  constexpr float kLog2e = 1.4426950408889634f;
 
   for (int tile = 0; tile < n_tiles; ++tile) {
     const int buf = tile & 1;
@@ -234,26 +246,35 @@ __global__ void __launch_bounds__(kThreads, 2) tri_flash_kernel(const FlashArgs 
       }
     }
 
-    // S = Q K^T for 64 keys (8 n-tiles of 8 keys), then the ordered rounding
-    // in bf16x2: sp[j][0] = row g keys (2t, 2t+1), sp[j][1] = row g + 8.
+    // S = Q K^T for 64 keys (8 n-tiles of 8 keys) and the ordered rounding in
+    // bf16x2: sp[j][0] = row g keys (2t, 2t+1), sp[j][1] = row g + 8.
     const int k0 = tile * kBK;
-    const __nv_bfloat16 *brow0 = sm.bias[buf] + (warp * 16 + g) * kBiasLd;
-    const __nv_bfloat16 *brow1 = brow0 + 8 * kBiasLd;
+    const bool masked = sm.tile_masked[tile] != 0;
     uint32_t sp[8][2];
     uint32_t tmax0 = kNegInf, tmax1 = kNegInf;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float s[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t kf[4];
-      ldmatrix_x4(kf, reinterpret_cast<uint8_t *>(sm.k[buf]) + qkv_chunk_offset(j * 8 + (lane & 7), lane >> 3));
-      mma_bf16(s, qf[0], kf[0], kf[1]);
-      mma_bf16(s, qf[1], kf[2], kf[3]);
-      const int kl = j * 8 + 2 * t;
-      const uint32_t mb = *reinterpret_cast<const uint32_t *>(mask_bias + k0 + kl);
-      const uint32_t b0 = *reinterpret_cast<const uint32_t *>(brow0 + kl);
-      const uint32_t b1 = *reinterpret_cast<const uint32_t *>(brow1 + kl);
-      sp[j][0] = add_bf16x2(add_bf16x2(cvt_bf16x2(s[0], s[1]), mb), b0);
-      sp[j][1] = add_bf16x2(add_bf16x2(cvt_bf16x2(s[2], s[3]), mb), b1);
+    for (int jp = 0; jp < 4; ++jp) {
+      // Bias fragments of n-tiles 2jp, 2jp+1: [0] row g, [1] row g+8, [2]/[3] next n-tile.
+      uint32_t bf[4];
+      ldmatrix_x4(bf, sm.bias[buf] + (warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * kBiasLd +
+                          (jp * 2 + (lane >> 4)) * 8);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int j = jp * 2 + half;
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t kf[4];
+        ldmatrix_x4(kf, reinterpret_cast<uint8_t *>(sm.k[buf]) + qkv_chunk_offset(j * 8 + (lane & 7), lane >> 3));
+        mma_bf16(s, qf[0], kf[0], kf[1]);
+        mma_bf16(s, qf[1], kf[2], kf[3]);
+        uint32_t p0 = cvt_bf16x2(s[0], s[1]), p1 = cvt_bf16x2(s[2], s[3]);
+        if (masked) {
+          const uint32_t mb = *reinterpret_cast<const uint32_t *>(mask_bias + k0 + j * 8 + 2 * t);
+          p0 = add_bf16x2(p0, mb);
+          p1 = add_bf16x2(p1, mb);
+        }
+        sp[j][0] = add_bf16x2(p0, bf[half * 2 + 0]);
+        sp[j][1] = add_bf16x2(p1, bf[half * 2 + 1]);
+      }
     }
     if (k0 + kBK > n) {  // last tile: keys past n contribute nothing
 #pragma unroll
@@ -273,29 +294,31 @@ __global__ void __launch_bounds__(kThreads, 2) tri_flash_kernel(const FlashArgs 
     uint32_t rmax = max_bf16x2((tmax0 & 0xffffu) | (tmax1 << 16), (tmax0 >> 16) | (tmax1 & 0xffff0000u));
     rmax = max_bf16x2(rmax, __shfl_xor_sync(0xffffffffu, rmax, 1));
     rmax = max_bf16x2(rmax, __shfl_xor_sync(0xffffffffu, rmax, 2));
-    const uint32_t m_new = max_bf16x2(m_run, rmax);
-    if (m_new != m_run) {
-      const float alpha0 = fast_exp2((bf16_lo(m_run) - bf16_lo(m_new)) * 1.4426950408889634f);
-      const float alpha1 = fast_exp2((bf16_hi(m_run) - bf16_hi(m_new)) * 1.4426950408889634f);
+    const float m_new0 = fmaxf(m_run0, bf16_lo(rmax)), m_new1 = fmaxf(m_run1, bf16_hi(rmax));
+    if (m_new0 != m_run0 || m_new1 != m_run1) {
+      const float alpha0 = fast_exp2((m_run0 - m_new0) * kLog2e);
+      const float alpha1 = fast_exp2((m_run1 - m_new1) * kLog2e);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         o_acc[i][0] *= alpha0, o_acc[i][1] *= alpha0;
         o_acc[i][2] *= alpha1, o_acc[i][3] *= alpha1;
       }
       l_acc[0] *= alpha0, l_acc[1] *= alpha0, l_acc[2] *= alpha1, l_acc[3] *= alpha1;
-      m_run = m_new;
+      m_run0 = m_new0, m_run1 = m_new1;
     }
-    const uint32_t m0 = splat_lo(m_run), m1 = splat_hi(m_run);
-    // P = exp2((t - m) log2 e) in bf16x2, laid out as the A fragments of P.V.
+    // P = exp2(t log2 e - m log2 e) in fp32 (the bf16 scores convert exactly),
+    // rounded to bf16x2 as the A fragments of P.V.
+    const float ml0 = m_run0 * kLog2e, ml1 = m_run1 * kLog2e;
     uint32_t pf[4][4];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      uint32_t x0 = sub_bf16x2(sp[j][0], m0), x1 = sub_bf16x2(sp[j][1], m1);
-      x0 = fma_bf16x2(x0, kLog2eLo, mul_bf16x2(x0, kLog2eHi));
-      x1 = fma_bf16x2(x1, kLog2eLo, mul_bf16x2(x1, kLog2eHi));
+      const float e0 = fast_exp2(fmaf(bf16_lo(sp[j][0]), kLog2e, -ml0));
+      const float e1 = fast_exp2(fmaf(bf16_hi(sp[j][0]), kLog2e, -ml0));
+      const float e2 = fast_exp2(fmaf(bf16_lo(sp[j][1]), kLog2e, -ml1));
+      const float e3 = fast_exp2(fmaf(bf16_hi(sp[j][1]), kLog2e, -ml1));
       const int kk = j >> 1, hi = j & 1;
-      pf[kk][hi * 2 + 0] = ex2_bf16x2(x0);
-      pf[kk][hi * 2 + 1] = ex2_bf16x2(x1);
+      pf[kk][hi * 2 + 0] = cvt_bf16x2(e0, e1);
+      pf[kk][hi * 2 + 1] = cvt_bf16x2(e2, e3);
     }
     // O += P V (4 k-steps of 16 keys x 4 n-tiles of 8 channels); l += P 1.
 #pragma unroll
@@ -383,9 +406,10 @@ extern "C" int bl_triangle_attention(const void *q, const void *k, const void *v
                                      const float *mask, int64_t ms_o, int64_t ms_k, float inf, int64_t heads,
                                      int64_t head_dim, int64_t n, void *out, int64_t out_ld, void *stream) {
   BL_REQUIRE(head_dim == kD, "bl_triangle_attention: head_dim must be 32");
-  BL_REQUIRE(n >= 0 && heads > 0 && heads <= 65535, "bl_triangle_attention: bad shape");
+  BL_REQUIRE(heads == kHeadsPerRow, "bl_triangle_attention: 4 heads supported");
+  BL_REQUIRE(n >= 0, "bl_triangle_attention: bad shape");
   if (n == 0) return BL_OK;
-  BL_REQUIRE(n <= 65535, "bl_triangle_attention: at most 65535 tokens");
+  BL_REQUIRE(n <= kMaxTiles * kBK, "bl_triangle_attention: at most 4096 tokens");
   BL_REQUIRE(q && k && v && g && bias && mask && out, "bl_triangle_attention: null pointer");
   BL_REQUIRE(ld % 8 == 0 && out_ld % 2 == 0 && bias_ld % 8 == 0 && bias_ld >= n,
              "bl_triangle_attention: leading dimensions must keep 16-byte rows");
@@ -411,7 +435,7 @@ extern "C" int bl_triangle_attention(const void *q, const void *k, const void *v
   const size_t smem = sizeof(Smem) + size_t(n_tiles) * kBK * sizeof(__nv_bfloat16);
   BL_REQUIRE(smem <= 227 * 1024, "bl_triangle_attention: too many tokens for the mask buffer");
   BL_CUDA(ensure_smem_limit(reinterpret_cast<const void *>(tri_flash_kernel), int(227 * 1024)));
-  dim3 grid(unsigned((n + kBQ - 1) / kBQ), unsigned(n), unsigned(heads));
+  dim3 grid(unsigned((n + kBQ - 1) / kBQ * kHeadsPerRow), unsigned(n));
   tri_flash_kernel<<<grid, kThreads, smem, as_stream(stream)>>>(args);
   BL_LAUNCH_CHECK();
   return BL_OK;
