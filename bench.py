@@ -91,6 +91,22 @@ def synthetic_inputs(n, seed):
     return s, z, mask, pair_mask
 
 
+def bench_config(n, world):
+    """The workload description shared by both arms."""
+    return {"workload": f"Pairformer block N={n} (TriMulOut+In, TriAttStart+End, Transition(z), single track)",
+            "tokens": n, "c_s": C_S, "c_z": C_Z, "heads": "4x32", "parallelism": f"dp{world} (one block per GPU)",
+            "l2": "inputs larger than L2: z 128 MiB fp32 plus per-op intermediates up to 256 MiB"}
+
+
+def max_over_ranks(value, dist, device):
+    """Max of a per-rank float over the process group (identity without one)."""
+    if dist is None:
+        return value
+    t = torch.tensor([float(value)], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def cpu_info():
     model = "unknown"
     try:
@@ -165,8 +181,7 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 3), "higher_is_better": False,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16-rounding oracle)", "data": "synthetic",
-        "config": {"workload": f"Pairformer block N={n}", "tokens": n, "c_s": C_S, "c_z": C_Z, "heads": "4x32",
-                   "parallelism": "cpu host"},
+        "config": bench_config(n, world),
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -324,10 +339,7 @@ def run_b200(args):
         launches_timed = observer.calls
         top_times = [e0.elapsed_time(e1) for name, a, e0, e1 in observer.records
                      if algorithmic_work(name, a)[2] == top_label]
-        if dist is not None:
-            t = torch.tensor([elapsed_ms], device=device)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            elapsed_ms = float(t.item())
+        elapsed_ms = max_over_ranks(elapsed_ms, dist, device)
         ms_per_step = elapsed_ms / args.steps
         value = ms_per_step / world  # aggregate: `world` blocks complete per step
 
@@ -354,10 +366,7 @@ def run_b200(args):
         torch.cuda.synchronize()
         barrier()
         e2e_ms = e_start.elapsed_time(e_end)
-        if dist is not None:
-            t = torch.tensor([e2e_ms], device=device)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_ms = float(t.item())
+        e2e_ms = max_over_ranks(e2e_ms, dist, device)
         e2e_value = e2e_ms / args.e2e_steps / world
         assert torch.isfinite(z_back).all() and torch.isfinite(s_back).all(), "non-finite block output"
         status = _lib.device_status(reset=True)
@@ -385,9 +394,7 @@ def run_b200(args):
         "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": round(ms_per_step, 4), "higher_is_better": False,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) inputs, N(0,1/128) weights)",
-        "config": {"workload": f"Pairformer block N={n} (TriMulOut+In, TriAttStart+End, Transition(z), single track)",
-                   "tokens": n, "c_s": C_S, "c_z": C_Z, "heads": "4x32", "parallelism": f"dp{world} (one block per GPU)",
-                   "l2": "inputs larger than L2: z 128 MiB fp32 plus per-op intermediates up to 272 MiB"},
+        "config": bench_config(n, world),
         "e2e": {"value": round(e2e_value, 4), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_timed,
         "launches_per_step": launches_per_step,

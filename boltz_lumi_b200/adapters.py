@@ -1,0 +1,121 @@
+"""Install the B200 pair-path forwards on a Boltz-2 model (the drop-in boundary).
+
+Mirrors the reference's ``install(model)`` (adapters.py:7-47): walk
+``model.named_modules()`` and rebind ``forward`` methods by class name and
+module path with ``types.MethodType``.  The rebound forwards fall back to the
+module's original class forward (upstream's eager code) only where upstream
+itself needs it -- autograd / training mode, or shapes the kernels do not
+cover (for example the template module's narrower pair width) -- exactly as
+the reference does; they never fall back to a CPU path.
+"""
+
+from types import MethodType
+
+import torch
+
+from . import forwards
+
+_TRIANGLE_ATTENTION = {"TriangleAttention", "TriangleAttentionEndingNode"}
+_TRIANGLE_MULTIPLICATION = {"TriangleMultiplicationIncoming", "TriangleMultiplicationOutgoing"}
+_DIFFUSION = {"AdaLN", "ConditionedTransitionBlock"}
+
+
+def device_supported(device=None):
+    """The kernels are built for sm_100a (B200)."""
+    if not torch.cuda.is_available():
+        return False
+    major, minor = torch.cuda.get_device_capability(device)
+    return (major, minor) == (10, 0)
+
+
+def _inference(module, *tensors):
+    return (not module.training and not torch.is_grad_enabled()
+            and all(t is None or t.is_cuda for t in tensors))
+
+
+def _bf16_autocast():
+    """The trunk kernels implement upstream's bf16-autocast contract (as the
+    reference requires, multiplication.py:61-62, triangle.py:156-159)."""
+    return torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16
+
+
+def _triangle_attention(self, x, mask=None, chunk_size=None, use_kernels=False):
+    cls = type(self)
+    if (use_kernels or not _inference(self, x, mask) or not _bf16_autocast() or x.dim() != 4
+            or x.shape[-1] != 128 or not forwards._attention_supported(self) or x.shape[1] > 4096):
+        return cls.forward(self, x, mask=mask, chunk_size=chunk_size, use_kernels=use_kernels)
+    starting = getattr(self, "starting", cls.__name__ != "TriangleAttentionEndingNode")
+    self.starting = starting
+    return forwards.triangle_attention_forward(self, x.float(), mask, chunk_size)
+
+
+def _triangle_multiplication(self, x, mask, use_kernels=False):
+    cls = type(self)
+    if (use_kernels or not _inference(self, x, mask) or not _bf16_autocast() or x.dim() != 4
+            or x.shape[-1] != 128 or self.p_in.weight.shape != (256, 128) or self.p_in.bias is not None):
+        return cls.forward(self, x, mask, use_kernels=use_kernels)
+    self.outgoing = cls.__name__ == "TriangleMultiplicationOutgoing"
+    return forwards.triangle_multiplication_forward(self, x.float(), mask)
+
+
+def _pair_transition(self, x, chunk_size=None):
+    cls = type(self)
+    if (chunk_size is not None or not _inference(self, x) or not _bf16_autocast() or x.shape[-1] % 8
+            or self.fc1.weight.shape[0] % 64 or any(f.bias is not None for f in (self.fc1, self.fc2, self.fc3))):
+        return cls.forward(self, x, chunk_size=chunk_size)
+    return forwards.transition_forward(self, x.float())
+
+
+def _adaln(self, a, s):
+    if (not _inference(self, a, s) or torch.is_autocast_enabled("cuda") or a.dtype != torch.float32
+            or s.dtype != torch.float32 or a.shape[-1] % 4 or a.shape[-1] > 2048):
+        return type(self).forward(self, a, s)
+    return forwards.adaln_forward(self, a.contiguous(), s.contiguous())
+
+
+def _conditioned_transition(self, a, s):
+    if (not _inference(self, a, s) or torch.is_autocast_enabled("cuda") or a.dtype != torch.float32
+            or s.dtype != torch.float32 or a.shape[-1] % 4 or a.shape[-1] > 2048):
+        return type(self).forward(self, a, s)
+    return forwards.conditioned_transition_forward(self, a.contiguous(), s.contiguous())
+
+
+def install(model, require_device=True):
+    """Rebind the hot-path forwards of ``model`` in place; idempotent.
+
+    Returns the number of modules rebound.  Like the reference, modules are
+    matched by class name: every TriangleAttention / TriangleAttentionEndingNode
+    and TriangleMultiplication{Incoming,Outgoing}, every ``*.transition_z``
+    Transition, and the AdaLN / ConditionedTransitionBlock modules under
+    ``structure_module.score_model``.
+    """
+    if getattr(model, "_b200_optimized", False):
+        return 0
+    if require_device and not device_supported():
+        return 0
+    count = 0
+    for name, module in model.named_modules():
+        cls = type(module).__name__
+        if cls in _TRIANGLE_ATTENTION:
+            module.forward = MethodType(_triangle_attention, module)
+            count += 1
+        elif cls in _TRIANGLE_MULTIPLICATION:
+            module.forward = MethodType(_triangle_multiplication, module)
+            count += 1
+        elif cls == "Transition" and name.endswith("transition_z"):
+            module.forward = MethodType(_pair_transition, module)
+            count += 1
+        elif cls in _DIFFUSION and name.startswith("structure_module.score_model."):
+            module.forward = MethodType(_adaln if cls == "AdaLN" else _conditioned_transition, module)
+            count += 1
+    model._b200_optimized = True
+    return count
+
+
+def uninstall(model):
+    """Restore the class forwards rebound by :func:`install`."""
+    for _, module in model.named_modules():
+        if "forward" in module.__dict__ and getattr(module.forward, "__func__", None) in (
+                _triangle_attention, _triangle_multiplication, _pair_transition, _adaln, _conditioned_transition):
+            del module.forward
+    model._b200_optimized = False

@@ -1,0 +1,150 @@
+"""CPU tests of the host-side logic: adapter installation, weight caches,
+input validation and the benchmark's multi-rank plumbing (gloo)."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+from torch import nn
+
+from boltz_lumi_b200 import adapters, forwards, layers
+
+
+class Transition(nn.Module):
+    """A stand-in with the upstream class name and attributes."""
+
+    def __init__(self):
+        super().__init__()
+        self.fc1 = nn.Linear(8, 64, bias=False)
+
+    def forward(self, x, chunk_size=None):
+        return x
+
+
+class AdaLN(nn.Module):
+    def forward(self, a, s):
+        return a
+
+
+class FakeModel(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.pairformer = nn.Module()
+        self.pairformer.transition_z = Transition()
+        self.pairformer.transition_s = Transition()
+        self.pairformer.tri_att_start = layers.TriangleAttention(128, 32, 4)
+        self.pairformer.tri_att_end = layers.TriangleAttentionEndingNode(128, 32, 4)
+        self.pairformer.tri_mul_out = layers.TriangleMultiplicationOutgoing(128)
+        self.pairformer.tri_mul_in = layers.TriangleMultiplicationIncoming(128)
+        self.structure_module = nn.Module()
+        self.structure_module.score_model = nn.Module()
+        self.structure_module.score_model.adaln = AdaLN()
+        self.other_adaln = AdaLN()
+
+
+def test_install_rebinds_by_class_name_and_path():
+    model = FakeModel()
+    count = adapters.install(model, require_device=False)
+    # 2 attentions + 2 multiplications + transition_z + the score-model AdaLN
+    assert count == 6
+    assert "forward" in model.pairformer.transition_z.__dict__
+    assert "forward" not in model.pairformer.transition_s.__dict__
+    assert "forward" in model.structure_module.score_model.adaln.__dict__
+    assert "forward" not in model.other_adaln.__dict__
+    assert adapters.install(model, require_device=False) == 0  # idempotent
+    adapters.uninstall(model)
+    assert "forward" not in model.pairformer.transition_z.__dict__
+    assert not model._b200_optimized
+
+
+def test_rebound_forward_falls_back_outside_inference():
+    """With grad enabled the upstream (class) forward runs, as in the reference."""
+    model = FakeModel()
+    adapters.install(model, require_device=False)
+    x = torch.randn(1, 2, 2, 8)
+    assert model.pairformer.transition_z(x) is x  # the stand-in class forward
+
+
+def test_install_requires_sm100_device():
+    if torch.cuda.is_available():
+        pytest.skip("CPU-only check")
+    assert adapters.install(FakeModel()) == 0
+
+
+def test_weight_cache_invalidation():
+    """Derived weights rebuild when a source parameter changes (multiplication.py:29-40)."""
+    module = layers.TriangleMultiplicationOutgoing(128)
+    first = forwards._multiplication_weights(module)
+    again = forwards._multiplication_weights(module)
+    assert first is again
+    with torch.no_grad():
+        module.p_in.weight.add_(0.01)
+    new = forwards._multiplication_weights(module)
+    assert new is not first
+    assert torch.equal(new["w_in"][:256], module.p_in.weight.bfloat16())
+    assert torch.equal(new["w_out"][:128, :128], module.p_out.weight.bfloat16())
+    assert torch.count_nonzero(new["w_out"][:128, 128:]) == 0
+
+
+def test_attention_weights_layout():
+    module = layers.TriangleAttention(128, 32, 4)
+    w = forwards._attention_weights(module)
+    assert w["w_in"].shape == (512, 128) and w["w_heads"].shape == (4, 128)
+    assert torch.equal(w["w_in"][256:384], module.mha.linear_v.weight.bfloat16())
+    assert torch.equal(w["b_in"][384:], module.mha.linear_g.bias)
+    assert torch.count_nonzero(w["b_in"][:384]) == 0
+
+
+def test_pair_input_validation():
+    with pytest.raises(RuntimeError, match="CUDA"):
+        forwards._check_pair_input(torch.zeros(1, 4, 4, 128), None)
+    with pytest.raises(RuntimeError, match="residual"):
+        forwards._check_residual(torch.zeros(1, 4, 4, 128, dtype=torch.bfloat16), torch.zeros(1, 4, 4, 128))
+
+
+def test_layers_are_inference_only():
+    mod = layers.Transition(128, 512)
+    with pytest.raises(RuntimeError, match="inference-only"):
+        mod(torch.zeros(1, 2, 2, 128))
+
+
+# ---------------------------------------------------------------------------
+# Multi-rank plumbing of bench.py on gloo (world size 2)
+# ---------------------------------------------------------------------------
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, results):
+    import torch.distributed as dist
+
+    import bench
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        # Each rank "measured" a different time; everyone must report the max.
+        results[rank] = bench.max_over_ranks(10.0 + rank, dist, torch.device("cpu"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bench_max_over_ranks_gloo():
+    port = _free_port()
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    mp.start_processes(_rank_main, args=(2, port, results), nprocs=2, start_method="spawn", join=True)
+    assert dict(results) == {0: 11.0, 1: 11.0}
+
+
+def test_bench_reference_arm_rank_nonzero_exits_without_work(monkeypatch):
+    import bench
+
+    monkeypatch.setenv("RANK", "1")
+    monkeypatch.setenv("WORLD_SIZE", "2")
+    ns = type("A", (), dict(steps=1, warmup=0, n=8, impl="reference"))()
+    assert bench.run_reference(ns) == 0

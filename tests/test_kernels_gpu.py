@@ -259,3 +259,36 @@ def test_linear_fused(m, gate, residual):
         assert_close(zc.cpu() - z0, y, atol=1e-5, rtol=rtol)
     else:
         assert_close(out.float(), y, atol=1e-5, rtol=rtol)
+
+
+# ---------------------------------------------------------------------------
+# Kernels against the committed golden vectors (reference test expressions)
+# ---------------------------------------------------------------------------
+def _golden():
+    from pathlib import Path
+
+    return torch.load(Path(__file__).resolve().parent / "golden" / "kernel_expressions.pt")
+
+
+def test_golden_ordered_softmax():
+    for case in _golden()["ordered_softmax"]:
+        bf16 = case["scores"].dtype == torch.bfloat16
+        got = kernels.ordered_softmax(case["scores"].cuda(), case["bias"].cuda(), case["mask"].cuda())
+        assert_close(got.float(), case["expected"].float(), atol=4e-3 if bf16 else 1e-5)
+
+
+def test_golden_silu_and_gate():
+    for case in _golden()["silu"]:
+        got = kernels.silu_mul(case["a"].cuda(), case["b"].cuda())
+        assert_close(got.float(), case["expected"].float(), atol=1e-30, rtol=2 * BF16_ULP)
+    case = _golden()["gate"]
+    got = kernels.gate(case["p"].cuda(), case["g"].cuda())
+    assert_close(got.float(), case["expected"].float(), atol=1e-30, rtol=2 * BF16_ULP)
+
+
+def test_golden_diffusion_epilogues():
+    case = _golden()["epilogue"]
+    a, b, c, wide = (case[k].cuda() for k in ("a", "b", "c", "wide"))
+    assert_close(kernels.epilogue(a, b, c, kernels.MODULATION), case["modulation"], atol=1e-5)
+    assert_close(kernels.epilogue(a, b, None, kernels.GATE), case["gate"], atol=1e-5)
+    assert_close(kernels.epilogue(wide, b, None, kernels.GATED_SWIGLU), case["swiglu"], atol=1e-4)
