@@ -236,6 +236,26 @@ BL_API int bl_triangle_attention(const void *q, const void *k, const void *v, co
                                  float inf, int64_t heads, int64_t head_dim, int64_t n, void *out,
                                  int64_t out_ld, void *stream);
 
+/*
+ * Pair transition (LayerNorm -> fc1|fc2 -> SwiGLU -> fc3, the bf16-autocast
+ * contract) that allocates no device memory.  This entry point has no
+ * counterpart in the reference; it exists for callers that may not allocate
+ * device memory while they run inference -- hosts that keep all of HBM in
+ * their own pool, or plugin interfaces that pass a kernel only its inputs
+ * and outputs.  The intermediates live in a fixed array compiled into the
+ * library (3.25 MiB, held on every GPU that loads the library until exit).
+ *   x: fp32 [rows, 128]; ln_weight, ln_bias: fp32 [128] (may be NULL);
+ *   w12: bf16 [1024, 128] (fc1 rows then fc2 rows); w3: bf16 [128, 512];
+ *   out: bf16 [rows, 128].  rows <= 1024, otherwise BL_ERR_INVALID.
+ * Runs on the current device.  Its first call on a device looks up the
+ * array's device address, so make that first call before any stream
+ * capture.  All calls on a device share the array: calls that overlap on the
+ * GPU (e.g. on two streams) race; calls ordered on one stream do not.
+ */
+BL_API int bl_pair_transition_static(const float *x, int64_t rows, const float *ln_weight,
+                                     const float *ln_bias, float eps, const void *w12, const void *w3,
+                                     void *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
