@@ -1,0 +1,438 @@
+// Flash triangle attention on tcgen05 tensor cores (starting and ending node).
+//
+// Same contract as the mma.sync kernel of triangle_attention.cu (upstream's
+// bf16 rounding points, fused sigmoid output gate, strides for the ending
+// node), restructured for Blackwell:
+//   * S = Q K^T for a 64-key tile is one pair of tcgen05.mma (M = 128 queries,
+//     N = 64 keys, K = 32) into TMEM, double-buffered so the MMA of tile j+1
+//     runs while the softmax of tile j is in progress;
+//   * one softmax thread per query row reads its 64 scores with two
+//     tcgen05.ld, applies the ordered rounding (bf16 score -> + mask -> + bias)
+//     on packed bf16x2, and writes P = exp2(t log2 e - m log2 e) (fp32 MUFU,
+//     rounded to bf16) into a 128-byte-swizzled shared tile -- no cross-thread
+//     reductions at all;
+//   * O += P V is a tcgen05.mma with P from shared memory and V in its natural
+//     [key][d] layout read MN-major; a constant block of ones appended to V
+//     makes the same MMA produce the row sums of the bf16 P in column 32;
+//   * O lives in TMEM and is rescaled (tcgen05.ld/st) only when a row maximum
+//     grows by more than 2^8, so P stays <= 256 and rescales are rare;
+//   * Q, K, V and the bias tiles arrive by TMA (3-D maps carry the
+//     starting/ending-node strides), no multicast.
+// Warp roles: warp 0 TMA producer, warp 1 TMEM allocation + MMA issue, warps
+// 2..5 softmax and epilogue (TMEM lane quarter = warp % 4, one row per thread).
+#include "tc.cuh"
+
+namespace bl {
+namespace {
+
+constexpr int kD = 32;
+constexpr int kBQ = 128;
+constexpr int kBK = 64;
+constexpr int kHeads = 4;
+constexpr int kMaxTiles = 64;  // n <= 4096
+constexpr int kThreads = 192;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleLog2 = 8.f;  // keep P = exp2(x - ref) <= 2^8 before rescaling O
+
+// Shared memory layout (offsets from a 1024-byte aligned base).
+constexpr int kQOff = 0;                 // Q   [128][32] bf16, 64B-swizzled       8 KB
+constexpr int kKOff = 8192;              // K   2 x [64][32] bf16, 64B-swizzled   2 x 4 KB
+constexpr int kVOff = 16384;             // V   2 x ([64][32] bf16 + ones block)  2 x 8 KB
+constexpr int kVStride = 8192;
+constexpr int kOnesOff = 4096;           // ones block right after each V tile
+constexpr int kBiasOff = 32768;          // bias 2 x [128][64] bf16, 128B-swizzled 2 x 16 KB
+constexpr int kPOff = 65536;             // P   2 x [128][64] bf16, 128B-swizzled 2 x 16 KB
+constexpr int kBarOff = 98304;
+constexpr int kFlagOff = kBarOff + 256;  // per-key-tile "has masked keys" flags
+constexpr int kMaskOff = kFlagOff + kMaxTiles * 4;
+constexpr int kStageTx = 4096 + 4096 + 16384;  // K + V + bias bytes per stage
+
+// TMEM columns: S[0] 0..63, S[1] 64..127, O|l 128..175.
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kOCol = 128;
+
+constexpr uint32_t kNegInf = 0xFF80FF80u;
+constexpr uint32_t kNegPad = 0xF14AF14Au;  // bf16x2 (-1e30, -1e30): finite, exp2 -> 0
+
+struct TcArgs {
+  const __nv_bfloat16 *g;
+  int64_t ld, so, si;
+  const float *mask;
+  int64_t ms_o, ms_k;
+  float inf, q_divisor;
+  __nv_bfloat16 *out;
+  int64_t out_ld;
+  int n;
+  unsigned int *status;
+};
+
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t add_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t max_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 64-byte swizzle descriptor (K-major: LBO unused = 16 B; MN-major: LBO = block stride), SBO = 512 B.
+__device__ __forceinline__ uint64_t desc_sw64(uint32_t saddr, uint32_t lbo_bytes) {
+  return uint64_t((saddr & 0x3FFFFu) >> 4) | (uint64_t((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+         (uint64_t(512 >> 4) << 32) | (uint64_t(1) << 46) | (uint64_t(4) << 61);
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Warp-uniform bounded wait: the whole warp continues only if every lane saw the phase.
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, unsigned int *status, unsigned code) {
+  return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, status, code));
+}
+
+__global__ void __launch_bounds__(kThreads, 2)
+    tri_flash_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                        const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_bias,
+                        const TcArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBarOff);
+  uint64_t *q_full = bars + 0;
+  uint64_t *st_full = bars + 1;   // [2] K, V, bias of a key tile landed
+  uint64_t *st_empty = bars + 3;  // [2] P.V of that tile completed (K, V, bias, P reusable)
+  uint64_t *s_full = bars + 5;    // [2] S tile in TMEM
+  uint64_t *s_empty = bars + 7;   // [2] S tile read by the softmax warps
+  uint64_t *p_full = bars + 9;    // [2] P tile written (and O rescaled if needed)
+  uint64_t *o_full = bars + 11;   // all P.V done
+  uint64_t *q_ready = bars + 12;  // Q scaled in place by the softmax warps
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 13);
+  int *tile_masked = reinterpret_cast<int *>(smem + kFlagOff);
+  __nv_bfloat16 *mask_bias = reinterpret_cast<__nv_bfloat16 *>(smem + kMaskOff);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n = args.n;
+  const int h = blockIdx.x % kHeads;
+  const int q0 = (blockIdx.x / kHeads) * kBQ;
+  const int outer = blockIdx.y;
+  const int n_tiles = (n + kBK - 1) / kBK;
+
+  if (tid < kMaxTiles) tile_masked[tid] = 0;
+  if (tid == 0) {
+    tc::mbar_init(q_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&st_full[b], 1);
+      tc::mbar_init(&st_empty[b], 1);
+      tc::mbar_init(&s_full[b], 1);
+      tc::mbar_init(&s_empty[b], 4);
+      tc::mbar_init(&p_full[b], 4);
+    }
+    tc::mbar_init(o_full, 1);
+    tc::mbar_init(q_ready, 4);
+    tc::fence_mbar_init();
+  }
+  // Ones block after each V tile (its swizzle is irrelevant: every element is 1).
+  for (int i = tid; i < 2 * 4096 / 16; i += kThreads) {
+    const int b = i / 256, off = (i % 256) * 16;
+    *reinterpret_cast<uint4 *>(smem + kVOff + b * kVStride + kOnesOff + off) =
+        make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  __syncthreads();
+  // Mask bias of this outer row (bf16; for mask in {0, 1} adding it rounds
+  // exactly like the fp32 value) and per-tile "any key masked" flags.
+  for (int key = tid; key < n_tiles * kBK; key += kThreads) {
+    const float mb =
+        key < n ? args.inf * (args.mask[int64_t(outer) * args.ms_o + int64_t(key) * args.ms_k] - 1.f) : 0.f;
+    mask_bias[key] = __float2bfloat16_rn(mb);
+    if (mb != 0.f) atomicOr(&tile_masked[key / kBK], 1);
+  }
+  tc::fence_proxy_async_smem();
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      tc::prefetch_tmap(&map_q);
+      tc::prefetch_tmap(&map_k);
+      tc::prefetch_tmap(&map_v);
+      tc::prefetch_tmap(&map_bias);
+      tc::mbar_arrive_expect_tx(q_full, kBQ * kD * 2);
+      tc::tma_load_3d(smem + kQOff, &map_q, q_full, h * kD, q0, outer);
+      for (int j = 0; j < n_tiles; ++j) {
+        const int b = j & 1;
+        if (!tc::mbar_wait(&st_empty[b], ((j >> 1) & 1) ^ 1u, args.status, 0x201)) break;
+        tc::mbar_arrive_expect_tx(&st_full[b], kStageTx);
+        tc::tma_load_3d(smem + kKOff + b * 4096, &map_k, &st_full[b], h * kD, j * kBK, outer);
+        tc::tma_load_3d(smem + kVOff + b * kVStride, &map_v, &st_full[b], h * kD, j * kBK, outer);
+        tc::tma_load_3d(smem + kBiasOff + b * 16384, &map_bias, &st_full[b], j * kBK, q0, h);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = tc::idesc_bf16(128, kBK, false, false);
+      constexpr uint32_t idesc_pv = tc::idesc_bf16(128, 48, false, true);
+      const uint32_t q_addr = tc::smem_u32(smem + kQOff);
+      bool ok = tc::mbar_wait(q_ready, 0, args.status, 0x202);
+      auto issue_s = [&](int j) {
+        const int b = j & 1;
+        if (!tc::mbar_wait(&st_full[b], (j >> 1) & 1, args.status, 0x203)) return false;
+        if (!tc::mbar_wait(&s_empty[b], ((j >> 1) & 1) ^ 1u, args.status, 0x204)) return false;
+        tc::tc_fence_after();
+        const uint32_t k_addr = tc::smem_u32(smem + kKOff + b * 4096);
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk)
+          tc::umma_f16_ss(tmem + uint32_t(b * kBK), desc_sw64(q_addr + kk * 32, 16), desc_sw64(k_addr + kk * 32, 16),
+                          idesc_s, kk);
+        tc::umma_commit(&s_full[b]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
+        const int b = j & 1;
+        if (!tc::mbar_wait(&p_full[b], (j >> 1) & 1, args.status, 0x205)) break;
+        tc::tc_fence_after();
+        const uint32_t p_addr = tc::smem_u32(smem + kPOff + b * 16384);
+        const uint32_t v_addr = tc::smem_u32(smem + kVOff + b * kVStride);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          tc::umma_f16_ss(tmem + kOCol, tc::desc_sw128(p_addr + kk * 32, 16), desc_sw64(v_addr + kk * 1024, kOnesOff),
+                          idesc_pv, (j | kk) != 0);
+        tc::umma_commit(&st_empty[b]);
+        if (j + 1 == n_tiles) tc::umma_commit(o_full);
+      }
+    }
+  } else {
+    // ---------------- softmax + epilogue: one query row per thread ----------------
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+    float m_ref = -INFINITY;  // reference maximum of the exponentials of this row
+    // Upstream divides q by sqrt(d) after the projection and rounds to bf16
+    // (_prep_qkv(apply_scale=True), triangle.py:80): apply that to this
+    // thread's Q row in place (the 64-byte swizzle keeps a row in its 64 bytes).
+    bool ok = warp_wait(q_full, 0, args.status, 0x20B);
+    if (ok) {
+      uint4 *q_row = reinterpret_cast<uint4 *>(smem + kQOff + row * 64);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint4 v = q_row[c];
+        uint32_t *w = &v.x;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          w[e] = pack_bf16x2(__fdiv_rn(bf16_lo(w[e]), args.q_divisor), __fdiv_rn(bf16_hi(w[e]), args.q_divisor));
+        q_row[c] = v;
+      }
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(q_ready);
+    }
+    for (int j = 0; j < n_tiles && ok; ++j) {
+      const int b = j & 1;
+      const uint32_t ph = (j >> 1) & 1;
+      if (!(ok = warp_wait(&s_full[b], ph, args.status, 0x206))) break;
+      tc::tc_fence_after();
+      uint32_t s[64];
+      tc::tmem_ld_32x32b_x32(lane_base + b * kBK, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+      tc::tmem_ld_32x32b_x32(lane_base + b * kBK + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+      tc::tmem_ld_wait();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&s_empty[b]);
+      if (!(ok = warp_wait(&st_full[b], ph, args.status, 0x207))) break;
+
+      // Ordered rounding: t = bf16(bf16(bf16(s) + mask) + bias), packed per key pair.
+      const int k0 = j * kBK;
+      const uint8_t *bias_row = smem + kBiasOff + b * 16384 + row * 128;
+      const bool masked = tile_masked[j] != 0;
+      uint32_t t[32];
+      uint32_t tmax = kNegInf;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {  // 16-byte chunk c = keys 8c .. 8c + 7
+        const uint4 bv = *reinterpret_cast<const uint4 *>(bias_row + ((c ^ (row & 7)) << 4));
+        const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int pr = c * 4 + e;
+          uint32_t x = cvt_bf16x2(__uint_as_float(s[2 * pr]), __uint_as_float(s[2 * pr + 1]));
+          if (masked) x = add_bf16x2(x, *reinterpret_cast<const uint32_t *>(mask_bias + k0 + 2 * pr));
+          x = add_bf16x2(x, bw[e]);
+          t[pr] = x;
+        }
+      }
+      if (k0 + kBK > n) {  // keys past n contribute nothing
+#pragma unroll
+        for (int pr = 0; pr < 32; ++pr) {
+          const int key = k0 + 2 * pr;
+          const uint32_t keep = (key < n ? 0x0000ffffu : 0u) | (key + 1 < n ? 0xffff0000u : 0u);
+          t[pr] = (t[pr] & keep) | (kNegPad & ~keep);
+        }
+      }
+#pragma unroll
+      for (int pr = 0; pr < 32; ++pr) tmax = max_bf16x2(tmax, t[pr]);
+      const float m_tile = fmaxf(bf16_lo(tmax), bf16_hi(tmax));
+
+      // Reference maximum: set on the first tile; raised (with O rescaled)
+      // only when this tile's maximum exceeds it by more than 2^8 in exp2.
+      const bool first = m_ref == -INFINITY;
+      const bool grow = !first && (m_tile - m_ref) * kLog2e > kRescaleLog2;
+      if (__any_sync(0xffffffffu, grow)) {
+        // O holds tiles < j: wait for the P.V of tile j - 1, then scale in place.
+        if (!(ok = warp_wait(&st_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, args.status, 0x208))) break;
+        tc::tc_fence_after();
+        const float alpha = grow ? fast_exp2((m_ref - m_tile) * kLog2e) : 1.f;
+        uint32_t o[32], l16[16];
+        tc::tmem_ld_32x32b_x32(lane_base + kOCol, o);
+        tc::tmem_ld_32x32b_x16(lane_base + kOCol + 32, l16);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) l16[i] = __float_as_uint(__uint_as_float(l16[i]) * alpha);
+        tmem_st_32x32b_x16(lane_base + kOCol, *reinterpret_cast<const uint32_t(*)[16]>(&o[0]));
+        tmem_st_32x32b_x16(lane_base + kOCol + 16, *reinterpret_cast<const uint32_t(*)[16]>(&o[16]));
+        tmem_st_32x32b_x16(lane_base + kOCol + 32, l16);
+        tmem_st_wait();
+      }
+      if (first || grow) m_ref = m_tile;
+      const float ml = m_ref * kLog2e;
+
+      // P buffer b was last read by the P.V of tile j - 2.
+      if (!(ok = warp_wait(&st_empty[b], ph ^ 1u, args.status, 0x209))) break;
+      uint8_t *p_row = smem + kPOff + b * 16384 + row * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t x = t[c * 4 + e];
+          w[e] = cvt_bf16x2(fast_exp2(fmaf(bf16_lo(x), kLog2e, -ml)), fast_exp2(fmaf(bf16_hi(x), kLog2e, -ml)));
+        }
+        *reinterpret_cast<uint4 *>(p_row + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&p_full[b]);
+    }
+    // Epilogue: O / l, bf16, gate, store.
+    if (ok && warp_wait(o_full, 0, args.status, 0x20A)) {
+      tc::tc_fence_after();
+      uint32_t o[32], l16[16];
+      tc::tmem_ld_32x32b_x32(lane_base + kOCol, o);
+      tc::tmem_ld_32x32b_x16(lane_base + kOCol + 32, l16);
+      tc::tmem_ld_wait();
+      const int qi = q0 + row;
+      if (qi < n) {
+        const float inv = 1.f / __uint_as_float(l16[0]);
+        const int64_t pair = int64_t(outer) * args.so + int64_t(qi) * args.si;
+        const uint4 *g4 = reinterpret_cast<const uint4 *>(args.g + pair * args.ld + h * kD);
+        uint4 *o4 = reinterpret_cast<uint4 *>(args.out + pair * args.out_ld + h * kD);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint4 gv = g4[c];
+          const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int d = c * 8 + e * 2;
+            const float o0 = bf16r(__uint_as_float(o[d]) * inv), o1 = bf16r(__uint_as_float(o[d + 1]) * inv);
+            const float g0 = bf16r(sigmoidf_fast(bf16_lo(gw[e]))), g1 = bf16r(sigmoidf_fast(bf16_hi(gw[e])));
+            w[e] = pack_bf16x2(o0 * g0, o1 * g1);
+          }
+          o4[c] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+bool pair_rows_map(CUtensorMap *map, const void *base, int64_t ld, int64_t so, int64_t si, int n, int box_rows) {
+  // Element (column c, inner b, outer a) at base + (a*so + b*si)*ld + c.
+  uint64_t dims[3] = {uint64_t(kHeads * kD), uint64_t(n), uint64_t(n)};
+  uint64_t strides[2] = {uint64_t(si * ld * 2), uint64_t(so * ld * 2)};
+  uint32_t box[3] = {uint32_t(kD), uint32_t(box_rows), 1};
+  return encode_tmap(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
+}  // namespace
+}  // namespace bl
+
+using namespace bl;
+
+extern "C" int bl_triangle_attention_tc(const void *q, const void *k, const void *v, const void *g, int64_t ld,
+                                        int64_t so, int64_t si, const void *bias, int64_t bias_ld, int64_t bias_hs,
+                                        const float *mask, int64_t ms_o, int64_t ms_k, float inf, int64_t heads,
+                                        int64_t head_dim, int64_t n, void *out, int64_t out_ld, void *stream) {
+  BL_REQUIRE(head_dim == kD && heads == kHeads, "bl_triangle_attention: 4 heads x 32 supported");
+  BL_REQUIRE(n >= 0, "bl_triangle_attention: bad shape");
+  if (n == 0) return BL_OK;
+  BL_REQUIRE(n <= kMaxTiles * kBK, "bl_triangle_attention: at most 4096 tokens");
+  BL_REQUIRE(q && k && v && g && bias && mask && out, "bl_triangle_attention: null pointer");
+  BL_REQUIRE(ld % 8 == 0 && out_ld % 8 == 0 && bias_ld % 8 == 0 && bias_ld >= n && bias_hs % 8 == 0,
+             "bl_triangle_attention: leading dimensions must keep 16-byte rows");
+  BL_REQUIRE(aligned_to(q, 16) && aligned_to(k, 16) && aligned_to(v, 16) && aligned_to(g, 16) &&
+                 aligned_to(bias, 16) && aligned_to(out, 16),
+             "bl_triangle_attention: pointers must be 16-byte aligned");
+  CUtensorMap map_q, map_k, map_v, map_bias;
+  BL_REQUIRE(pair_rows_map(&map_q, q, ld, so, si, int(n), kBQ) && pair_rows_map(&map_k, k, ld, so, si, int(n), kBK) &&
+                 pair_rows_map(&map_v, v, ld, so, si, int(n), kBK),
+             "bl_triangle_attention: cannot encode the q/k/v tensor maps");
+  {
+    uint64_t dims[3] = {uint64_t(bias_ld), uint64_t(n), uint64_t(kHeads)};
+    uint64_t strides[2] = {uint64_t(bias_ld * 2), uint64_t(bias_hs * 2)};
+    uint32_t box[3] = {kBK, kBQ, 1};
+    BL_REQUIRE(encode_tmap(&map_bias, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, bias, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B),
+               "bl_triangle_attention: cannot encode the bias tensor map");
+  }
+  TcArgs args;
+  args.g = static_cast<const __nv_bfloat16 *>(g);
+  args.ld = ld, args.so = so, args.si = si;
+  args.mask = mask, args.ms_o = ms_o, args.ms_k = ms_k;
+  args.inf = inf;
+  args.q_divisor = sqrtf(float(head_dim));
+  args.out = static_cast<__nv_bfloat16 *>(out);
+  args.out_ld = out_ld;
+  args.n = int(n);
+  args.status = device_status_ptr();
+  BL_REQUIRE(args.status, "bl_triangle_attention: device status word unavailable");
+  const int n_tiles = int((n + kBK - 1) / kBK);
+  const int smem = kMaskOff + n_tiles * kBK * 2 + 1024;
+  BL_CUDA(ensure_smem_limit(reinterpret_cast<const void *>(tri_flash_tc_kernel), 232448));
+  dim3 grid(unsigned((n + kBQ - 1) / kBQ * kHeads), unsigned(n));
+  tri_flash_tc_kernel<<<grid, kThreads, smem, as_stream(stream)>>>(map_q, map_k, map_v, map_bias, args);
+  BL_LAUNCH_CHECK();
+  return BL_OK;
+}

@@ -237,6 +237,17 @@ BL_API int bl_triangle_attention(const void *q, const void *k, const void *v, co
                                  int64_t out_ld, void *stream);
 
 /*
+ * Same contract as bl_triangle_attention, computed with tcgen05 tensor cores
+ * (S and P.V in TMEM, TMA-fed tiles, one softmax thread per query row).
+ * Pointers 16-byte aligned; ld, out_ld, bias_ld, bias_hs multiples of 8.
+ */
+BL_API int bl_triangle_attention_tc(const void *q, const void *k, const void *v, const void *g, int64_t ld,
+                                    int64_t so, int64_t si, const void *bias, int64_t bias_ld,
+                                    int64_t bias_hs, const float *mask, int64_t ms_o, int64_t ms_k,
+                                    float inf, int64_t heads, int64_t head_dim, int64_t n, void *out,
+                                    int64_t out_ld, void *stream);
+
+/*
  * Pair transition (LayerNorm -> fc1|fc2 -> SwiGLU -> fc3, the bf16-autocast
  * contract) that allocates no device memory.  This entry point has no
  * counterpart in the reference; it exists for callers that may not allocate
