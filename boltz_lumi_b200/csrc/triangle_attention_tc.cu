@@ -8,16 +8,16 @@
 //     runs while the softmax of tile j is in progress;
 //   * one softmax thread per query row reads its 64 scores with two
 //     tcgen05.ld, applies the ordered rounding (bf16 score -> + mask -> + bias)
-//     on packed bf16x2, and writes P = exp2(t log2 e - m log2 e) (fp32 MUFU,
-//     rounded to bf16) into a 128-byte-swizzled shared tile -- no cross-thread
-//     reductions at all;
-//   * O += P V is a tcgen05.mma with P from shared memory and V in its natural
+//     on packed bf16x2, and computes P = exp2(t log2 e - m log2 e) (fp32 MUFU,
+//     rounded to bf16) -- no cross-thread reductions at all;
+//   * P goes back into TMEM over the columns its S tile occupied, and
+//     O += P V is a tcgen05.mma with A = P from TMEM and B = V in its natural
 //     [key][d] layout read MN-major; a constant block of ones appended to V
 //     makes the same MMA produce the row sums of the bf16 P in column 32;
 //   * O lives in TMEM and is rescaled (tcgen05.ld/st) only when a row maximum
 //     grows by more than 2^8, so P stays <= 256 and rescales are rare;
-//   * Q, K, V and the bias tiles arrive by TMA (3-D maps carry the
-//     starting/ending-node strides), no multicast.
+//   * Q, K, V and the bias tiles arrive by TMA through a 4-deep ring (3-D
+//     maps carry the starting/ending-node strides); no multicast.
 // Warp roles: warp 0 TMA producer, warp 1 TMEM allocation + MMA issue, warps
 // 2..5 softmax and epilogue (TMEM lane quarter = warp % 4, one row per thread).
 #include "tc.cuh"
@@ -31,23 +31,23 @@ constexpr int kBK = 64;
 constexpr int kHeads = 4;
 constexpr int kMaxTiles = 64;  // n <= 4096
 constexpr int kThreads = 192;
+constexpr int kStages = 4;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.f;  // keep P = exp2(x - ref) <= 2^8 before rescaling O
 
 // Shared memory layout (offsets from a 1024-byte aligned base).
-constexpr int kQOff = 0;                 // Q   [128][32] bf16, 64B-swizzled       8 KB
-constexpr int kKOff = 8192;              // K   2 x [64][32] bf16, 64B-swizzled   2 x 4 KB
-constexpr int kVOff = 16384;             // V   2 x ([64][32] bf16 + ones block)  2 x 8 KB
-constexpr int kVStride = 8192;
-constexpr int kOnesOff = 4096;           // ones block right after each V tile
-constexpr int kBiasOff = 32768;          // bias 2 x [128][64] bf16, 128B-swizzled 2 x 16 KB
-constexpr int kPOff = 65536;             // P   2 x [128][64] bf16, 128B-swizzled 2 x 16 KB
-constexpr int kBarOff = 98304;
-constexpr int kFlagOff = kBarOff + 256;  // per-key-tile "has masked keys" flags
+constexpr int kQOff = 0;                        // Q [128][32] bf16, 64B-swizzled              8 KB
+constexpr int kStageOff = 8192;                 // ring of {K, V, bias}
+constexpr int kKBytes = kBK * kD * 2;           // K [64][32] bf16, 64B-swizzled               4 KB
+constexpr int kVBytes = kBK * kD * 2;           // V [64][32] bf16, 64B-swizzled               4 KB
+constexpr int kBiasBytes = kBQ * kBK * 2;       // bias [128][64] bf16, 128B-swizzled         16 KB
+constexpr int kStageBytes = kKBytes + kVBytes + kBiasBytes;
+constexpr int kOnesOff = kStageOff + kStages * kStageBytes;  // [64][32] ones (V's extra N block)
+constexpr int kBarOff = kOnesOff + kVBytes;
+constexpr int kFlagOff = kBarOff + 256;         // per-key-tile "has masked keys" flags
 constexpr int kMaskOff = kFlagOff + kMaxTiles * 4;
-constexpr int kStageTx = 4096 + 4096 + 16384;  // K + V + bias bytes per stage
 
-// TMEM columns: S[0] 0..63, S[1] 64..127, O|l 128..175.
+// TMEM columns: S/P[0] 0..63, S/P[1] 64..127, O|l 128..175.
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kOCol = 128;
 
@@ -93,16 +93,6 @@ __device__ __forceinline__ uint64_t desc_sw64(uint32_t saddr, uint32_t lbo_bytes
          (uint64_t(512 >> 4) << 32) | (uint64_t(1) << 46) | (uint64_t(4) << 61);
 }
 
-__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-}
-__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
 // Warp-uniform bounded wait: the whole warp continues only if every lane saw the phase.
 __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, unsigned int *status, unsigned code) {
   return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, status, code));
@@ -116,14 +106,14 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBarOff);
   uint64_t *q_full = bars + 0;
-  uint64_t *st_full = bars + 1;   // [2] K, V, bias of a key tile landed
-  uint64_t *st_empty = bars + 3;  // [2] P.V of that tile completed (K, V, bias, P reusable)
-  uint64_t *s_full = bars + 5;    // [2] S tile in TMEM
-  uint64_t *s_empty = bars + 7;   // [2] S tile read by the softmax warps
-  uint64_t *p_full = bars + 9;    // [2] P tile written (and O rescaled if needed)
-  uint64_t *o_full = bars + 11;   // all P.V done
-  uint64_t *q_ready = bars + 12;  // Q scaled in place by the softmax warps
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 13);
+  uint64_t *q_ready = bars + 1;              // Q scaled in place by the softmax warps
+  uint64_t *st_full = bars + 2;              // [kStages] K, V, bias of a key tile landed
+  uint64_t *st_empty = bars + 2 + kStages;   // [kStages] P.V of that tile completed
+  uint64_t *s_full = bars + 2 + 2 * kStages; // [2] S tile in TMEM
+  uint64_t *p_full = s_full + 2;             // [2] P tile in TMEM (and O rescaled if needed)
+  uint64_t *pv_done = p_full + 2;            // [2] P.V reading TMEM buffer b completed
+  uint64_t *o_full = pv_done + 2;            // all P.V done
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(o_full + 1);
   int *tile_masked = reinterpret_cast<int *>(smem + kFlagOff);
   __nv_bfloat16 *mask_bias = reinterpret_cast<__nv_bfloat16 *>(smem + kMaskOff);
 
@@ -137,23 +127,22 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (tid < kMaxTiles) tile_masked[tid] = 0;
   if (tid == 0) {
     tc::mbar_init(q_full, 1);
+    tc::mbar_init(q_ready, 4);
+    for (int s = 0; s < kStages; ++s) {
+      tc::mbar_init(&st_full[s], 1);
+      tc::mbar_init(&st_empty[s], 1);
+    }
     for (int b = 0; b < 2; ++b) {
-      tc::mbar_init(&st_full[b], 1);
-      tc::mbar_init(&st_empty[b], 1);
       tc::mbar_init(&s_full[b], 1);
-      tc::mbar_init(&s_empty[b], 4);
       tc::mbar_init(&p_full[b], 4);
+      tc::mbar_init(&pv_done[b], 1);
     }
     tc::mbar_init(o_full, 1);
-    tc::mbar_init(q_ready, 4);
     tc::fence_mbar_init();
   }
-  // Ones block after each V tile (its swizzle is irrelevant: every element is 1).
-  for (int i = tid; i < 2 * 4096 / 16; i += kThreads) {
-    const int b = i / 256, off = (i % 256) * 16;
-    *reinterpret_cast<uint4 *>(smem + kVOff + b * kVStride + kOnesOff + off) =
-        make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
-  }
+  // Ones block read as V's second N block (its swizzle is irrelevant: every element is 1).
+  for (int i = tid; i < kVBytes / 16; i += kThreads)
+    *reinterpret_cast<uint4 *>(smem + kOnesOff + i * 16) = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
   if (warp == 1) {
     tc::tmem_alloc(tmem_slot, kTmemCols);
     tc::tmem_relinquish();
@@ -183,12 +172,13 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc::mbar_arrive_expect_tx(q_full, kBQ * kD * 2);
       tc::tma_load_3d(smem + kQOff, &map_q, q_full, h * kD, q0, outer);
       for (int j = 0; j < n_tiles; ++j) {
-        const int b = j & 1;
-        if (!tc::mbar_wait(&st_empty[b], ((j >> 1) & 1) ^ 1u, args.status, 0x201)) break;
-        tc::mbar_arrive_expect_tx(&st_full[b], kStageTx);
-        tc::tma_load_3d(smem + kKOff + b * 4096, &map_k, &st_full[b], h * kD, j * kBK, outer);
-        tc::tma_load_3d(smem + kVOff + b * kVStride, &map_v, &st_full[b], h * kD, j * kBK, outer);
-        tc::tma_load_3d(smem + kBiasOff + b * 16384, &map_bias, &st_full[b], j * kBK, q0, h);
+        const int s = j % kStages;
+        if (!tc::mbar_wait(&st_empty[s], ((j / kStages) & 1) ^ 1u, args.status, 0x201)) break;
+        uint8_t *stage = smem + kStageOff + s * kStageBytes;
+        tc::mbar_arrive_expect_tx(&st_full[s], kStageBytes);
+        tc::tma_load_3d(stage, &map_k, &st_full[s], h * kD, j * kBK, outer);
+        tc::tma_load_3d(stage + kKBytes, &map_v, &st_full[s], h * kD, j * kBK, outer);
+        tc::tma_load_3d(stage + kKBytes + kVBytes, &map_bias, &st_full[s], j * kBK, q0, h);
       }
     }
   } else if (warp == 1) {
@@ -197,13 +187,15 @@ __global__ void __launch_bounds__(kThreads, 2)
       constexpr uint32_t idesc_s = tc::idesc_bf16(128, kBK, false, false);
       constexpr uint32_t idesc_pv = tc::idesc_bf16(128, 48, false, true);
       const uint32_t q_addr = tc::smem_u32(smem + kQOff);
+      const uint32_t ones_addr = tc::smem_u32(smem + kOnesOff);
       bool ok = tc::mbar_wait(q_ready, 0, args.status, 0x202);
       auto issue_s = [&](int j) {
-        const int b = j & 1;
-        if (!tc::mbar_wait(&st_full[b], (j >> 1) & 1, args.status, 0x203)) return false;
-        if (!tc::mbar_wait(&s_empty[b], ((j >> 1) & 1) ^ 1u, args.status, 0x204)) return false;
+        const int s = j % kStages, b = j & 1;
+        if (!tc::mbar_wait(&st_full[s], (j / kStages) & 1, args.status, 0x203)) return false;
+        // TMEM buffer b still holds P_{j-2}: its P.V must have finished reading it.
+        if (j >= 2 && !tc::mbar_wait(&pv_done[b], ((j - 2) >> 1) & 1, args.status, 0x204)) return false;
         tc::tc_fence_after();
-        const uint32_t k_addr = tc::smem_u32(smem + kKOff + b * 4096);
+        const uint32_t k_addr = tc::smem_u32(smem + kStageOff + s * kStageBytes);
 #pragma unroll
         for (int kk = 0; kk < 2; ++kk)
           tc::umma_f16_ss(tmem + uint32_t(b * kBK), desc_sw64(q_addr + kk * 32, 16), desc_sw64(k_addr + kk * 32, 16),
@@ -214,16 +206,17 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (ok) ok = issue_s(0);
       for (int j = 0; j < n_tiles && ok; ++j) {
         if (j + 1 < n_tiles && !issue_s(j + 1)) break;
-        const int b = j & 1;
+        const int s = j % kStages, b = j & 1;
         if (!tc::mbar_wait(&p_full[b], (j >> 1) & 1, args.status, 0x205)) break;
         tc::tc_fence_after();
-        const uint32_t p_addr = tc::smem_u32(smem + kPOff + b * 16384);
-        const uint32_t v_addr = tc::smem_u32(smem + kVOff + b * kVStride);
+        const uint32_t v_addr = tc::smem_u32(smem + kStageOff + s * kStageBytes + kKBytes);
+        const uint32_t lbo = ones_addr - v_addr;
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)
-          tc::umma_f16_ss(tmem + kOCol, tc::desc_sw128(p_addr + kk * 32, 16), desc_sw64(v_addr + kk * 1024, kOnesOff),
-                          idesc_pv, (j | kk) != 0);
-        tc::umma_commit(&st_empty[b]);
+          tc::umma_f16_ts(tmem + kOCol, tmem + uint32_t(b * kBK + kk * 8), desc_sw64(v_addr + kk * 1024, lbo), idesc_pv,
+                          (j | kk) != 0);
+        tc::umma_commit(&st_empty[s]);
+        tc::umma_commit(&pv_done[b]);
         if (j + 1 == n_tiles) tc::umma_commit(o_full);
       }
     }
@@ -253,25 +246,20 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (lane == 0) tc::mbar_arrive(q_ready);
     }
     for (int j = 0; j < n_tiles && ok; ++j) {
-      const int b = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      if (!(ok = warp_wait(&s_full[b], ph, args.status, 0x206))) break;
+      const int s = j % kStages, b = j & 1;
+      if (!(ok = warp_wait(&s_full[b], (j >> 1) & 1, args.status, 0x206))) break;
       tc::tc_fence_after();
-      uint32_t s[64];
-      tc::tmem_ld_32x32b_x32(lane_base + b * kBK, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-      tc::tmem_ld_32x32b_x32(lane_base + b * kBK + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+      uint32_t sv[64];
+      tc::tmem_ld_32x32b_x32(lane_base + b * kBK, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+      tc::tmem_ld_32x32b_x32(lane_base + b * kBK + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+      if (!(ok = warp_wait(&st_full[s], (j / kStages) & 1, args.status, 0x207))) break;
       tc::tmem_ld_wait();
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&s_empty[b]);
-      if (!(ok = warp_wait(&st_full[b], ph, args.status, 0x207))) break;
 
       // Ordered rounding: t = bf16(bf16(bf16(s) + mask) + bias), packed per key pair.
       const int k0 = j * kBK;
-      const uint8_t *bias_row = smem + kBiasOff + b * 16384 + row * 128;
+      const uint8_t *bias_row = smem + kStageOff + s * kStageBytes + kKBytes + kVBytes + row * 128;
       const bool masked = tile_masked[j] != 0;
       uint32_t t[32];
-      uint32_t tmax = kNegInf;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {  // 16-byte chunk c = keys 8c .. 8c + 7
         const uint4 bv = *reinterpret_cast<const uint4 *>(bias_row + ((c ^ (row & 7)) << 4));
@@ -279,10 +267,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int pr = c * 4 + e;
-          uint32_t x = cvt_bf16x2(__uint_as_float(s[2 * pr]), __uint_as_float(s[2 * pr + 1]));
+          uint32_t x = cvt_bf16x2(__uint_as_float(sv[2 * pr]), __uint_as_float(sv[2 * pr + 1]));
           if (masked) x = add_bf16x2(x, *reinterpret_cast<const uint32_t *>(mask_bias + k0 + 2 * pr));
-          x = add_bf16x2(x, bw[e]);
-          t[pr] = x;
+          t[pr] = add_bf16x2(x, bw[e]);
         }
       }
       if (k0 + kBK > n) {  // keys past n contribute nothing
@@ -293,17 +280,19 @@ __global__ void __launch_bounds__(kThreads, 2)
           t[pr] = (t[pr] & keep) | (kNegPad & ~keep);
         }
       }
+      uint32_t mx[4] = {t[0], t[1], t[2], t[3]};
 #pragma unroll
-      for (int pr = 0; pr < 32; ++pr) tmax = max_bf16x2(tmax, t[pr]);
+      for (int pr = 4; pr < 32; ++pr) mx[pr & 3] = max_bf16x2(mx[pr & 3], t[pr]);
+      const uint32_t tmax = max_bf16x2(max_bf16x2(mx[0], mx[1]), max_bf16x2(mx[2], mx[3]));
       const float m_tile = fmaxf(bf16_lo(tmax), bf16_hi(tmax));
 
       // Reference maximum: set on the first tile; raised (with O rescaled)
       // only when this tile's maximum exceeds it by more than 2^8 in exp2.
-      const bool first = m_ref == -INFINITY;
+      const bool first = j == 0;
       const bool grow = !first && (m_tile - m_ref) * kLog2e > kRescaleLog2;
       if (__any_sync(0xffffffffu, grow)) {
         // O holds tiles < j: wait for the P.V of tile j - 1, then scale in place.
-        if (!(ok = warp_wait(&st_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, args.status, 0x208))) break;
+        if (!(ok = warp_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, args.status, 0x208))) break;
         tc::tc_fence_after();
         const float alpha = grow ? fast_exp2((m_ref - m_tile) * kLog2e) : 1.f;
         uint32_t o[32], l16[16];
@@ -314,28 +303,21 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
 #pragma unroll
         for (int i = 0; i < 16; ++i) l16[i] = __float_as_uint(__uint_as_float(l16[i]) * alpha);
-        tmem_st_32x32b_x16(lane_base + kOCol, *reinterpret_cast<const uint32_t(*)[16]>(&o[0]));
-        tmem_st_32x32b_x16(lane_base + kOCol + 16, *reinterpret_cast<const uint32_t(*)[16]>(&o[16]));
-        tmem_st_32x32b_x16(lane_base + kOCol + 32, l16);
-        tmem_st_wait();
+        tc::tmem_st_32x32b_x16(lane_base + kOCol, *reinterpret_cast<const uint32_t(*)[16]>(&o[0]));
+        tc::tmem_st_32x32b_x16(lane_base + kOCol + 16, *reinterpret_cast<const uint32_t(*)[16]>(&o[16]));
+        tc::tmem_st_32x32b_x16(lane_base + kOCol + 32, l16);
       }
       if (first || grow) m_ref = m_tile;
       const float ml = m_ref * kLog2e;
 
-      // P buffer b was last read by the P.V of tile j - 2.
-      if (!(ok = warp_wait(&st_empty[b], ph ^ 1u, args.status, 0x209))) break;
-      uint8_t *p_row = smem + kPOff + b * 16384 + row * 128;
+      // P (bf16x2 per key pair) over the first 32 columns of this S buffer.
+      uint32_t p[32];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint32_t x = t[c * 4 + e];
-          w[e] = cvt_bf16x2(fast_exp2(fmaf(bf16_lo(x), kLog2e, -ml)), fast_exp2(fmaf(bf16_hi(x), kLog2e, -ml)));
-        }
-        *reinterpret_cast<uint4 *>(p_row + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-      tc::fence_proxy_async_smem();
+      for (int pr = 0; pr < 32; ++pr)
+        p[pr] = cvt_bf16x2(fast_exp2(fmaf(bf16_lo(t[pr]), kLog2e, -ml)), fast_exp2(fmaf(bf16_hi(t[pr]), kLog2e, -ml)));
+      tc::tmem_st_32x32b_x16(lane_base + b * kBK, *reinterpret_cast<const uint32_t(*)[16]>(&p[0]));
+      tc::tmem_st_32x32b_x16(lane_base + b * kBK + 16, *reinterpret_cast<const uint32_t(*)[16]>(&p[16]));
+      tc::tmem_st_wait();
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&p_full[b]);
