@@ -4,8 +4,9 @@
 // bf16 rounding points, fused sigmoid output gate, strides for the ending
 // node), restructured for Blackwell:
 //   * S = Q K^T for a 64-key tile is one pair of tcgen05.mma (M = 128 queries,
-//     N = 64 keys, K = 32) into TMEM, double-buffered so the MMA of tile j+1
-//     runs while the softmax of tile j is in progress;
+//     N = 64 keys, K = 32) into TMEM, triple-buffered: the MMA of tile j+2 is
+//     issued while the softmax of tile j runs, so the MMA latency of
+//     P.V(j-1) -> S(j+2) hides behind two softmax tiles;
 //   * one softmax thread per query row reads its 64 scores with two
 //     tcgen05.ld, applies the ordered rounding (bf16 score -> + mask -> + bias)
 //     on packed bf16x2, and computes P = exp2(t log2 e - m log2 e) (fp32 MUFU,
@@ -47,9 +48,10 @@ constexpr int kBarOff = kOnesOff + kVBytes;
 constexpr int kFlagOff = kBarOff + 256;         // per-key-tile "has masked keys" flags
 constexpr int kMaskOff = kFlagOff + kMaxTiles * 4;
 
-// TMEM columns: S/P[0] 0..63, S/P[1] 64..127, O|l 128..175.
+// TMEM columns: S/P[b] at 64 b (b = 0..2), O|l 192..239.
+constexpr int kSBufs = 3;
 constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kOCol = 128;
+constexpr uint32_t kOCol = 192;
 
 constexpr uint32_t kNegInf = 0xFF80FF80u;
 constexpr uint32_t kNegPad = 0xF14AF14Au;  // bf16x2 (-1e30, -1e30): finite, exp2 -> 0
@@ -109,10 +111,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t *q_ready = bars + 1;              // Q scaled in place by the softmax warps
   uint64_t *st_full = bars + 2;              // [kStages] K, V, bias of a key tile landed
   uint64_t *st_empty = bars + 2 + kStages;   // [kStages] P.V of that tile completed
-  uint64_t *s_full = bars + 2 + 2 * kStages; // [2] S tile in TMEM
-  uint64_t *p_full = s_full + 2;             // [2] P tile in TMEM (and O rescaled if needed)
-  uint64_t *pv_done = p_full + 2;            // [2] P.V reading TMEM buffer b completed
-  uint64_t *o_full = pv_done + 2;            // all P.V done
+  uint64_t *s_full = bars + 2 + 2 * kStages; // [kSBufs] S tile in TMEM
+  uint64_t *p_full = s_full + kSBufs;        // [kSBufs] P tile in TMEM (and O rescaled if needed)
+  uint64_t *pv_done = p_full + kSBufs;       // [kSBufs] P.V reading TMEM buffer b completed
+  uint64_t *o_full = pv_done + kSBufs;       // all P.V done
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(o_full + 1);
   int *tile_masked = reinterpret_cast<int *>(smem + kFlagOff);
   __nv_bfloat16 *mask_bias = reinterpret_cast<__nv_bfloat16 *>(smem + kMaskOff);
@@ -132,7 +134,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc::mbar_init(&st_full[s], 1);
       tc::mbar_init(&st_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kSBufs; ++b) {
       tc::mbar_init(&s_full[b], 1);
       tc::mbar_init(&p_full[b], 4);
       tc::mbar_init(&pv_done[b], 1);
@@ -148,6 +150,31 @@ __global__ void __launch_bounds__(kThreads, 2)
     tc::tmem_relinquish();
   }
   __syncthreads();
+  // Start the Q load and fill the ring before the mask pass so the TMA
+  // latency overlaps it.
+  const int prefilled = n_tiles < kStages ? n_tiles : kStages;
+  if (tid == 0) {
+    tc::prefetch_tmap(&map_q);
+    tc::prefetch_tmap(&map_k);
+    tc::prefetch_tmap(&map_v);
+    tc::prefetch_tmap(&map_bias);
+    tc::mbar_arrive_expect_tx(q_full, kBQ * kD * 2);
+    tc::tma_load_3d(smem + kQOff, &map_q, q_full, h * kD, q0, outer);
+    for (int j = 0; j < prefilled; ++j) {
+      uint8_t *stage = smem + kStageOff + j * kStageBytes;
+      tc::mbar_arrive_expect_tx(&st_full[j], kStageBytes);
+      tc::tma_load_3d(stage, &map_k, &st_full[j], h * kD, j * kBK, outer);
+      tc::tma_load_3d(stage + kKBytes, &map_v, &st_full[j], h * kD, j * kBK, outer);
+      tc::tma_load_3d(stage + kKBytes + kVBytes, &map_bias, &st_full[j], j * kBK, q0, h);
+    }
+  }
+  if (warp >= 2) {
+    // The gate row is read in the epilogue; start bringing it into L2 now.
+    const int qi = q0 + (warp & 3) * 32 + lane;
+    if (qi < n)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(args.g + (int64_t(outer) * args.so + int64_t(qi) * args.si) *
+                                                                  args.ld + h * kD));
+  }
   // Mask bias of this outer row (bf16; for mask in {0, 1} adding it rounds
   // exactly like the fp32 value) and per-tile "any key masked" flags.
   for (int key = tid; key < n_tiles * kBK; key += kThreads) {
@@ -165,13 +192,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      tc::prefetch_tmap(&map_q);
-      tc::prefetch_tmap(&map_k);
-      tc::prefetch_tmap(&map_v);
-      tc::prefetch_tmap(&map_bias);
-      tc::mbar_arrive_expect_tx(q_full, kBQ * kD * 2);
-      tc::tma_load_3d(smem + kQOff, &map_q, q_full, h * kD, q0, outer);
-      for (int j = 0; j < n_tiles; ++j) {
+      for (int j = prefilled; j < n_tiles; ++j) {
         const int s = j % kStages;
         if (!tc::mbar_wait(&st_empty[s], ((j / kStages) & 1) ^ 1u, args.status, 0x201)) break;
         uint8_t *stage = smem + kStageOff + s * kStageBytes;
@@ -190,10 +211,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t ones_addr = tc::smem_u32(smem + kOnesOff);
       bool ok = tc::mbar_wait(q_ready, 0, args.status, 0x202);
       auto issue_s = [&](int j) {
-        const int s = j % kStages, b = j & 1;
+        const int s = j % kStages, b = j % kSBufs;
         if (!tc::mbar_wait(&st_full[s], (j / kStages) & 1, args.status, 0x203)) return false;
-        // TMEM buffer b still holds P_{j-2}: its P.V must have finished reading it.
-        if (j >= 2 && !tc::mbar_wait(&pv_done[b], ((j - 2) >> 1) & 1, args.status, 0x204)) return false;
+        // TMEM buffer b still holds P of tile j - kSBufs: its P.V must have finished reading it.
+        if (j >= kSBufs && !tc::mbar_wait(&pv_done[b], ((j - kSBufs) / kSBufs) & 1, args.status, 0x204))
+          return false;
         tc::tc_fence_after();
         const uint32_t k_addr = tc::smem_u32(smem + kStageOff + s * kStageBytes);
 #pragma unroll
@@ -203,11 +225,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         tc::umma_commit(&s_full[b]);
         return true;
       };
-      if (ok) ok = issue_s(0);
+      for (int j = 0; j < kSBufs - 1 && j < n_tiles && ok; ++j) ok = issue_s(j);
       for (int j = 0; j < n_tiles && ok; ++j) {
-        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
-        const int s = j % kStages, b = j & 1;
-        if (!tc::mbar_wait(&p_full[b], (j >> 1) & 1, args.status, 0x205)) break;
+        if (j + kSBufs - 1 < n_tiles && !issue_s(j + kSBufs - 1)) break;
+        const int s = j % kStages, b = j % kSBufs;
+        if (!tc::mbar_wait(&p_full[b], (j / kSBufs) & 1, args.status, 0x205)) break;
         tc::tc_fence_after();
         const uint32_t v_addr = tc::smem_u32(smem + kStageOff + s * kStageBytes + kKBytes);
         const uint32_t lbo = ones_addr - v_addr;
@@ -246,8 +268,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (lane == 0) tc::mbar_arrive(q_ready);
     }
     for (int j = 0; j < n_tiles && ok; ++j) {
-      const int s = j % kStages, b = j & 1;
-      if (!(ok = warp_wait(&s_full[b], (j >> 1) & 1, args.status, 0x206))) break;
+      const int s = j % kStages, b = j % kSBufs;
+      if (!(ok = warp_wait(&s_full[b], (j / kSBufs) & 1, args.status, 0x206))) break;
       tc::tc_fence_after();
       uint32_t sv[64];
       tc::tmem_ld_32x32b_x32(lane_base + b * kBK, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
@@ -292,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const bool grow = !first && (m_tile - m_ref) * kLog2e > kRescaleLog2;
       if (__any_sync(0xffffffffu, grow)) {
         // O holds tiles < j: wait for the P.V of tile j - 1, then scale in place.
-        if (!(ok = warp_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, args.status, 0x208))) break;
+        if (!(ok = warp_wait(&pv_done[(j - 1) % kSBufs], ((j - 1) / kSBufs) & 1, args.status, 0x208))) break;
         tc::tc_fence_after();
         const float alpha = grow ? fast_exp2((m_ref - m_tile) * kLog2e) : 1.f;
         uint32_t o[32], l16[16];
