@@ -4,23 +4,26 @@
 // bf16 rounding points, fused sigmoid output gate, strides for the ending
 // node), restructured for Blackwell:
 //   * S = Q K^T for a 64-key tile is one pair of tcgen05.mma (M = 128 queries,
-//     N = 64 keys, K = 32) into TMEM, triple-buffered: the MMA of tile j+2 is
-//     issued while the softmax of tile j runs, so the MMA latency of
-//     P.V(j-1) -> S(j+2) hides behind two softmax tiles;
-//   * one softmax thread per query row reads its 64 scores with two
+//     N = 64 keys, K = 32) into TMEM, double-buffered so the MMA of tile j+1
+//     runs while the softmax of tile j is in progress;
+//   * each query row is handled by two softmax threads (keys 0..31 and 32..63
+//     of every tile, TMEM lane = row).  A thread reads its 32 scores with one
 //     tcgen05.ld, applies the ordered rounding (bf16 score -> + mask -> + bias)
-//     on packed bf16x2, and computes P = exp2(t log2 e - m log2 e) (fp32 MUFU,
-//     rounded to bf16) -- no cross-thread reductions at all;
-//   * P goes back into TMEM over the columns its S tile occupied, and
-//     O += P V is a tcgen05.mma with A = P from TMEM and B = V in its natural
-//     [key][d] layout read MN-major; a constant block of ones appended to V
-//     makes the same MMA produce the row sums of the bf16 P in column 32;
-//   * O lives in TMEM and is rescaled (tcgen05.ld/st) only when a row maximum
-//     grows by more than 2^8, so P stays <= 256 and rescales are rare;
+//     on packed bf16x2 and computes P = exp2(t log2 e - m log2 e) (fp32 MUFU,
+//     rounded to bf16).  The two halves keep separate running maxima and
+//     separate O / row-sum accumulators, so they never synchronise per tile;
+//     the epilogue merges them (flash-decoding style split of the key axis);
+//   * P goes back into TMEM over the columns its S half occupied, and
+//     O_h += P_h V_h is a tcgen05.mma with A = P from TMEM and B = V in its
+//     natural [key][d] layout read MN-major; a constant block of ones appended
+//     to V makes the same MMA produce the row sums of the bf16 P (column 32);
+//   * O_h is rescaled (tcgen05.ld/st) only when its maximum grows by more than
+//     2^8, so P stays <= 256 and rescales are rare;
 //   * Q, K, V and the bias tiles arrive by TMA through a 4-deep ring (3-D
 //     maps carry the starting/ending-node strides); no multicast.
 // Warp roles: warp 0 TMA producer, warp 1 TMEM allocation + MMA issue, warps
-// 2..5 softmax and epilogue (TMEM lane quarter = warp % 4, one row per thread).
+// 2..9 softmax and epilogue (TMEM lane quarter = warp % 4; warps 2..5 take key
+// half 0, warps 6..9 key half 1).
 #include "tc.cuh"
 
 namespace bl {
@@ -31,7 +34,8 @@ constexpr int kBQ = 128;
 constexpr int kBK = 64;
 constexpr int kHeads = 4;
 constexpr int kMaxTiles = 64;  // n <= 4096
-constexpr int kThreads = 192;
+constexpr int kSoftmaxWarps = 8;
+constexpr int kThreads = (2 + kSoftmaxWarps) * 32;
 constexpr int kStages = 4;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.f;  // keep P = exp2(x - ref) <= 2^8 before rescaling O
@@ -45,16 +49,18 @@ constexpr int kBiasBytes = kBQ * kBK * 2;       // bias [128][64] bf16, 128B-swi
 constexpr int kStageBytes = kKBytes + kVBytes + kBiasBytes;
 constexpr int kOnesOff = kStageOff + kStages * kStageBytes;  // [64][32] ones (V's extra N block)
 constexpr int kBarOff = kOnesOff + kVBytes;
-constexpr int kFlagOff = kBarOff + 256;         // per-key-tile "has masked keys" flags
+constexpr int kMaxOff = kBarOff + 256;          // per-half row maxima exchanged in the epilogue
+constexpr int kFlagOff = kMaxOff + 2 * kBQ * 4; // per-key-tile "has masked keys" flags
 constexpr int kMaskOff = kFlagOff + kMaxTiles * 4;
 
-// TMEM columns: S/P[b] at 64 b (b = 0..2), O|l 192..239.
-constexpr int kSBufs = 3;
+// TMEM columns: S/P[b] at 64 b (b = 0, 1; key half h at +32 h),
+// O_h | l_h at 128 + 48 h (32 output columns + 16 row-sum columns).
 constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kOCol = 192;
+constexpr uint32_t kOCol = 128;
+constexpr uint32_t kOStride = 48;
 
 constexpr uint32_t kNegInf = 0xFF80FF80u;
-constexpr uint32_t kNegPad = 0xF14AF14Au;  // bf16x2 (-1e30, -1e30): finite, exp2 -> 0
+constexpr uint32_t kNegPad = 0xF14AF14Au;  // bf16x2 (-1e30, -1e30)
 
 struct TcArgs {
   const __nv_bfloat16 *g;
@@ -111,11 +117,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t *q_ready = bars + 1;              // Q scaled in place by the softmax warps
   uint64_t *st_full = bars + 2;              // [kStages] K, V, bias of a key tile landed
   uint64_t *st_empty = bars + 2 + kStages;   // [kStages] P.V of that tile completed
-  uint64_t *s_full = bars + 2 + 2 * kStages; // [kSBufs] S tile in TMEM
-  uint64_t *p_full = s_full + kSBufs;        // [kSBufs] P tile in TMEM (and O rescaled if needed)
-  uint64_t *pv_done = p_full + kSBufs;       // [kSBufs] P.V reading TMEM buffer b completed
-  uint64_t *o_full = pv_done + kSBufs;       // all P.V done
+  uint64_t *s_full = bars + 2 + 2 * kStages; // [2] S tile in TMEM
+  uint64_t *p_full = s_full + 2;             // [2] P tile in TMEM (and O rescaled if needed)
+  uint64_t *pv_done = p_full + 2;            // [2] P.V reading TMEM buffer b completed
+  uint64_t *o_full = pv_done + 2;            // all P.V done
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(o_full + 1);
+  float *row_max = reinterpret_cast<float *>(smem + kMaxOff);
   int *tile_masked = reinterpret_cast<int *>(smem + kFlagOff);
   __nv_bfloat16 *mask_bias = reinterpret_cast<__nv_bfloat16 *>(smem + kMaskOff);
 
@@ -129,14 +136,14 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (tid < kMaxTiles) tile_masked[tid] = 0;
   if (tid == 0) {
     tc::mbar_init(q_full, 1);
-    tc::mbar_init(q_ready, 4);
+    tc::mbar_init(q_ready, kSoftmaxWarps);
     for (int s = 0; s < kStages; ++s) {
       tc::mbar_init(&st_full[s], 1);
       tc::mbar_init(&st_empty[s], 1);
     }
-    for (int b = 0; b < kSBufs; ++b) {
+    for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&s_full[b], 1);
-      tc::mbar_init(&p_full[b], 4);
+      tc::mbar_init(&p_full[b], kSoftmaxWarps);
       tc::mbar_init(&pv_done[b], 1);
     }
     tc::mbar_init(o_full, 1);
@@ -167,13 +174,6 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc::tma_load_3d(stage + kKBytes, &map_v, &st_full[j], h * kD, j * kBK, outer);
       tc::tma_load_3d(stage + kKBytes + kVBytes, &map_bias, &st_full[j], j * kBK, q0, h);
     }
-  }
-  if (warp >= 2) {
-    // The gate row is read in the epilogue; start bringing it into L2 now.
-    const int qi = q0 + (warp & 3) * 32 + lane;
-    if (qi < n)
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(args.g + (int64_t(outer) * args.so + int64_t(qi) * args.si) *
-                                                                  args.ld + h * kD));
   }
   // Mask bias of this outer row (bf16; for mask in {0, 1} adding it rounds
   // exactly like the fp32 value) and per-tile "any key masked" flags.
@@ -211,11 +211,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t ones_addr = tc::smem_u32(smem + kOnesOff);
       bool ok = tc::mbar_wait(q_ready, 0, args.status, 0x202);
       auto issue_s = [&](int j) {
-        const int s = j % kStages, b = j % kSBufs;
+        const int s = j % kStages, b = j & 1;
         if (!tc::mbar_wait(&st_full[s], (j / kStages) & 1, args.status, 0x203)) return false;
-        // TMEM buffer b still holds P of tile j - kSBufs: its P.V must have finished reading it.
-        if (j >= kSBufs && !tc::mbar_wait(&pv_done[b], ((j - kSBufs) / kSBufs) & 1, args.status, 0x204))
-          return false;
+        // TMEM buffer b still holds P of tile j - 2: its P.V must have finished reading it.
+        if (j >= 2 && !tc::mbar_wait(&pv_done[b], ((j - 2) >> 1) & 1, args.status, 0x204)) return false;
         tc::tc_fence_after();
         const uint32_t k_addr = tc::smem_u32(smem + kStageOff + s * kStageBytes);
 #pragma unroll
@@ -225,37 +224,41 @@ __global__ void __launch_bounds__(kThreads, 2)
         tc::umma_commit(&s_full[b]);
         return true;
       };
-      for (int j = 0; j < kSBufs - 1 && j < n_tiles && ok; ++j) ok = issue_s(j);
+      if (ok) ok = issue_s(0);
       for (int j = 0; j < n_tiles && ok; ++j) {
-        if (j + kSBufs - 1 < n_tiles && !issue_s(j + kSBufs - 1)) break;
-        const int s = j % kStages, b = j % kSBufs;
-        if (!tc::mbar_wait(&p_full[b], (j / kSBufs) & 1, args.status, 0x205)) break;
+        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
+        const int s = j % kStages, b = j & 1;
+        if (!tc::mbar_wait(&p_full[b], (j >> 1) & 1, args.status, 0x205)) break;
         tc::tc_fence_after();
         const uint32_t v_addr = tc::smem_u32(smem + kStageOff + s * kStageBytes + kKBytes);
         const uint32_t lbo = ones_addr - v_addr;
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk)
-          tc::umma_f16_ts(tmem + kOCol, tmem + uint32_t(b * kBK + kk * 8), desc_sw64(v_addr + kk * 1024, lbo), idesc_pv,
-                          (j | kk) != 0);
+        for (int half = 0; half < 2; ++half)
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk)
+            tc::umma_f16_ts(tmem + kOCol + half * kOStride, tmem + uint32_t(b * kBK + half * 32 + kk * 8),
+                            desc_sw64(v_addr + (half * 2 + kk) * 1024, lbo), idesc_pv, (j | kk) != 0);
         tc::umma_commit(&st_empty[s]);
         tc::umma_commit(&pv_done[b]);
         if (j + 1 == n_tiles) tc::umma_commit(o_full);
       }
     }
   } else {
-    // ---------------- softmax + epilogue: one query row per thread ----------------
+    // ---------------- softmax + epilogue: half a query row per thread ----------------
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
-    float m_ref = -INFINITY;  // reference maximum of the exponentials of this row
+    const uint32_t o_base = lane_base + kOCol + half * kOStride;
+    float m_ref = -INFINITY;  // reference maximum of this half-row's exponentials
     // Upstream divides q by sqrt(d) after the projection and rounds to bf16
-    // (_prep_qkv(apply_scale=True), triangle.py:80): apply that to this
-    // thread's Q row in place (the 64-byte swizzle keeps a row in its 64 bytes).
+    // (_prep_qkv(apply_scale=True), triangle.py:80): apply it to this thread's
+    // half of its Q row in place (elementwise, so the swizzle does not matter).
     bool ok = warp_wait(q_full, 0, args.status, 0x20B);
     if (ok) {
-      uint4 *q_row = reinterpret_cast<uint4 *>(smem + kQOff + row * 64);
+      uint4 *q_row = reinterpret_cast<uint4 *>(smem + kQOff + row * 64) + half * 2;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint4 v = q_row[c];
         uint32_t *w = &v.x;
 #pragma unroll
@@ -268,23 +271,23 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (lane == 0) tc::mbar_arrive(q_ready);
     }
     for (int j = 0; j < n_tiles && ok; ++j) {
-      const int s = j % kStages, b = j % kSBufs;
-      if (!(ok = warp_wait(&s_full[b], (j / kSBufs) & 1, args.status, 0x206))) break;
+      const int s = j % kStages, b = j & 1;
+      if (!(ok = warp_wait(&s_full[b], (j >> 1) & 1, args.status, 0x206))) break;
       tc::tc_fence_after();
-      uint32_t sv[64];
-      tc::tmem_ld_32x32b_x32(lane_base + b * kBK, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-      tc::tmem_ld_32x32b_x32(lane_base + b * kBK + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+      uint32_t sv[32];
+      tc::tmem_ld_32x32b_x32(lane_base + b * kBK + half * 32, sv);
       if (!(ok = warp_wait(&st_full[s], (j / kStages) & 1, args.status, 0x207))) break;
       tc::tmem_ld_wait();
 
       // Ordered rounding: t = bf16(bf16(bf16(s) + mask) + bias), packed per key pair.
-      const int k0 = j * kBK;
+      const int k0 = j * kBK + half * 32;
       const uint8_t *bias_row = smem + kStageOff + s * kStageBytes + kKBytes + kVBytes + row * 128;
       const bool masked = tile_masked[j] != 0;
-      uint32_t t[32];
+      uint32_t t[16];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {  // 16-byte chunk c = keys 8c .. 8c + 7
-        const uint4 bv = *reinterpret_cast<const uint4 *>(bias_row + ((c ^ (row & 7)) << 4));
+      for (int c = 0; c < 4; ++c) {  // 16-byte chunk = keys 8c .. 8c + 7 of this half
+        const int chunk = half * 4 + c;
+        const uint4 bv = *reinterpret_cast<const uint4 *>(bias_row + ((chunk ^ (row & 7)) << 4));
         const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -294,9 +297,11 @@ __global__ void __launch_bounds__(kThreads, 2)
           t[pr] = add_bf16x2(x, bw[e]);
         }
       }
-      if (k0 + kBK > n) {  // keys past n contribute nothing
+      // Keys past n: excluded from the maximum here and zeroed in P below.
+      const bool tail = k0 + 32 > n;
+      if (tail) {
 #pragma unroll
-        for (int pr = 0; pr < 32; ++pr) {
+        for (int pr = 0; pr < 16; ++pr) {
           const int key = k0 + 2 * pr;
           const uint32_t keep = (key < n ? 0x0000ffffu : 0u) | (key + 1 < n ? 0xffff0000u : 0u);
           t[pr] = (t[pr] & keep) | (kNegPad & ~keep);
@@ -304,70 +309,86 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       uint32_t mx[4] = {t[0], t[1], t[2], t[3]};
 #pragma unroll
-      for (int pr = 4; pr < 32; ++pr) mx[pr & 3] = max_bf16x2(mx[pr & 3], t[pr]);
+      for (int pr = 4; pr < 16; ++pr) mx[pr & 3] = max_bf16x2(mx[pr & 3], t[pr]);
       const uint32_t tmax = max_bf16x2(max_bf16x2(mx[0], mx[1]), max_bf16x2(mx[2], mx[3]));
       const float m_tile = fmaxf(bf16_lo(tmax), bf16_hi(tmax));
 
-      // Reference maximum: set on the first tile; raised (with O rescaled)
+      // Reference maximum: set on the first tile; raised (with O_h rescaled)
       // only when this tile's maximum exceeds it by more than 2^8 in exp2.
       const bool first = j == 0;
       const bool grow = !first && (m_tile - m_ref) * kLog2e > kRescaleLog2;
       if (__any_sync(0xffffffffu, grow)) {
-        // O holds tiles < j: wait for the P.V of tile j - 1, then scale in place.
-        if (!(ok = warp_wait(&pv_done[(j - 1) % kSBufs], ((j - 1) / kSBufs) & 1, args.status, 0x208))) break;
+        // O_h holds tiles < j: wait for the P.V of tile j - 1, then scale in place.
+        if (!(ok = warp_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, args.status, 0x208))) break;
         tc::tc_fence_after();
         const float alpha = grow ? fast_exp2((m_ref - m_tile) * kLog2e) : 1.f;
         uint32_t o[32], l16[16];
-        tc::tmem_ld_32x32b_x32(lane_base + kOCol, o);
-        tc::tmem_ld_32x32b_x16(lane_base + kOCol + 32, l16);
+        tc::tmem_ld_32x32b_x32(o_base, o);
+        tc::tmem_ld_32x32b_x16(o_base + 32, l16);
         tc::tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
 #pragma unroll
         for (int i = 0; i < 16; ++i) l16[i] = __float_as_uint(__uint_as_float(l16[i]) * alpha);
-        tc::tmem_st_32x32b_x16(lane_base + kOCol, *reinterpret_cast<const uint32_t(*)[16]>(&o[0]));
-        tc::tmem_st_32x32b_x16(lane_base + kOCol + 16, *reinterpret_cast<const uint32_t(*)[16]>(&o[16]));
-        tc::tmem_st_32x32b_x16(lane_base + kOCol + 32, l16);
+        tc::tmem_st_32x32b_x16(o_base, *reinterpret_cast<const uint32_t(*)[16]>(&o[0]));
+        tc::tmem_st_32x32b_x16(o_base + 16, *reinterpret_cast<const uint32_t(*)[16]>(&o[16]));
+        tc::tmem_st_32x32b_x16(o_base + 32, l16);
       }
       if (first || grow) m_ref = m_tile;
       const float ml = m_ref * kLog2e;
 
-      // P (bf16x2 per key pair) over the first 32 columns of this S buffer.
-      uint32_t p[32];
+      // P (bf16x2 per key pair) over the first 16 columns of this S half.
+      uint32_t p[16];
 #pragma unroll
-      for (int pr = 0; pr < 32; ++pr)
+      for (int pr = 0; pr < 16; ++pr)
         p[pr] = cvt_bf16x2(fast_exp2(fmaf(bf16_lo(t[pr]), kLog2e, -ml)), fast_exp2(fmaf(bf16_hi(t[pr]), kLog2e, -ml)));
-      tc::tmem_st_32x32b_x16(lane_base + b * kBK, *reinterpret_cast<const uint32_t(*)[16]>(&p[0]));
-      tc::tmem_st_32x32b_x16(lane_base + b * kBK + 16, *reinterpret_cast<const uint32_t(*)[16]>(&p[16]));
+      if (tail) {
+#pragma unroll
+        for (int pr = 0; pr < 16; ++pr) {
+          const int key = k0 + 2 * pr;
+          p[pr] &= (key < n ? 0x0000ffffu : 0u) | (key + 1 < n ? 0xffff0000u : 0u);
+        }
+      }
+      tc::tmem_st_32x32b_x16(lane_base + b * kBK + half * 32, p);
       tc::tmem_st_wait();
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&p_full[b]);
     }
-    // Epilogue: O / l, bf16, gate, store.
+    // Epilogue: merge the two key halves, O / l, bf16, gate, store.  This
+    // thread writes output channels 16 half .. 16 half + 15 of its row.
+    row_max[half * kBQ + row] = m_ref;
+    asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxWarps * 32) : "memory");
+    const float m_other = row_max[(half ^ 1) * kBQ + row];
     if (ok && warp_wait(o_full, 0, args.status, 0x20A)) {
       tc::tc_fence_after();
-      uint32_t o[32], l16[16];
-      tc::tmem_ld_32x32b_x32(lane_base + kOCol, o);
-      tc::tmem_ld_32x32b_x16(lane_base + kOCol + 32, l16);
+      const float m0 = half == 0 ? m_ref : m_other, m1 = half == 0 ? m_other : m_ref;
+      const float m = fmaxf(m0, m1);
+      const float a0 = fast_exp2((m0 - m) * kLog2e), a1 = fast_exp2((m1 - m) * kLog2e);
+      uint32_t o0[16], o1[16], l0[16], l1[16];
+      tc::tmem_ld_32x32b_x16(lane_base + kOCol + half * 16, o0);
+      tc::tmem_ld_32x32b_x16(lane_base + kOCol + kOStride + half * 16, o1);
+      tc::tmem_ld_32x32b_x16(lane_base + kOCol + 32, l0);
+      tc::tmem_ld_32x32b_x16(lane_base + kOCol + kOStride + 32, l1);
       tc::tmem_ld_wait();
       const int qi = q0 + row;
       if (qi < n) {
-        const float inv = 1.f / __uint_as_float(l16[0]);
+        const float inv = 1.f / (__uint_as_float(l0[0]) * a0 + __uint_as_float(l1[0]) * a1);
         const int64_t pair = int64_t(outer) * args.so + int64_t(qi) * args.si;
-        const uint4 *g4 = reinterpret_cast<const uint4 *>(args.g + pair * args.ld + h * kD);
-        uint4 *o4 = reinterpret_cast<uint4 *>(args.out + pair * args.out_ld + h * kD);
+        const uint4 *g4 = reinterpret_cast<const uint4 *>(args.g + pair * args.ld + h * kD + half * 16);
+        uint4 *o4 = reinterpret_cast<uint4 *>(args.out + pair * args.out_ld + h * kD + half * 16);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           const uint4 gv = g4[c];
           const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
           uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int d = c * 8 + e * 2;
-            const float o0 = bf16r(__uint_as_float(o[d]) * inv), o1 = bf16r(__uint_as_float(o[d + 1]) * inv);
+            const float v0 = (__uint_as_float(o0[d]) * a0 + __uint_as_float(o1[d]) * a1) * inv;
+            const float v1 = (__uint_as_float(o0[d + 1]) * a0 + __uint_as_float(o1[d + 1]) * a1) * inv;
             const float g0 = bf16r(sigmoidf_fast(bf16_lo(gw[e]))), g1 = bf16r(sigmoidf_fast(bf16_hi(gw[e])));
-            w[e] = pack_bf16x2(o0 * g0, o1 * g1);
+            w[e] = pack_bf16x2(bf16r(v0) * g0, bf16r(v1) * g1);
           }
           o4[c] = make_uint4(w[0], w[1], w[2], w[3]);
         }
