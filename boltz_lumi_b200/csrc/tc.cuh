@@ -58,6 +58,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return done != 0;
 }
 
+// Same, but a thread whose phase is not complete sleeps (up to `suspend_ns`)
+// until it completes instead of returning at once: waiting threads then do
+// not take issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t suspend_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(suspend_ns)
+      : "memory");
+  return done != 0;
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -76,8 +91,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsign
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   for (uint32_t spin = 1;; ++spin) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((spin & 255u) == 0) {
+    if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
+    if ((spin & 15u) == 0) {
       if (*reinterpret_cast<volatile unsigned int *>(status) != 0u) return false;
       if (global_timer_ns() - start > kWaitLimitNs) {
         atomicCAS(status, 0u, code);
