@@ -44,8 +44,6 @@ SIGNATURES = {
     "bl_triangle_bias_planes": [_p, c_int64, c_int64, c_int64, c_int, _p, c_int64, _p],
     "bl_triangle_attention": [_p, _p, _p, _p, c_int64, c_int64, c_int64, _p, c_int64, c_int64, _p, c_int64,
                               c_int64, c_float, c_int64, c_int64, c_int64, _p, c_int64, _p],
-    "bl_triangle_attention_tc": [_p, _p, _p, _p, c_int64, c_int64, c_int64, _p, c_int64, c_int64, _p, c_int64,
-                                 c_int64, c_float, c_int64, c_int64, c_int64, _p, c_int64, _p],
     "bl_pair_transition_static": [_p, c_int64, _p, _p, c_float, _p, _p, _p, _p],
 }
 _RESTYPES = {"bl_last_error": ctypes.c_char_p}

@@ -1,5 +1,4 @@
-// Flash triangle attention (starting and ending node) with the upstream bf16
-// rounding points and the fused sigmoid output gate.
+// Flash triangle attention on tcgen05 tensor cores (starting and ending node).
 //
 // For every outer row a of the pair tensor, head h and query b:
 //   s(b, c) = bf16(q_s(a, b) . k(a, c))                    q_s = bf16(q / sqrt(d))
@@ -9,80 +8,79 @@
 // This is the reference's ordered_triangle_forward (triangle.py:32-104 and
 // kernels/triangle_softmax.py:90-113) plus upstream _wrap_up's gate, without
 // materialising the [I, H, N, N] scores.  The ending node is the same
-// computation on z transposed; the caller expresses it through row strides
-// (pair row of (outer, inner) = outer * so + inner * si) and a transposed bias
-// plane, so no transposed copy of z or of q/k/v is made.
-//
-// Cost model: head dim 32 makes the core exp/issue-bound (N^3 H exponentials
-// at 16 MUFU ops/clk/SM vs 4 N^3 H d flops), so the two small contractions
-// stay on mma.sync m16n8k16 and the per-score work is kept minimal:
-//   cvt.rn.bf16x2 (s) -> add.bf16x2 (mask; skipped on key tiles without
-//   masked keys) -> add.bf16x2 (bias, loaded with ldmatrix in fragment
-//   layout) -> max.bf16x2 -> one fp32 FFMA + MUFU.EX2 per score -> cvt = P
-// (measured on B200: packed ex2.bf16x2 costs two MUFU ops, so the exponent
-// runs in fp32, which also keeps t*log2(e) exact).  P feeds the P.V mma
-// directly and the row sums come from one extra mma against a ones fragment.
-#include "common.cuh"
+// computation on z transposed, expressed through row strides and a
+// transposed bias plane.  Blackwell structure:
+//   * S = Q K^T for a 64-key tile is one pair of tcgen05.mma (M = 128 queries,
+//     N = 64 keys, K = 32) into TMEM, double-buffered so the MMA of tile j+1
+//     runs while the softmax of tile j is in progress;
+//   * each query row is handled by two softmax threads (keys 0..31 and 32..63
+//     of every tile, TMEM lane = row).  A thread reads its 32 scores with one
+//     tcgen05.ld, applies the ordered rounding (bf16 score -> + mask -> + bias)
+//     on packed bf16x2 and computes P = exp2(t log2 e - m log2 e) (fp32 MUFU,
+//     rounded to bf16).  The two halves keep separate running maxima and
+//     separate O / row-sum accumulators, so they never synchronise per tile;
+//     the epilogue merges them (flash-decoding style split of the key axis);
+//   * P goes back into TMEM over the columns its S half occupied, and
+//     O_h += P_h V_h is a tcgen05.mma with A = P from TMEM and B = V in its
+//     natural [key][d] layout read MN-major; a constant block of ones appended
+//     to V makes the same MMA produce the row sums of the bf16 P (column 32);
+//   * O_h is rescaled (tcgen05.ld/st) only when its maximum grows by more than
+//     2^8, so P stays <= 256 and rescales are rare;
+//   * Q, K, V and the bias tiles arrive by TMA through a 4-deep ring (3-D
+//     maps carry the starting/ending-node strides); no multicast.
+// Warp roles: warp 0 TMA producer, warp 1 TMEM allocation + MMA issue, warps
+// 2..9 softmax and epilogue (TMEM lane quarter = warp % 4; warps 2..5 take key
+// half 0, warps 6..9 key half 1).
+#include "tc.cuh"
 
 namespace bl {
 namespace {
 
 constexpr int kD = 32;
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
-constexpr int kBQ = kWarps * 16;  // 128 queries per CTA
-constexpr int kBK = 64;           // keys per tile
-constexpr int kBiasLd = kBK + 8;  // padded smem row (144 B): conflict-free fragment reads
-constexpr int kHeadsPerRow = 4;   // heads (grid.x = heads * query tiles)
-constexpr int kMaxTiles = 64;     // key tiles per row: n <= 4096
+constexpr int kBQ = 128;
+constexpr int kBK = 64;
+constexpr int kHeads = 4;
+constexpr int kMaxTiles = 64;  // n <= 4096
+constexpr int kSoftmaxWarps = 8;
+constexpr int kThreads = (2 + kSoftmaxWarps) * 32;
+constexpr int kStages = 4;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleLog2 = 8.f;  // keep P = exp2(x - ref) <= 2^8 before rescaling O
 
-struct FlashArgs {
-  const __nv_bfloat16 *q, *k, *v, *g;
-  int64_t ld;      // elements per pair row of q/k/v/g; head h at columns [h*32, h*32+32)
-  int64_t so, si;  // pair row of (outer, inner)
-  const __nv_bfloat16 *bias;  // bias(h, q, k) at bias + h*bias_hs + q*bias_ld + k
-  int64_t bias_ld, bias_hs;
-  const float *mask;  // mask(outer, key) at mask + outer*ms_o + key*ms_k
+// Shared memory layout (offsets from a 1024-byte aligned base).
+constexpr int kQOff = 0;                        // Q [128][32] bf16, 64B-swizzled              8 KB
+constexpr int kStageOff = 8192;                 // ring of {K, V, bias}
+constexpr int kKBytes = kBK * kD * 2;           // K [64][32] bf16, 64B-swizzled               4 KB
+constexpr int kVBytes = kBK * kD * 2;           // V [64][32] bf16, 64B-swizzled               4 KB
+constexpr int kBiasBytes = kBQ * kBK * 2;       // bias [128][64] bf16, 128B-swizzled         16 KB
+constexpr int kStageBytes = kKBytes + kVBytes + kBiasBytes;
+constexpr int kOnesOff = kStageOff + kStages * kStageBytes;  // [64][32] ones (V's extra N block)
+constexpr int kBarOff = kOnesOff + kVBytes;
+constexpr int kMaxOff = kBarOff + 256;          // per-half row maxima exchanged in the epilogue
+constexpr int kFlagOff = kMaxOff + 2 * kBQ * 4; // per-key-tile "has masked keys" flags
+constexpr int kMaskOff = kFlagOff + kMaxTiles * 4;
+
+// TMEM columns: S/P[b] at 64 b (b = 0, 1; key half h at +32 h),
+// O_h | l_h at 128 + 48 h (32 output columns + 16 row-sum columns).
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kOCol = 128;
+constexpr uint32_t kOStride = 48;
+
+constexpr uint32_t kNegInf = 0xFF80FF80u;
+constexpr uint32_t kNegPad = 0xF14AF14Au;  // bf16x2 (-1e30, -1e30)
+
+struct TcArgs {
+  const __nv_bfloat16 *g;
+  int64_t ld, so, si;
+  const float *mask;
   int64_t ms_o, ms_k;
-  float inf;
-  float q_divisor;
+  float inf, q_divisor;
   __nv_bfloat16 *out;
   int64_t out_ld;
   int n;
+  unsigned int *status;
 };
 
-__device__ __forceinline__ uint32_t smem_addr(const void *p) { return uint32_t(__cvta_generic_to_shared(p)); }
-
-__device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
-               "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N> __device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void *p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_addr(p)));
-}
-__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void *p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_addr(p)));
-}
-
-__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// Packed bf16x2 arithmetic (each result rounded once to nearest-even).
 __device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
@@ -93,29 +91,9 @@ __device__ __forceinline__ uint32_t add_bf16x2(uint32_t a, uint32_t b) {
   asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
 }
-__device__ __forceinline__ uint32_t sub_bf16x2(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-__device__ __forceinline__ uint32_t fma_bf16x2(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t r;
-  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
-  return r;
-}
 __device__ __forceinline__ uint32_t max_bf16x2(uint32_t a, uint32_t b) {
   uint32_t r;
   asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-__device__ __forceinline__ uint32_t ex2_bf16x2(uint32_t a) {
-  uint32_t r;
-  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(r) : "r"(a));
   return r;
 }
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -123,239 +101,321 @@ __device__ __forceinline__ float fast_exp2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-__device__ __forceinline__ uint32_t splat_lo(uint32_t v) { return (v & 0xffffu) | (v << 16); }
-__device__ __forceinline__ uint32_t splat_hi(uint32_t v) { return (v >> 16) | (v & 0xffff0000u); }
 
-constexpr uint32_t kOnes = 0x3F803F80u;      // bf16x2 (1, 1)
-constexpr uint32_t kNegInf = 0xFF80FF80u;    // bf16x2 (-inf, -inf): max identity
-// Padding keys get -1e30 rather than -inf so (t - m) log2(e) stays finite in
-// the two-term fma (inf - inf would give NaN); ex2 of it is exactly 0.
-constexpr uint32_t kNegPad = 0xF14AF14Au;    // bf16x2 (-1.0003e30, -1.0003e30)
-// log2(e) as an unbiased two-term bf16 constant: c1 = bf16(log2 e), c2 = bf16(log2 e - c1).
-constexpr uint32_t kLog2eHi = 0x3FB93FB9u;   // 1.4453125
-constexpr uint32_t kLog2eLo = 0xBB2CBB2Cu;   // -0.00262451171875
-
-// [rows][32] bf16 tile, 4 chunks of 16 B per row, chunk c of row r stored at
-// c ^ ((r >> 1) & 3): conflict-free for ldmatrix row groups of 8.
-__device__ __forceinline__ int qkv_chunk_offset(int row, int chunk) {
-  return row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4);
+// 64-byte swizzle descriptor (K-major: LBO unused = 16 B; MN-major: LBO = block stride), SBO = 512 B.
+__device__ __forceinline__ uint64_t desc_sw64(uint32_t saddr, uint32_t lbo_bytes) {
+  return uint64_t((saddr & 0x3FFFFu) >> 4) | (uint64_t((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+         (uint64_t(512 >> 4) << 32) | (uint64_t(1) << 46) | (uint64_t(4) << 61);
 }
 
-struct Smem {
-  alignas(128) __nv_bfloat16 q[kBQ * kD];
-  alignas(128) __nv_bfloat16 k[2][kBK * kD];
-  alignas(128) __nv_bfloat16 v[2][kBK * kD];
-  alignas(128) __nv_bfloat16 bias[2][kBQ * kBiasLd];
-  int tile_masked[kMaxTiles];
-  // followed by the per-key mask bias of this outer row (bf16, dynamic)
-};
+// Warp-uniform bounded wait: the whole warp continues only if every lane saw the phase.
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, unsigned int *status, unsigned code) {
+  return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, status, code));
+}
 
-__global__ void __launch_bounds__(kThreads, 2) tri_flash_kernel(const FlashArgs args) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
-  __nv_bfloat16 *mask_bias = reinterpret_cast<__nv_bfloat16 *>(smem_raw + sizeof(Smem));
+__global__ void __launch_bounds__(kThreads, 2)
+    tri_flash_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                        const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_bias,
+                        const TcArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBarOff);
+  uint64_t *q_full = bars + 0;
+  uint64_t *q_ready = bars + 1;              // Q scaled in place by the softmax warps
+  uint64_t *st_full = bars + 2;              // [kStages] K, V, bias of a key tile landed
+  uint64_t *st_empty = bars + 2 + kStages;   // [kStages] P.V of that tile completed
+  uint64_t *s_full = bars + 2 + 2 * kStages; // [2] S tile in TMEM
+  uint64_t *p_full = s_full + 2;             // [2] P tile in TMEM (and O rescaled if needed)
+  uint64_t *pv_done = p_full + 2;            // [2] P.V reading TMEM buffer b completed
+  uint64_t *o_full = pv_done + 2;            // all P.V done
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(o_full + 1);
+  float *row_max = reinterpret_cast<float *>(smem + kMaxOff);
+  int *tile_masked = reinterpret_cast<int *>(smem + kFlagOff);
+  __nv_bfloat16 *mask_bias = reinterpret_cast<__nv_bfloat16 *>(smem + kMaskOff);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n = args.n;
-  // Heads of one query tile are adjacent in the grid: they read the same pair rows.
-  const int h = blockIdx.x % kHeadsPerRow;
-  const int q0 = (blockIdx.x / kHeadsPerRow) * kBQ;
-  const int64_t outer = blockIdx.y;
-  const int col0 = h * kD;
+  const int h = blockIdx.x % kHeads;
+  const int q0 = (blockIdx.x / kHeads) * kBQ;
+  const int outer = blockIdx.y;
   const int n_tiles = (n + kBK - 1) / kBK;
 
-  // Per-key additive mask of this outer row (bf16; for mask in {0, 1} adding it
-  // rounds exactly like adding the fp32 value) and a flag per key tile that
-  // says whether any key of the tile is masked at all.
-  if (tid < kMaxTiles) sm.tile_masked[tid] = 0;
+  if (tid < kMaxTiles) tile_masked[tid] = 0;
+  if (tid == 0) {
+    tc::mbar_init(q_full, 1);
+    tc::mbar_init(q_ready, kSoftmaxWarps);
+    for (int s = 0; s < kStages; ++s) {
+      tc::mbar_init(&st_full[s], 1);
+      tc::mbar_init(&st_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&s_full[b], 1);
+      tc::mbar_init(&p_full[b], kSoftmaxWarps);
+      tc::mbar_init(&pv_done[b], 1);
+    }
+    tc::mbar_init(o_full, 1);
+    tc::fence_mbar_init();
+  }
+  // Ones block read as V's second N block (its swizzle is irrelevant: every element is 1).
+  for (int i = tid; i < kVBytes / 16; i += kThreads)
+    *reinterpret_cast<uint4 *>(smem + kOnesOff + i * 16) = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, kTmemCols);
+    tc::tmem_relinquish();
+  }
   __syncthreads();
+  // Start the Q load and fill the ring before the mask pass so the TMA
+  // latency overlaps it.
+  const int prefilled = n_tiles < kStages ? n_tiles : kStages;
+  if (tid == 0) {
+    tc::prefetch_tmap(&map_q);
+    tc::prefetch_tmap(&map_k);
+    tc::prefetch_tmap(&map_v);
+    tc::prefetch_tmap(&map_bias);
+    tc::mbar_arrive_expect_tx(q_full, kBQ * kD * 2);
+    tc::tma_load_3d(smem + kQOff, &map_q, q_full, h * kD, q0, outer);
+    for (int j = 0; j < prefilled; ++j) {
+      uint8_t *stage = smem + kStageOff + j * kStageBytes;
+      tc::mbar_arrive_expect_tx(&st_full[j], kStageBytes);
+      tc::tma_load_3d(stage, &map_k, &st_full[j], h * kD, j * kBK, outer);
+      tc::tma_load_3d(stage + kKBytes, &map_v, &st_full[j], h * kD, j * kBK, outer);
+      tc::tma_load_3d(stage + kKBytes + kVBytes, &map_bias, &st_full[j], j * kBK, q0, h);
+    }
+  }
+  // Mask bias of this outer row (bf16; for mask in {0, 1} adding it rounds
+  // exactly like the fp32 value) and per-tile "any key masked" flags.
   for (int key = tid; key < n_tiles * kBK; key += kThreads) {
-    float mb = key < n ? args.inf * (args.mask[outer * args.ms_o + int64_t(key) * args.ms_k] - 1.f) : 0.f;
+    const float mb =
+        key < n ? args.inf * (args.mask[int64_t(outer) * args.ms_o + int64_t(key) * args.ms_k] - 1.f) : 0.f;
     mask_bias[key] = __float2bfloat16_rn(mb);
-    if (mb != 0.f) atomicOr(&sm.tile_masked[key / kBK], 1);
+    if (mb != 0.f) atomicOr(&tile_masked[key / kBK], 1);
   }
+  tc::fence_proxy_async_smem();
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
 
-  // Per-thread load addresses: K/V row (tid / 4, 16-byte chunk tid % 4) and
-  // four bias chunks (rows tid / 8 + 32 i, chunk tid % 8), advanced per tile.
-  const int kv_row = tid >> 2, kv_chunk = tid & 3;
-  const int64_t kv_base = (outer * args.so + int64_t(kv_row) * args.si) * args.ld + col0 + kv_chunk * 8;
-  const int64_t kv_step = int64_t(kBK) * args.si * args.ld;
-  const int b_row = tid >> 3, b_chunk = tid & 7;
-  const __nv_bfloat16 *bias_base = args.bias + int64_t(h) * args.bias_hs + int64_t(q0 + b_row) * args.bias_ld + b_chunk * 8;
-  const int64_t bias_rows32 = 32 * args.bias_ld;
-
-  for (int c = tid; c < kBQ * 4; c += kThreads) {
-    int row = c >> 2, chunk = c & 3;
-    int qi = q0 + row;
-    bool valid = qi < n;
-    const __nv_bfloat16 *src =
-        valid ? args.q + (outer * args.so + int64_t(qi) * args.si) * args.ld + col0 + chunk * 8 : args.q;
-    cp_async16(reinterpret_cast<uint8_t *>(sm.q) + qkv_chunk_offset(row, chunk), src, valid);
-  }
-  auto load_tile = [&](int tile, int buf) {
-    const int k0 = tile * kBK;
-    const bool kv_valid = k0 + kv_row < n;
-    const int64_t off = kv_base + tile * kv_step;
-    cp_async16(reinterpret_cast<uint8_t *>(sm.k[buf]) + qkv_chunk_offset(kv_row, kv_chunk),
-               kv_valid ? args.k + off : args.k, kv_valid);
-    cp_async16(reinterpret_cast<uint8_t *>(sm.v[buf]) + qkv_chunk_offset(kv_row, kv_chunk),
-               kv_valid ? args.v + off : args.v, kv_valid);
-    const bool col_valid = k0 + b_chunk * 8 < args.bias_ld;
-#pragma unroll
-    for (int i = 0; i < kBQ / 32; ++i) {
-      const bool valid = col_valid && q0 + b_row + 32 * i < n;
-      cp_async16(sm.bias[buf] + (b_row + 32 * i) * kBiasLd + b_chunk * 8,
-                 valid ? bias_base + i * bias_rows32 + k0 : args.bias, valid);
-    }
-  };
-
-  load_tile(0, 0);
-  cp_async_commit();
-
-  const int g = lane >> 2, t = lane & 3;
-  float o_acc[4][4];
-  float l_acc[4];  // row sums from the ones-fragment mma: [0] row g, [2] row g + 8
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    l_acc[i] = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) o_acc[i][j] = 0.f;
-  }
-  float m_run0 = -INFINITY, m_run1 = -INFINITY;  // running maxima of rows g, g + 8
-  uint32_t qf[2][4];
-  constexpr float kLog2e = 1.4426950408889634f;
-
-  for (int tile = 0; tile < n_tiles; ++tile) {
-    const int buf = tile & 1;
-    if (tile + 1 < n_tiles) load_tile(tile + 1, buf ^ 1);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-
-    if (tile == 0) {
-      // Q fragments, scaled and re-rounded as upstream's in-place q /= sqrt(d).
-#pragma unroll
-      for (int ks = 0; ks < 2; ++ks) {
-        int row = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        int chunk = ks * 2 + (lane >> 4);
-        ldmatrix_x4(qf[ks], reinterpret_cast<uint8_t *>(sm.q) + qkv_chunk_offset(row, chunk));
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-          qf[ks][r] = pack_bf16x2(__fdiv_rn(bf16_lo(qf[ks][r]), args.q_divisor),
-                                  __fdiv_rn(bf16_hi(qf[ks][r]), args.q_divisor));
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      for (int j = prefilled; j < n_tiles; ++j) {
+        const int s = j % kStages;
+        if (!tc::mbar_wait(&st_empty[s], ((j / kStages) & 1) ^ 1u, args.status, 0x201)) break;
+        uint8_t *stage = smem + kStageOff + s * kStageBytes;
+        tc::mbar_arrive_expect_tx(&st_full[s], kStageBytes);
+        tc::tma_load_3d(stage, &map_k, &st_full[s], h * kD, j * kBK, outer);
+        tc::tma_load_3d(stage + kKBytes, &map_v, &st_full[s], h * kD, j * kBK, outer);
+        tc::tma_load_3d(stage + kKBytes + kVBytes, &map_bias, &st_full[s], j * kBK, q0, h);
       }
     }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = tc::idesc_bf16(128, kBK, false, false);
+      constexpr uint32_t idesc_pv = tc::idesc_bf16(128, 48, false, true);
+      const uint32_t q_addr = tc::smem_u32(smem + kQOff);
+      const uint32_t ones_addr = tc::smem_u32(smem + kOnesOff);
+      bool ok = tc::mbar_wait(q_ready, 0, args.status, 0x202);
+      auto issue_s = [&](int j) {
+        const int s = j % kStages, b = j & 1;
+        if (!tc::mbar_wait(&st_full[s], (j / kStages) & 1, args.status, 0x203)) return false;
+        // TMEM buffer b still holds P of tile j - 2: its P.V must have finished reading it.
+        if (j >= 2 && !tc::mbar_wait(&pv_done[b], ((j - 2) >> 1) & 1, args.status, 0x204)) return false;
+        tc::tc_fence_after();
+        const uint32_t k_addr = tc::smem_u32(smem + kStageOff + s * kStageBytes);
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk)
+          tc::umma_f16_ss(tmem + uint32_t(b * kBK), desc_sw64(q_addr + kk * 32, 16), desc_sw64(k_addr + kk * 32, 16),
+                          idesc_s, kk);
+        tc::umma_commit(&s_full[b]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
+        const int s = j % kStages, b = j & 1;
+        if (!tc::mbar_wait(&p_full[b], (j >> 1) & 1, args.status, 0x205)) break;
+        tc::tc_fence_after();
+        const uint32_t v_addr = tc::smem_u32(smem + kStageOff + s * kStageBytes + kKBytes);
+        const uint32_t lbo = ones_addr - v_addr;
+#pragma unroll
+        for (int half = 0; half < 2; ++half)
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk)
+            tc::umma_f16_ts(tmem + kOCol + half * kOStride, tmem + uint32_t(b * kBK + half * 32 + kk * 8),
+                            desc_sw64(v_addr + (half * 2 + kk) * 1024, lbo), idesc_pv, (j | kk) != 0);
+        tc::umma_commit(&st_empty[s]);
+        tc::umma_commit(&pv_done[b]);
+        if (j + 1 == n_tiles) tc::umma_commit(o_full);
+      }
+    }
+  } else {
+    // ---------------- softmax + epilogue: half a query row per thread ----------------
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+    const uint32_t o_base = lane_base + kOCol + half * kOStride;
+    float m_ref = -INFINITY;  // reference maximum of this half-row's exponentials
+    // Upstream divides q by sqrt(d) after the projection and rounds to bf16
+    // (_prep_qkv(apply_scale=True), triangle.py:80): apply it to this thread's
+    // half of its Q row in place (elementwise, so the swizzle does not matter).
+    bool ok = warp_wait(q_full, 0, args.status, 0x20B);
+    if (ok) {
+      uint4 *q_row = reinterpret_cast<uint4 *>(smem + kQOff + row * 64) + half * 2;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint4 v = q_row[c];
+        uint32_t *w = &v.x;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          w[e] = pack_bf16x2(__fdiv_rn(bf16_lo(w[e]), args.q_divisor), __fdiv_rn(bf16_hi(w[e]), args.q_divisor));
+        q_row[c] = v;
+      }
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(q_ready);
+    }
+    for (int j = 0; j < n_tiles && ok; ++j) {
+      const int s = j % kStages, b = j & 1;
+      if (!(ok = warp_wait(&s_full[b], (j >> 1) & 1, args.status, 0x206))) break;
+      tc::tc_fence_after();
+      uint32_t sv[32];
+      tc::tmem_ld_32x32b_x32(lane_base + b * kBK + half * 32, sv);
+      if (!(ok = warp_wait(&st_full[s], (j / kStages) & 1, args.status, 0x207))) break;
+      tc::tmem_ld_wait();
 
-    // S = Q K^T for 64 keys (8 n-tiles of 8 keys) and the ordered rounding in
-    // bf16x2: sp[j][0] = row g keys (2t, 2t+1), sp[j][1] = row g + 8.
-    const int k0 = tile * kBK;
-    const bool masked = sm.tile_masked[tile] != 0;
-    uint32_t sp[8][2];
-    uint32_t tmax0 = kNegInf, tmax1 = kNegInf;
+      // Ordered rounding: t = bf16(bf16(bf16(s) + mask) + bias), packed per key pair.
+      const int k0 = j * kBK + half * 32;
+      const uint8_t *bias_row = smem + kStageOff + s * kStageBytes + kKBytes + kVBytes + row * 128;
+      const bool masked = tile_masked[j] != 0;
+      uint32_t t[16];
 #pragma unroll
-    for (int jp = 0; jp < 4; ++jp) {
-      // Bias fragments of n-tiles 2jp, 2jp+1: [0] row g, [1] row g+8, [2]/[3] next n-tile.
-      uint32_t bf[4];
-      ldmatrix_x4(bf, sm.bias[buf] + (warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * kBiasLd +
-                          (jp * 2 + (lane >> 4)) * 8);
+      for (int c = 0; c < 4; ++c) {  // 16-byte chunk = keys 8c .. 8c + 7 of this half
+        const int chunk = half * 4 + c;
+        const uint4 bv = *reinterpret_cast<const uint4 *>(bias_row + ((chunk ^ (row & 7)) << 4));
+        const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int j = jp * 2 + half;
-        float s[4] = {0.f, 0.f, 0.f, 0.f};
-        uint32_t kf[4];
-        ldmatrix_x4(kf, reinterpret_cast<uint8_t *>(sm.k[buf]) + qkv_chunk_offset(j * 8 + (lane & 7), lane >> 3));
-        mma_bf16(s, qf[0], kf[0], kf[1]);
-        mma_bf16(s, qf[1], kf[2], kf[3]);
-        uint32_t p0 = cvt_bf16x2(s[0], s[1]), p1 = cvt_bf16x2(s[2], s[3]);
-        if (masked) {
-          const uint32_t mb = *reinterpret_cast<const uint32_t *>(mask_bias + k0 + j * 8 + 2 * t);
-          p0 = add_bf16x2(p0, mb);
-          p1 = add_bf16x2(p1, mb);
+        for (int e = 0; e < 4; ++e) {
+          const int pr = c * 4 + e;
+          uint32_t x = cvt_bf16x2(__uint_as_float(sv[2 * pr]), __uint_as_float(sv[2 * pr + 1]));
+          if (masked) x = add_bf16x2(x, *reinterpret_cast<const uint32_t *>(mask_bias + k0 + 2 * pr));
+          t[pr] = add_bf16x2(x, bw[e]);
         }
-        sp[j][0] = add_bf16x2(p0, bf[half * 2 + 0]);
-        sp[j][1] = add_bf16x2(p1, bf[half * 2 + 1]);
       }
-    }
-    if (k0 + kBK > n) {  // last tile: keys past n contribute nothing
+      // Keys past n: excluded from the maximum here and zeroed in P below.
+      const bool tail = k0 + 32 > n;
+      if (tail) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int key = k0 + j * 8 + 2 * t;
-        const uint32_t keep = (key < n ? 0x0000ffffu : 0u) | (key + 1 < n ? 0xffff0000u : 0u);
-        sp[j][0] = (sp[j][0] & keep) | (kNegPad & ~keep);
-        sp[j][1] = (sp[j][1] & keep) | (kNegPad & ~keep);
+        for (int pr = 0; pr < 16; ++pr) {
+          const int key = k0 + 2 * pr;
+          const uint32_t keep = (key < n ? 0x0000ffffu : 0u) | (key + 1 < n ? 0xffff0000u : 0u);
+          t[pr] = (t[pr] & keep) | (kNegPad & ~keep);
+        }
       }
-    }
+      uint32_t mx[4] = {t[0], t[1], t[2], t[3]};
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      tmax0 = max_bf16x2(tmax0, sp[j][0]);
-      tmax1 = max_bf16x2(tmax1, sp[j][1]);
-    }
-    // Row maxima packed as (row g, row g + 8), reduced over the 4-thread quad.
-    uint32_t rmax = max_bf16x2((tmax0 & 0xffffu) | (tmax1 << 16), (tmax0 >> 16) | (tmax1 & 0xffff0000u));
-    rmax = max_bf16x2(rmax, __shfl_xor_sync(0xffffffffu, rmax, 1));
-    rmax = max_bf16x2(rmax, __shfl_xor_sync(0xffffffffu, rmax, 2));
-    const float m_new0 = fmaxf(m_run0, bf16_lo(rmax)), m_new1 = fmaxf(m_run1, bf16_hi(rmax));
-    if (m_new0 != m_run0 || m_new1 != m_run1) {
-      const float alpha0 = fast_exp2((m_run0 - m_new0) * kLog2e);
-      const float alpha1 = fast_exp2((m_run1 - m_new1) * kLog2e);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        o_acc[i][0] *= alpha0, o_acc[i][1] *= alpha0;
-        o_acc[i][2] *= alpha1, o_acc[i][3] *= alpha1;
-      }
-      l_acc[0] *= alpha0, l_acc[1] *= alpha0, l_acc[2] *= alpha1, l_acc[3] *= alpha1;
-      m_run0 = m_new0, m_run1 = m_new1;
-    }
-    // P = exp2(t log2 e - m log2 e) in fp32 (the bf16 scores convert exactly),
-    // rounded to bf16x2 as the A fragments of P.V.
-    const float ml0 = m_run0 * kLog2e, ml1 = m_run1 * kLog2e;
-    uint32_t pf[4][4];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float e0 = fast_exp2(fmaf(bf16_lo(sp[j][0]), kLog2e, -ml0));
-      const float e1 = fast_exp2(fmaf(bf16_hi(sp[j][0]), kLog2e, -ml0));
-      const float e2 = fast_exp2(fmaf(bf16_lo(sp[j][1]), kLog2e, -ml1));
-      const float e3 = fast_exp2(fmaf(bf16_hi(sp[j][1]), kLog2e, -ml1));
-      const int kk = j >> 1, hi = j & 1;
-      pf[kk][hi * 2 + 0] = cvt_bf16x2(e0, e1);
-      pf[kk][hi * 2 + 1] = cvt_bf16x2(e2, e3);
-    }
-    // O += P V (4 k-steps of 16 keys x 4 n-tiles of 8 channels); l += P 1.
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      uint32_t a[4] = {pf[kk][0], pf[kk][1], pf[kk][2], pf[kk][3]};
-#pragma unroll
-      for (int np = 0; np < 2; ++np) {
-        uint32_t vf[4];
-        int row = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        int chunk = np * 2 + (lane >> 4);
-        ldmatrix_x4_trans(vf, reinterpret_cast<uint8_t *>(sm.v[buf]) + qkv_chunk_offset(row, chunk));
-        mma_bf16(o_acc[np * 2 + 0], a, vf[0], vf[1]);
-        mma_bf16(o_acc[np * 2 + 1], a, vf[2], vf[3]);
-      }
-      mma_bf16(l_acc, a, kOnes, kOnes);
-    }
-    __syncthreads();
-  }
+      for (int pr = 4; pr < 16; ++pr) mx[pr & 3] = max_bf16x2(mx[pr & 3], t[pr]);
+      const uint32_t tmax = max_bf16x2(max_bf16x2(mx[0], mx[1]), max_bf16x2(mx[2], mx[3]));
+      const float m_tile = fmaxf(bf16_lo(tmax), bf16_hi(tmax));
 
-  // Normalise, round, gate, store.
+      // Reference maximum: set on the first tile; raised (with O_h rescaled)
+      // only when this tile's maximum exceeds it by more than 2^8 in exp2.
+      const bool first = j == 0;
+      const bool grow = !first && (m_tile - m_ref) * kLog2e > kRescaleLog2;
+      if (__any_sync(0xffffffffu, grow)) {
+        // O_h holds tiles < j: wait for the P.V of tile j - 1, then scale in place.
+        if (!(ok = warp_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, args.status, 0x208))) break;
+        tc::tc_fence_after();
+        const float alpha = grow ? fast_exp2((m_ref - m_tile) * kLog2e) : 1.f;
+        uint32_t o[32], l16[16];
+        tc::tmem_ld_32x32b_x32(o_base, o);
+        tc::tmem_ld_32x32b_x16(o_base + 32, l16);
+        tc::tmem_ld_wait();
 #pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int qi = q0 + warp * 16 + g + r * 8;
-    if (qi >= n) continue;
-    const float inv = 1.f / l_acc[r * 2];
-    const int64_t pair = outer * args.so + int64_t(qi) * args.si;
-    const __nv_bfloat16 *grow = args.g + pair * args.ld + col0;
-    __nv_bfloat16 *orow = args.out + pair * args.out_ld + col0;
+        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int d = i * 8 + 2 * t;
-      const uint32_t gv = *reinterpret_cast<const uint32_t *>(grow + d);
-      float o0 = bf16r(o_acc[i][r * 2 + 0] * inv), o1 = bf16r(o_acc[i][r * 2 + 1] * inv);
-      float g0 = bf16r(sigmoidf_fast(bf16_lo(gv))), g1 = bf16r(sigmoidf_fast(bf16_hi(gv)));
-      *reinterpret_cast<uint32_t *>(orow + d) = pack_bf16x2(o0 * g0, o1 * g1);
+        for (int i = 0; i < 16; ++i) l16[i] = __float_as_uint(__uint_as_float(l16[i]) * alpha);
+        tc::tmem_st_32x32b_x16(o_base, *reinterpret_cast<const uint32_t(*)[16]>(&o[0]));
+        tc::tmem_st_32x32b_x16(o_base + 16, *reinterpret_cast<const uint32_t(*)[16]>(&o[16]));
+        tc::tmem_st_32x32b_x16(o_base + 32, l16);
+      }
+      if (first || grow) m_ref = m_tile;
+      const float ml = m_ref * kLog2e;
+
+      // P (bf16x2 per key pair) over the first 16 columns of this S half.
+      uint32_t p[16];
+#pragma unroll
+      for (int pr = 0; pr < 16; ++pr)
+        p[pr] = cvt_bf16x2(fast_exp2(fmaf(bf16_lo(t[pr]), kLog2e, -ml)), fast_exp2(fmaf(bf16_hi(t[pr]), kLog2e, -ml)));
+      if (tail) {
+#pragma unroll
+        for (int pr = 0; pr < 16; ++pr) {
+          const int key = k0 + 2 * pr;
+          p[pr] &= (key < n ? 0x0000ffffu : 0u) | (key + 1 < n ? 0xffff0000u : 0u);
+        }
+      }
+      tc::tmem_st_32x32b_x16(lane_base + b * kBK + half * 32, p);
+      tc::tmem_st_wait();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&p_full[b]);
+    }
+    // Epilogue: merge the two key halves, O / l, bf16, gate, store.  This
+    // thread writes output channels 16 half .. 16 half + 15 of its row.
+    row_max[half * kBQ + row] = m_ref;
+    asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxWarps * 32) : "memory");
+    const float m_other = row_max[(half ^ 1) * kBQ + row];
+    if (ok && warp_wait(o_full, 0, args.status, 0x20A)) {
+      tc::tc_fence_after();
+      const float m0 = half == 0 ? m_ref : m_other, m1 = half == 0 ? m_other : m_ref;
+      const float m = fmaxf(m0, m1);
+      const float a0 = fast_exp2((m0 - m) * kLog2e), a1 = fast_exp2((m1 - m) * kLog2e);
+      uint32_t o0[16], o1[16], l0[16], l1[16];
+      tc::tmem_ld_32x32b_x16(lane_base + kOCol + half * 16, o0);
+      tc::tmem_ld_32x32b_x16(lane_base + kOCol + kOStride + half * 16, o1);
+      tc::tmem_ld_32x32b_x16(lane_base + kOCol + 32, l0);
+      tc::tmem_ld_32x32b_x16(lane_base + kOCol + kOStride + 32, l1);
+      tc::tmem_ld_wait();
+      const int qi = q0 + row;
+      if (qi < n) {
+        const float inv = 1.f / (__uint_as_float(l0[0]) * a0 + __uint_as_float(l1[0]) * a1);
+        const int64_t pair = int64_t(outer) * args.so + int64_t(qi) * args.si;
+        const uint4 *g4 = reinterpret_cast<const uint4 *>(args.g + pair * args.ld + h * kD + half * 16);
+        uint4 *o4 = reinterpret_cast<uint4 *>(args.out + pair * args.out_ld + h * kD + half * 16);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const uint4 gv = g4[c];
+          const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int d = c * 8 + e * 2;
+            const float v0 = (__uint_as_float(o0[d]) * a0 + __uint_as_float(o1[d]) * a1) * inv;
+            const float v1 = (__uint_as_float(o0[d + 1]) * a0 + __uint_as_float(o1[d + 1]) * a1) * inv;
+            const float g0 = bf16r(sigmoidf_fast(bf16_lo(gw[e]))), g1 = bf16r(sigmoidf_fast(bf16_hi(gw[e])));
+            w[e] = pack_bf16x2(bf16r(v0) * g0, bf16r(v1) * g1);
+          }
+          o4[c] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
     }
   }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+bool pair_rows_map(CUtensorMap *map, const void *base, int64_t ld, int64_t so, int64_t si, int n, int box_rows) {
+  // Element (column c, inner b, outer a) at base + (a*so + b*si)*ld + c.
+  uint64_t dims[3] = {uint64_t(kHeads * kD), uint64_t(n), uint64_t(n)};
+  uint64_t strides[2] = {uint64_t(si * ld * 2), uint64_t(so * ld * 2)};
+  uint32_t box[3] = {uint32_t(kD), uint32_t(box_rows), 1};
+  return encode_tmap(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
 // Bias planes from the pair-major projection: natural[h][r][s] = tb[r*n + s][h]
@@ -388,6 +448,52 @@ __global__ void bias_planes_kernel(const __nv_bfloat16 *tb, int64_t tb_ld, int h
 
 using namespace bl;
 
+extern "C" int bl_triangle_attention(const void *q, const void *k, const void *v, const void *g, int64_t ld,
+                                        int64_t so, int64_t si, const void *bias, int64_t bias_ld, int64_t bias_hs,
+                                        const float *mask, int64_t ms_o, int64_t ms_k, float inf, int64_t heads,
+                                        int64_t head_dim, int64_t n, void *out, int64_t out_ld, void *stream) {
+  BL_REQUIRE(head_dim == kD && heads == kHeads, "bl_triangle_attention: 4 heads x 32 supported");
+  BL_REQUIRE(n >= 0, "bl_triangle_attention: bad shape");
+  if (n == 0) return BL_OK;
+  BL_REQUIRE(n <= kMaxTiles * kBK, "bl_triangle_attention: at most 4096 tokens");
+  BL_REQUIRE(q && k && v && g && bias && mask && out, "bl_triangle_attention: null pointer");
+  BL_REQUIRE(ld % 8 == 0 && out_ld % 8 == 0 && bias_ld % 8 == 0 && bias_ld >= n && bias_hs % 8 == 0,
+             "bl_triangle_attention: leading dimensions must keep 16-byte rows");
+  BL_REQUIRE(aligned_to(q, 16) && aligned_to(k, 16) && aligned_to(v, 16) && aligned_to(g, 16) &&
+                 aligned_to(bias, 16) && aligned_to(out, 16),
+             "bl_triangle_attention: pointers must be 16-byte aligned");
+  CUtensorMap map_q, map_k, map_v, map_bias;
+  BL_REQUIRE(pair_rows_map(&map_q, q, ld, so, si, int(n), kBQ) && pair_rows_map(&map_k, k, ld, so, si, int(n), kBK) &&
+                 pair_rows_map(&map_v, v, ld, so, si, int(n), kBK),
+             "bl_triangle_attention: cannot encode the q/k/v tensor maps");
+  {
+    uint64_t dims[3] = {uint64_t(bias_ld), uint64_t(n), uint64_t(kHeads)};
+    uint64_t strides[2] = {uint64_t(bias_ld * 2), uint64_t(bias_hs * 2)};
+    uint32_t box[3] = {kBK, kBQ, 1};
+    BL_REQUIRE(encode_tmap(&map_bias, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, bias, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B),
+               "bl_triangle_attention: cannot encode the bias tensor map");
+  }
+  TcArgs args;
+  args.g = static_cast<const __nv_bfloat16 *>(g);
+  args.ld = ld, args.so = so, args.si = si;
+  args.mask = mask, args.ms_o = ms_o, args.ms_k = ms_k;
+  args.inf = inf;
+  args.q_divisor = sqrtf(float(head_dim));
+  args.out = static_cast<__nv_bfloat16 *>(out);
+  args.out_ld = out_ld;
+  args.n = int(n);
+  args.status = device_status_ptr();
+  BL_REQUIRE(args.status, "bl_triangle_attention: device status word unavailable");
+  const int n_tiles = int((n + kBK - 1) / kBK);
+  const int smem = kMaskOff + n_tiles * kBK * 2 + 1024;
+  BL_CUDA(ensure_smem_limit(reinterpret_cast<const void *>(tri_flash_tc_kernel), 232448));
+  dim3 grid(unsigned((n + kBQ - 1) / kBQ * kHeads), unsigned(n));
+  tri_flash_tc_kernel<<<grid, kThreads, smem, as_stream(stream)>>>(map_q, map_k, map_v, map_bias, args);
+  BL_LAUNCH_CHECK();
+  return BL_OK;
+}
+
 extern "C" int bl_triangle_bias_planes(const void *tb, int64_t tb_ld, int64_t heads, int64_t n, int transpose,
                                        void *out, int64_t ld, void *stream) {
   BL_REQUIRE(n >= 0 && heads > 0 && heads <= 64, "bl_triangle_bias_planes: bad shape");
@@ -397,46 +503,6 @@ extern "C" int bl_triangle_bias_planes(const void *tb, int64_t tb_ld, int64_t he
   dim3 grid((n + 31) / 32, (n + 31) / 32, heads);
   bias_planes_kernel<<<grid, 256, 0, as_stream(stream)>>>(static_cast<const __nv_bfloat16 *>(tb), tb_ld, int(heads),
                                                          int(n), transpose, static_cast<__nv_bfloat16 *>(out), ld);
-  BL_LAUNCH_CHECK();
-  return BL_OK;
-}
-
-extern "C" int bl_triangle_attention(const void *q, const void *k, const void *v, const void *g, int64_t ld,
-                                     int64_t so, int64_t si, const void *bias, int64_t bias_ld, int64_t bias_hs,
-                                     const float *mask, int64_t ms_o, int64_t ms_k, float inf, int64_t heads,
-                                     int64_t head_dim, int64_t n, void *out, int64_t out_ld, void *stream) {
-  BL_REQUIRE(head_dim == kD, "bl_triangle_attention: head_dim must be 32");
-  BL_REQUIRE(heads == kHeadsPerRow, "bl_triangle_attention: 4 heads supported");
-  BL_REQUIRE(n >= 0, "bl_triangle_attention: bad shape");
-  if (n == 0) return BL_OK;
-  BL_REQUIRE(n <= kMaxTiles * kBK, "bl_triangle_attention: at most 4096 tokens");
-  BL_REQUIRE(q && k && v && g && bias && mask && out, "bl_triangle_attention: null pointer");
-  BL_REQUIRE(ld % 8 == 0 && out_ld % 2 == 0 && bias_ld % 8 == 0 && bias_ld >= n,
-             "bl_triangle_attention: leading dimensions must keep 16-byte rows");
-  BL_REQUIRE(aligned_to(q, 16) && aligned_to(k, 16) && aligned_to(v, 16) && aligned_to(bias, 16) &&
-                 aligned_to(g, 4) && aligned_to(out, 4),
-             "bl_triangle_attention: misaligned pointer");
-  BL_REQUIRE(bias_hs % 8 == 0, "bl_triangle_attention: bias head stride must be a multiple of 8");
-  FlashArgs args;
-  args.q = static_cast<const __nv_bfloat16 *>(q);
-  args.k = static_cast<const __nv_bfloat16 *>(k);
-  args.v = static_cast<const __nv_bfloat16 *>(v);
-  args.g = static_cast<const __nv_bfloat16 *>(g);
-  args.ld = ld, args.so = so, args.si = si;
-  args.bias = static_cast<const __nv_bfloat16 *>(bias);
-  args.bias_ld = bias_ld, args.bias_hs = bias_hs;
-  args.mask = mask, args.ms_o = ms_o, args.ms_k = ms_k;
-  args.inf = inf;
-  args.q_divisor = sqrtf(float(head_dim));
-  args.out = static_cast<__nv_bfloat16 *>(out);
-  args.out_ld = out_ld;
-  args.n = int(n);
-  const int n_tiles = int((n + kBK - 1) / kBK);
-  const size_t smem = sizeof(Smem) + size_t(n_tiles) * kBK * sizeof(__nv_bfloat16);
-  BL_REQUIRE(smem <= 227 * 1024, "bl_triangle_attention: too many tokens for the mask buffer");
-  BL_CUDA(ensure_smem_limit(reinterpret_cast<const void *>(tri_flash_kernel), int(227 * 1024)));
-  dim3 grid(unsigned((n + kBQ - 1) / kBQ * kHeadsPerRow), unsigned(n));
-  tri_flash_kernel<<<grid, kThreads, smem, as_stream(stream)>>>(args);
   BL_LAUNCH_CHECK();
   return BL_OK;
 }

@@ -23,9 +23,6 @@ from . import _lib, kernels
 from ._lib import call, stream_of
 
 _BF16 = torch.bfloat16
-# C-ABI entry of the flash triangle-attention kernel.
-ATTENTION_ENTRY = "bl_triangle_attention"
-
 
 def _pad8(n):
     return (n + 7) // 8 * 8
@@ -143,7 +140,7 @@ def triangle_attention_forward(self, x, mask=None, chunk_size=None, use_kernels=
         so, si = (n, 1) if starting else (1, n)
         ms_o, ms_k = (n, 1) if starting else (1, n)
         base = proj.data_ptr()
-        call(ATTENTION_ENTRY, base, base + 128 * 2, base + 256 * 2, base + 384 * 2, width, so, si,
+        call("bl_triangle_attention", base, base + 128 * 2, base + 256 * 2, base + 384 * 2, width, so, si,
              bias.data_ptr(), n_pad, n * n_pad, mask[b].data_ptr(), ms_o, ms_k, float(getattr(self, "inf", 1e9)),
              4, 32, n, gated.data_ptr(), 128, stream)
         del proj, bias

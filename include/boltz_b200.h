@@ -228,24 +228,15 @@ BL_API int bl_triangle_bias_planes(const void *tb, int64_t tb_ld, int64_t heads,
  * (outer a, inner b) = a*so + b*si (starting node: so = n, si = 1; ending
  * node: so = 1, si = n).  bias(h, b, c) at bias + h*bias_hs + b*bias_ld + c.
  * mask(a, c) at mask + a*ms_o + c*ms_k (fp32).  out rows of out_ld elements
- * at the same pair rows.  head_dim must be 32.
+ * at the same pair rows.  heads must be 4 and head_dim 32, n <= 4096; all pointers
+ * 16-byte aligned, ld / out_ld / bias_ld / bias_hs multiples of 8.  Runs on
+ * tcgen05 tensor cores (scores and P in TMEM, TMA-fed key tiles).
  */
 BL_API int bl_triangle_attention(const void *q, const void *k, const void *v, const void *g, int64_t ld,
                                  int64_t so, int64_t si, const void *bias, int64_t bias_ld,
                                  int64_t bias_hs, const float *mask, int64_t ms_o, int64_t ms_k,
                                  float inf, int64_t heads, int64_t head_dim, int64_t n, void *out,
                                  int64_t out_ld, void *stream);
-
-/*
- * Same contract as bl_triangle_attention, computed with tcgen05 tensor cores
- * (S and P.V in TMEM, TMA-fed tiles, one softmax thread per query row).
- * Pointers 16-byte aligned; ld, out_ld, bias_ld, bias_hs multiples of 8.
- */
-BL_API int bl_triangle_attention_tc(const void *q, const void *k, const void *v, const void *g, int64_t ld,
-                                    int64_t so, int64_t si, const void *bias, int64_t bias_ld,
-                                    int64_t bias_hs, const float *mask, int64_t ms_o, int64_t ms_k,
-                                    float inf, int64_t heads, int64_t head_dim, int64_t n, void *out,
-                                    int64_t out_ld, void *stream);
 
 /*
  * Pair transition (LayerNorm -> fc1|fc2 -> SwiGLU -> fc3, the bf16-autocast
