@@ -151,6 +151,11 @@ template <int N> __device__ __forceinline__ void bulk_wait() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Hint: bring [p, p + bytes) into L2 (p 16-byte aligned, bytes a multiple of 16).
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
@@ -239,6 +244,22 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
       : "r"(taddr)
       : "memory");
 }
+
+// tcgen05.wait::ld that also names the registers the pending loads write, so
+// the compiler cannot move any use of them above the wait.
+#define BL_R16(a) "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]), \
+    "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]), "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15])
+__device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&a)[16], uint32_t (&b)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : BL_R16(a), BL_R16(b)::"memory");
+}
+__device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&a)[32], uint32_t (&b)[32]) {
+  uint32_t(&a0)[16] = *reinterpret_cast<uint32_t(*)[16]>(&a[0]);
+  uint32_t(&a1)[16] = *reinterpret_cast<uint32_t(*)[16]>(&a[16]);
+  uint32_t(&b0)[16] = *reinterpret_cast<uint32_t(*)[16]>(&b[0]);
+  uint32_t(&b1)[16] = *reinterpret_cast<uint32_t(*)[16]>(&b[16]);
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : BL_R16(a0), BL_R16(a1), BL_R16(b0), BL_R16(b1)::"memory");
+}
+#undef BL_R16
 
 __device__ __forceinline__ uint32_t tmem_addr(uint32_t base, uint32_t lane, uint32_t col) {
   return base + (lane << 16) + col;

@@ -127,15 +127,14 @@ def triangle_attention_forward(self, x, mask=None, chunk_size=None, use_kernels=
     rows = n * n
     for b in range(batch):
         xb = x[b].reshape(rows, 128).float().contiguous()
-        xn = torch.empty(rows, 128, device=x.device, dtype=_BF16)
         bias = torch.empty(4, n, n_pad, device=x.device, dtype=_BF16)
-        # LayerNorm fused with the 128 -> 4 triangle-bias projection, written as
-        # [h][query][key] planes (transposed for the ending node).
-        call("bl_layernorm_heads", xb.data_ptr(), n, _f32(ln.weight).data_ptr(), _f32(ln.bias).data_ptr(),
-             float(ln.eps), w["w_heads"].data_ptr(), 4, int(not starting), xn.data_ptr(), bias.data_ptr(), n_pad,
-             stream)
-        proj = _linear_bf16(xn, w["w_in"], w["b_in"])  # [n*n, 512]: q | k | v | g (+ g bias)
-        del xn
+        proj = torch.empty(rows, 512, device=x.device, dtype=_BF16)  # q | k | v | g (+ g bias)
+        # LayerNorm, the q/k/v/g projection and the 128 -> 4 triangle-bias
+        # projection in one pass; bias planes are [h][query][key] (transposed
+        # for the ending node).
+        call("bl_attention_projection", xb.data_ptr(), n, _f32(ln.weight).data_ptr(), _f32(ln.bias).data_ptr(),
+             float(ln.eps), w["w_in"].data_ptr(), w["b_in"].data_ptr(), w["w_heads"].data_ptr(), int(not starting),
+             proj.data_ptr(), 512, bias.data_ptr(), n_pad, stream)
         gated = torch.empty(rows, 128, device=x.device, dtype=_BF16)
         so, si = (n, 1) if starting else (1, n)
         ms_o, ms_k = (n, 1) if starting else (1, n)
@@ -191,13 +190,15 @@ def triangle_multiplication_forward(self, x, mask, use_kernels=False, residual=N
     out = None if residual is not None else torch.empty(batch, n, n, 128, device=x.device, dtype=_BF16)
     stream = stream_of(x)
     for b in range(batch):
-        xn = _layer_norm_bf16(x[b].reshape(rows, 128), self.norm_in)
-        pg = _linear_bf16(xn, w["w_in"])  # [n*n, 512]: p | g
-        a = torch.empty(128, n, n_pad, device=x.device, dtype=_BF16)
-        bp = torch.empty_like(a)
-        call("bl_trimul_pack_planes", pg.data_ptr(), 512, mask[b].data_ptr(), n, n_pad, a.data_ptr(), bp.data_ptr(),
-             stream)
-        del pg
+        xb = x[b].reshape(rows, 128).float().contiguous()
+        xn = torch.empty(rows, 128, device=x.device, dtype=_BF16)
+        planes = torch.empty(256, n, n_pad, device=x.device, dtype=_BF16)
+        # LayerNorm, p_in | g_in, the sigmoid gate and the mask in one pass,
+        # written as channel planes a = planes[:128], b = planes[128:].
+        call("bl_trimul_projection", xb.data_ptr(), n, _f32(self.norm_in.weight).data_ptr(),
+             _f32(self.norm_in.bias).data_ptr(), float(self.norm_in.eps), w["w_in"].data_ptr(), mask[b].data_ptr(),
+             planes.data_ptr(), n_pad, xn.data_ptr(), stream)
+        a, bp = planes[:128], planes[128:]
         prod = torch.empty_like(a)
         plane = n * n_pad
         # outgoing: O_c = A_c B_c^T over planes [i][k] (K-major);
@@ -205,7 +206,7 @@ def triangle_multiplication_forward(self, x, mask, use_kernels=False, residual=N
         mn = int(not outgoing)
         call("bl_batched_gemm", a.data_ptr(), mn, n_pad, plane, bp.data_ptr(), mn, n_pad, plane, prod.data_ptr(),
              n_pad, plane, 128, n, n, n, None, stream)
-        del a, bp
+        del a, bp, planes
         normed = torch.empty(rows, 128, device=x.device, dtype=_BF16)
         call("bl_layernorm_planes", prod.data_ptr(), n, n_pad, _f32(self.norm_out.weight).data_ptr(),
              _f32(self.norm_out.bias).data_ptr(), float(self.norm_out.eps), normed.data_ptr(), _lib.BL_BF16, stream)

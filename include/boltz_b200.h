@@ -200,6 +200,39 @@ BL_API int bl_trimul_pack_planes(const void *pg, int64_t pg_ld, const float *mas
                                  int64_t plane_ld, void *a_planes, void *b_planes, void *stream);
 
 /*
+ * Triangle-attention input stage in one pass over the fp32 pair rows
+ * x [n*n][128] (16-byte aligned):
+ *   x_hat = bf16(LayerNorm(x))                                  (fp32 statistics)
+ *   proj[r][0:512] = bf16(x_hat[r] . w^T + bias)                w bf16 [512][128] = q | k | v | g rows
+ *   bias_planes[h][q][k] = bf16(x_hat[q*n + k] . w_heads[h])    (transpose = 0, starting node)
+ *   bias_planes[h][k][q] = same                                 (transpose = 1, ending node)
+ * bias (fp32 [512]) may be NULL; w_heads is bf16 [4][128]; proj rows are
+ * proj_ld >= 512 elements (multiple of 8), bias planes bias_ld >= n.
+ * Replaces the layer_norm fast path (triangle.py:107-146), the q/k/v/g
+ * linears of _prep_qkv (triangle.py:80, upstream Attention) and upstream's
+ * triangle-bias `linear` that feed ordered_triangle_forward (triangle.py:32).
+ */
+BL_API int bl_attention_projection(const float *x, int64_t n, const float *ln_weight, const float *ln_bias,
+                                   float eps, const void *w, const float *bias, const void *w_heads,
+                                   int transpose, void *proj, int64_t proj_ld, void *bias_planes,
+                                   int64_t bias_ld, void *stream);
+
+/*
+ * Triangle-multiplication input stage in one pass over the fp32 pair rows
+ * x [n*n][128]:
+ *   x_hat = bf16(LayerNorm(x)) -> xn [n*n][128]
+ *   p = x_hat . w[0:256]^T, g = x_hat . w[256:512]^T        (bf16 results; w = [p_in; g_in])
+ *   planes[c][i][k] = bf16(bf16(p_c * bf16(sigmoid(g_c))) * mask[i*n + k])   c < 256
+ * planes is bf16 [256][n][plane_ld] (channels 0..127 = a, 128..255 = b),
+ * plane_ld >= n and a multiple of 8.  Replaces norm_in + p_in/g_in + the
+ * gate/pack/split kernels and layout copies of multiplication.py:48-120
+ * (multiplication_gate_hip.cu:16-58).
+ */
+BL_API int bl_trimul_projection(const float *x, int64_t n, const float *ln_weight, const float *ln_bias,
+                                float eps, const void *w, const float *mask, void *planes, int64_t plane_ld,
+                                void *xn, void *stream);
+
+/*
  * Pair-transition activation on the joint fc1|fc2 projection:
  *   out[r][c] = bf16(bf16(silu(x[r][c])) * x[r][width + c]).
  * Replaces kernels/pair_hip.cu:42 `pair_silu_mul` on separate fc1/fc2
