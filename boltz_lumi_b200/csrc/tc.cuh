@@ -142,6 +142,13 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void 
                : "memory");
 }
 
+// global[tile at (x, y)] += shared tile, element-wise in the map's type (fp32 here).
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, const void *src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 template <int N> __device__ __forceinline__ void bulk_wait_read() {

@@ -246,6 +246,19 @@ def transition_forward(self, x, chunk_size=None, residual=None):
     w = _transition_weights(self)
     rows = x.numel() // dim
     stream = stream_of(x)
+    if dim == 128 and hidden == 512 and out_dim == 128:
+        # One fused kernel: LN, fc1|fc2, SwiGLU and fc3 with the hidden
+        # activations on chip; the residual lands as a reduce-add into z.
+        xf = x.reshape(rows, dim).float().contiguous()
+        norm = self.norm
+        args = (xf.data_ptr(), rows, _f32(norm.weight).data_ptr(), _f32(norm.bias).data_ptr(), float(norm.eps),
+                w["w12"].data_ptr(), w["w3"].data_ptr())
+        if residual is not None:
+            call("bl_pair_transition", *args, residual.data_ptr(), None, stream)
+            return residual
+        out = torch.empty(rows, out_dim, device=x.device, dtype=_BF16)
+        call("bl_pair_transition", *args, None, out.data_ptr(), stream)
+        return out.view(*x.shape[:-1], out_dim)
     xn = _layer_norm_bf16(x.reshape(rows, dim).contiguous(), self.norm)
     h12 = _linear_bf16(xn, w["w12"])
     del xn

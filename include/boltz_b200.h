@@ -233,6 +233,19 @@ BL_API int bl_trimul_projection(const float *x, int64_t n, const float *ln_weigh
                                 void *xn, void *stream);
 
 /*
+ * Pair transition in one pass over fp32 rows x [rows][128]:
+ *   x_hat = bf16(LayerNorm(x)), u = bf16(bf16(silu(bf16(x_hat fc1^T))) * bf16(x_hat fc2^T)),
+ *   y = bf16(u fc3^T)
+ * then z += y (z fp32 [rows][128], may alias x) or out = y (bf16 [rows][128]);
+ * exactly one of z and out is non-NULL.  w12 is bf16 [1024][128] (fc1 rows
+ * then fc2 rows), w3 is bf16 [128][512].  Replaces upstream
+ * Transition.forward (pair_transition.py:8-28) including the pair_silu_mul
+ * kernel (kernels/pair_hip.cu:42-64); the hidden activations stay on chip.
+ */
+BL_API int bl_pair_transition(const float *x, int64_t rows, const float *ln_weight, const float *ln_bias,
+                              float eps, const void *w12, const void *w3, float *z, void *out, void *stream);
+
+/*
  * Pair-transition activation on the joint fc1|fc2 projection:
  *   out[r][c] = bf16(bf16(silu(x[r][c])) * x[r][width + c]).
  * Replaces kernels/pair_hip.cu:42 `pair_silu_mul` on separate fc1/fc2

@@ -85,6 +85,21 @@ def test_pair_transition(n):
             assert_close(actual.float(), expected, atol=BF16_ATOL)
 
 
+@pytest.mark.parametrize("rows", [1, 129, 5000])
+def test_pair_transition_residual_in_place(rows):
+    """z += Transition(z) with z both the input and the residual (the block's
+    in-place update); ragged row counts exercise the last partial tile."""
+    from boltz_lumi_b200 import forwards
+
+    mod, ref = build(layers.Transition, oracle.Transition, 128, 512, std=0.05)
+    z = torch.randn(rows, 128, generator=torch.Generator().manual_seed(rows))
+    expected = z + ref(z)
+    with torch.inference_mode():
+        zc = z.cuda()
+        forwards.transition_forward(mod, zc, residual=zc)
+    assert_close(zc.cpu(), expected, atol=BF16_ATOL)
+
+
 # fp32 diffusion ops: weights ~ N(0, 1/fan_in) keep outputs O(1), where a 1e-4
 # absolute bound is meaningful (N(0, 0.08) at width 1536 gives outputs in the tens).
 @pytest.mark.parametrize("tokens,dim", [(384, 768), (1000, 128), (5, 768)])
