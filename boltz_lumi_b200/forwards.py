@@ -162,7 +162,9 @@ def _multiplication_weights(module):
         w_out = torch.zeros(256, 256, device=w_in.device, dtype=torch.float32)
         w_out[:128, :128] = module.p_out.weight
         w_out[128:, 128:] = module.g_out.weight
-        return dict(w_in=w_in.to(_BF16).contiguous(), w_out=w_out.to(_BF16).contiguous())
+        w_pg = torch.cat([module.p_out.weight, module.g_out.weight], 0)  # [256][128]
+        return dict(w_in=w_in.to(_BF16).contiguous(), w_out=w_out.to(_BF16).contiguous(),
+                    w_pg=w_pg.to(_BF16).contiguous())
 
     return _cached(module, "_bl_multiplication_weights", params, build)
 
@@ -207,16 +209,16 @@ def triangle_multiplication_forward(self, x, mask, use_kernels=False, residual=N
         call("bl_batched_gemm", a.data_ptr(), mn, n_pad, plane, bp.data_ptr(), mn, n_pad, plane, prod.data_ptr(),
              n_pad, plane, 128, n, n, n, None, stream)
         del a, bp, planes
-        normed = torch.empty(rows, 128, device=x.device, dtype=_BF16)
-        call("bl_layernorm_planes", prod.data_ptr(), n, n_pad, _f32(self.norm_out.weight).data_ptr(),
-             _f32(self.norm_out.bias).data_ptr(), float(self.norm_out.eps), normed.data_ptr(), _lib.BL_BF16, stream)
-        del prod
-        # y = bf16(p_out(normed)) * bf16(sigmoid(g_out(xn))) in one GEMM (K = 256).
+        # LayerNorm over the product's channel planes, p_out, g_out(x_hat), the
+        # gate and the residual add in one kernel.
+        norm = self.norm_out
+        args = (prod.data_ptr(), n, n_pad, _f32(norm.weight).data_ptr(), _f32(norm.bias).data_ptr(),
+                float(norm.eps), xn.data_ptr(), w["w_pg"].data_ptr())
         if residual is not None:
-            _linear_out(normed, w["w_out"], rows, 256, stream, a2=xn, k1=128, gate=True,
-                        residual=residual[b].view(rows, 128))
+            call("bl_trimul_output", *args, residual[b].data_ptr(), None, stream)
         else:
-            _linear_out(normed, w["w_out"], rows, 256, stream, a2=xn, k1=128, gate=True, out=out[b].view(rows, 128))
+            call("bl_trimul_output", *args, None, out[b].data_ptr(), stream)
+        del prod
     return residual if residual is not None else out
 
 

@@ -246,6 +246,21 @@ BL_API int bl_pair_transition(const float *x, int64_t rows, const float *ln_weig
                               float eps, const void *w12, const void *w3, float *z, void *out, void *stream);
 
 /*
+ * Output stage of the triangle multiplication:
+ *   o_hat = bf16(LayerNorm(O)) over the 128 channels of the product planes
+ *           prod bf16 [128][n][ld] (O_c[i][j] at c*n*ld + i*ld + j),
+ *   y = bf16(bf16(o_hat p_out^T) * bf16(sigmoid(bf16(x_hat g_out^T))))
+ * with x_hat = xn bf16 [n*n][128] and w_out = bf16 [256][128] (p_out rows then
+ * g_out rows); then z += y (fp32 [n*n][128]) or out = y (bf16), exactly one
+ * non-NULL.  ld is a multiple of 8, pointers 16-byte aligned.  Replaces
+ * norm_out + p_out + g_out + the gate of multiplication.py:124-137 and the
+ * Pairformer's residual add.
+ */
+BL_API int bl_trimul_output(const void *prod, int64_t n, int64_t ld, const float *ln_weight,
+                            const float *ln_bias, float eps, const void *xn, const void *w_out, float *z,
+                            void *out, void *stream);
+
+/*
  * Pair-transition activation on the joint fc1|fc2 projection:
  *   out[r][c] = bf16(bf16(silu(x[r][c])) * x[r][width + c]).
  * Replaces kernels/pair_hip.cu:42 `pair_silu_mul` on separate fc1/fc2
