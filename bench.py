@@ -204,12 +204,6 @@ def algorithmic_work(name, a):
         size = {0: 4, 1: 2}
         rows, cols = a[2], a[3]
         return "bytes", rows * cols * (size[a[1]] + size[a[9]]), f"bl_layernorm[rows={rows},cols={cols}]"
-    if name == "bl_layernorm_planes":
-        n, out_size = a[1], 2 if a[7] == 1 else 4
-        return "bytes", n * n * 128 * (2 + out_size), f"bl_layernorm_planes[n={n}]"
-    if name == "bl_trimul_pack_planes":
-        n, plane_ld = a[3], a[4]
-        return "bytes", n * n * (512 * 2 + 4) + 2 * 128 * n * plane_ld * 2, f"bl_trimul_pack_planes[n={n}]"
     if name == "bl_swiglu_rows":
         rows, width = a[2], a[3]
         return "bytes", rows * width * 6, f"bl_swiglu_rows[rows={rows},width={width}]"

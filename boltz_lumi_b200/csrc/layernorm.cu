@@ -144,59 +144,6 @@ __global__ void __launch_bounds__(256) layernorm_channel_first_kernel(const Tin 
   }
 }
 
-// LayerNorm of fp32 pair rows [n*n, 128] -> bf16 rows, fused with the triangle
-// bias projection (128 -> heads, bias-free, bf16 operands, fp32 accumulation):
-//   bias[h][r][s] = bf16(sum_c bf16(ln(x[r, s]))_c * w[h][c])     (transpose = 0)
-//   bias[h][s][r] = same                                           (transpose = 1)
-// One warp per pair row; lane holds channels 4*lane .. 4*lane+3.
-template <int HEADS>
-__global__ void layernorm_heads_kernel(const float *x, int n, const float *w, const float *b, float eps,
-                                       const __nv_bfloat16 *w_heads, int transpose, __nv_bfloat16 *out,
-                                       __nv_bfloat16 *bias, int64_t ld) {
-  const int lane = threadIdx.x & 31;
-  const int warps = blockDim.x >> 5;
-  const int64_t rows = int64_t(n) * n;
-  float wl[4], bl_[4], wh[HEADS][4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    wl[e] = w ? w[lane * 4 + e] : 1.f;
-    bl_[e] = b ? b[lane * 4 + e] : 0.f;
-#pragma unroll
-    for (int hh = 0; hh < HEADS; ++hh) wh[hh][e] = __bfloat162float(w_heads[hh * 128 + lane * 4 + e]);
-  }
-  const int64_t plane = int64_t(n) * ld;
-  for (int64_t row = blockIdx.x * int64_t(warps) + (threadIdx.x >> 5); row < rows;
-       row += int64_t(gridDim.x) * warps) {
-    float v[4];
-    Vec4<float>::load(x + row * 128 + lane * 4, v);
-    const float mean = warp_sum((v[0] + v[1]) + (v[2] + v[3])) * (1.f / 128.f);
-    float sq = 0.f;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float d = v[e] - mean;
-      sq += d * d;
-    }
-    const float rstd = rsqrtf(warp_sum(sq) * (1.f / 128.f) + eps);
-    float y[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) y[e] = bf16r((v[e] - mean) * rstd * wl[e] + bl_[e]);
-    Vec4<__nv_bfloat16>::store(out + row * 128 + lane * 4, y);
-    float dots[HEADS];
-#pragma unroll
-    for (int hh = 0; hh < HEADS; ++hh)
-      dots[hh] = warp_sum((y[0] * wh[hh][0] + y[1] * wh[hh][1]) + (y[2] * wh[hh][2] + y[3] * wh[hh][3]));
-    if (lane < HEADS) {
-      float d = dots[0];
-#pragma unroll
-      for (int hh = 1; hh < HEADS; ++hh)
-        if (lane == hh) d = dots[hh];
-      const int64_t r = row / n, s = row % n;
-      const int64_t at = transpose ? s * ld + r : r * ld + s;
-      bias[lane * plane + at] = __float2bfloat16_rn(d);
-    }
-  }
-}
-
 template <typename Tin, typename Tout>
 static int launch_channel_first(const Tin *x, int64_t rows, int64_t inner, int64_t ld, int64_t plane,
                                 const float *w, const float *b, float eps, Tout *out, cudaStream_t s) {
@@ -269,33 +216,4 @@ extern "C" int bl_layernorm(const void *x, int x_dtype, int64_t rows, int64_t co
                             static_cast<float *>(out), s);
   return launch_layernorm(static_cast<const __nv_bfloat16 *>(x), rows, cols, channel_first, weight, bias, eps,
                           static_cast<__nv_bfloat16 *>(out), s);
-}
-
-extern "C" int bl_layernorm_heads(const float *x, int64_t n, const float *weight, const float *bias, float eps,
-                                  const void *w_heads, int64_t heads, int transpose, void *out, void *bias_planes,
-                                  int64_t ld, void *stream) {
-  BL_REQUIRE(heads == 4, "bl_layernorm_heads: 4 heads supported");
-  BL_REQUIRE(n >= 0 && n <= 65535 && ld >= n && eps > 0.f, "bl_layernorm_heads: bad shape");
-  if (n == 0) return BL_OK;
-  BL_REQUIRE(x && w_heads && out && bias_planes, "bl_layernorm_heads: null pointer");
-  BL_REQUIRE(aligned_to(x, 16) && aligned_to(out, 8), "bl_layernorm_heads: misaligned rows");
-  int64_t rows = n * n, blocks = (rows + 7) / 8, cap = int64_t(num_sms()) * 16;
-  layernorm_heads_kernel<4><<<int(blocks < cap ? blocks : cap), 256, 0, as_stream(stream)>>>(
-      x, int(n), weight, bias, eps, static_cast<const __nv_bfloat16 *>(w_heads), transpose,
-      static_cast<__nv_bfloat16 *>(out), static_cast<__nv_bfloat16 *>(bias_planes), ld);
-  BL_LAUNCH_CHECK();
-  return BL_OK;
-}
-
-extern "C" int bl_layernorm_planes(const void *planes, int64_t n, int64_t ld, const float *weight, const float *bias,
-                                   float eps, void *out, int out_dtype, void *stream) {
-  BL_REQUIRE(out_dtype == BL_F32 || out_dtype == BL_BF16, "bl_layernorm_planes: bad output dtype");
-  BL_REQUIRE(n >= 0 && ld >= n && eps > 0.f, "bl_layernorm_planes: bad shape");
-  if (n == 0) return BL_OK;
-  BL_REQUIRE(planes && out, "bl_layernorm_planes: null pointer");
-  auto x = static_cast<const __nv_bfloat16 *>(planes);
-  auto s = as_stream(stream);
-  if (out_dtype == BL_F32)
-    return launch_channel_first(x, n * n, n, ld, n * ld, weight, bias, eps, static_cast<float *>(out), s);
-  return launch_channel_first(x, n * n, n, ld, n * ld, weight, bias, eps, static_cast<__nv_bfloat16 *>(out), s);
 }

@@ -1,61 +1,10 @@
-// Pair-track layout kernels that sit between the tensor-core GEMMs of the
-// triangle multiplication and the pair transition.
+// SwiGLU over the joint fc1|fc2 rows of the unfused pair transition (the
+// shapes the fused transition kernel does not cover, and the allocation-free
+// entry point).
 #include "common.cuh"
 
 namespace bl {
 namespace {
-
-__device__ __forceinline__ float gate_value(float p, float g) { return bf16r(p * bf16r(sigmoidf_fast(g))); }
-
-// Gate + mask the joint projection of a triangle multiplication and write the
-// two operands as natural channel-first planes:
-//   a[c][r][s] = bf16(bf16(p[r,s,c] * bf16(sigmoid(g[r,s,c]))) * mask[r,s])      c < 128
-//   b[c][r][s] = same with channel 128 + c
-// (multiplication_gate_hip.cu:16-20,41-42; einsum operands of multiplication.py).
-// One CTA: one row r, 64 consecutive s, all 256 channels.
-constexpr int kPlaneTile = 64;
-
-__global__ void __launch_bounds__(256) pack_planes_kernel(const __nv_bfloat16 *pg, int64_t pg_ld, const float *mask,
-                                                          int n, int64_t plane_ld, __nv_bfloat16 *a,
-                                                          __nv_bfloat16 *b) {
-  __shared__ __nv_bfloat16 tile[256][kPlaneTile + 2];
-  const int r = blockIdx.y, s0 = blockIdx.x * kPlaneTile;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Each warp gates 8 pairs; lane covers channels 8*lane .. 8*lane+7 of p and g.
-  for (int ps = warp; ps < kPlaneTile; ps += 8) {
-    const int s = s0 + ps;
-    float v[8];
-    if (s < n) {
-      const int64_t pair = int64_t(r) * n + s;
-      const float m = mask[pair];
-      const __nv_bfloat16 *row = pg + pair * pg_ld;
-      uint4 pv = *reinterpret_cast<const uint4 *>(row + lane * 8);
-      uint4 gv = *reinterpret_cast<const uint4 *>(row + 256 + lane * 8);
-      const uint32_t *p32 = &pv.x, *g32 = &gv.x;
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        v[2 * w] = bf16r(gate_value(bf16_lo(p32[w]), bf16_lo(g32[w])) * m);
-        v[2 * w + 1] = bf16r(gate_value(bf16_hi(p32[w]), bf16_hi(g32[w])) * m);
-      }
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = 0.f;
-    }
-#pragma unroll
-    for (int e = 0; e < 8; ++e) tile[lane * 8 + e][ps] = __float2bfloat16_rn(v[e]);
-  }
-  __syncthreads();
-  // Each warp writes channel rows: 64 s values = 128 B per channel.
-  const int64_t plane = int64_t(n) * plane_ld;
-  for (int c = warp; c < 256; c += 8) {
-    __nv_bfloat16 *dst = (c < 128 ? a + int64_t(c) * plane : b + int64_t(c - 128) * plane) + int64_t(r) * plane_ld;
-    for (int ps = lane; ps < kPlaneTile; ps += 32) {
-      const int s = s0 + ps;
-      if (s < n) dst[s] = tile[c][ps];
-      else if (s < plane_ld) dst[s] = __float2bfloat16_rn(0.f);
-    }
-  }
-}
 
 // out[r][c] = bf16(bf16(silu(x[r][c])) * x[r][w + c]) for the joint fc1|fc2
 // projection of the pair transition (pair_transition.py:20-28, pair_hip.cu:12-17).
@@ -85,21 +34,6 @@ __global__ void swiglu_rows_vec_kernel(const __nv_bfloat16 *x, int64_t x_ld, int
 }  // namespace bl
 
 using namespace bl;
-
-extern "C" int bl_trimul_pack_planes(const void *pg, int64_t pg_ld, const float *mask, int64_t n, int64_t plane_ld,
-                                     void *a_planes, void *b_planes, void *stream) {
-  BL_REQUIRE(n >= 0 && n <= 65535, "bl_trimul_pack_planes: bad token count");
-  if (n == 0) return BL_OK;
-  BL_REQUIRE(pg && mask && a_planes && b_planes, "bl_trimul_pack_planes: null pointer");
-  BL_REQUIRE(pg_ld >= 512 && pg_ld % 8 == 0 && aligned_to(pg, 16), "bl_trimul_pack_planes: projection rows must be 16-byte aligned and hold p|g");
-  BL_REQUIRE(plane_ld >= n, "bl_trimul_pack_planes: plane row stride too small");
-  dim3 grid(unsigned((n + kPlaneTile - 1) / kPlaneTile), unsigned(n));
-  pack_planes_kernel<<<grid, 256, 0, as_stream(stream)>>>(static_cast<const __nv_bfloat16 *>(pg), pg_ld, mask, int(n),
-                                                          plane_ld, static_cast<__nv_bfloat16 *>(a_planes),
-                                                          static_cast<__nv_bfloat16 *>(b_planes));
-  BL_LAUNCH_CHECK();
-  return BL_OK;
-}
 
 extern "C" int bl_swiglu_rows(const void *x, int64_t x_ld, int64_t rows, int64_t width, void *out, int64_t out_ld,
                               void *stream) {

@@ -418,31 +418,6 @@ bool pair_rows_map(CUtensorMap *map, const void *base, int64_t ld, int64_t so, i
   return encode_tmap(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
-// Bias planes from the pair-major projection: natural[h][r][s] = tb[r*n + s][h]
-// (starting node) or transposed[h][s][r] (ending node), rows padded to `ld`
-// with zeros.
-__global__ void bias_planes_kernel(const __nv_bfloat16 *tb, int64_t tb_ld, int heads, int n, int transpose,
-                                   __nv_bfloat16 *out, int64_t ld) {
-  __shared__ __nv_bfloat16 tile[32][33];
-  const int r0 = blockIdx.y * 32, s0 = blockIdx.x * 32, h = blockIdx.z;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
-  for (int y = ty; y < 32; y += 8) {
-    int r = r0 + y, s = s0 + tx;
-    tile[y][tx] = (r < n && s < n) ? tb[(int64_t(r) * n + s) * tb_ld + h] : __float2bfloat16_rn(0.f);
-  }
-  __syncthreads();
-  __nv_bfloat16 *plane = out + int64_t(h) * n * ld;
-  for (int y = ty; y < 32; y += 8) {
-    if (!transpose) {
-      int r = r0 + y, s = s0 + tx;
-      if (r < n && s < ld) plane[int64_t(r) * ld + s] = tile[y][tx];
-    } else {
-      int row = s0 + y, col = r0 + tx;  // out[s][r]
-      if (row < n && col < ld) plane[int64_t(row) * ld + col] = tile[tx][y];
-    }
-  }
-}
-
 }  // namespace
 }  // namespace bl
 
@@ -490,19 +465,6 @@ extern "C" int bl_triangle_attention(const void *q, const void *k, const void *v
   BL_CUDA(ensure_smem_limit(reinterpret_cast<const void *>(tri_flash_tc_kernel), 232448));
   dim3 grid(unsigned((n + kBQ - 1) / kBQ * kHeads), unsigned(n));
   tri_flash_tc_kernel<<<grid, kThreads, smem, as_stream(stream)>>>(map_q, map_k, map_v, map_bias, args);
-  BL_LAUNCH_CHECK();
-  return BL_OK;
-}
-
-extern "C" int bl_triangle_bias_planes(const void *tb, int64_t tb_ld, int64_t heads, int64_t n, int transpose,
-                                       void *out, int64_t ld, void *stream) {
-  BL_REQUIRE(n >= 0 && heads > 0 && heads <= 64, "bl_triangle_bias_planes: bad shape");
-  if (n == 0) return BL_OK;
-  BL_REQUIRE(tb && out, "bl_triangle_bias_planes: null pointer");
-  BL_REQUIRE(ld >= n && ld <= (n + 31) / 32 * 32 && tb_ld >= heads, "bl_triangle_bias_planes: bad leading dimension");
-  dim3 grid((n + 31) / 32, (n + 31) / 32, heads);
-  bias_planes_kernel<<<grid, 256, 0, as_stream(stream)>>>(static_cast<const __nv_bfloat16 *>(tb), tb_ld, int(heads),
-                                                         int(n), transpose, static_cast<__nv_bfloat16 *>(out), ld);
   BL_LAUNCH_CHECK();
   return BL_OK;
 }

@@ -168,38 +168,6 @@ BL_API int bl_linear_fused(const void *a, int64_t a_ld, const void *a2, int64_t 
                            int64_t out_ld, void *stream);
 
 /*
- * LayerNorm over 128 channel planes (bf16 [128][n][ld], the per-channel
- * matmul output of the triangle multiplication) into pair rows [n*n, 128].
- * Replaces the channel-first norm call of multiplication.py:124-133.
- */
-BL_API int bl_layernorm_planes(const void *planes, int64_t n, int64_t ld, const float *weight,
-                               const float *bias, float eps, void *out, int out_dtype, void *stream);
-
-/*
- * LayerNorm of fp32 pair rows x [n*n, 128] to bf16 rows `out`, fused with the
- * bias-free triangle-bias projection (bf16 weights w_heads [heads][128]):
- *   bias[h][r][s] = bf16(bf16(ln(x[r*n+s])) . w_heads[h])   (transpose = 0)
- *   bias[h][s][r] = same                                    (transpose = 1, ending node)
- * with bias planes of row stride ld.  Replaces the layer_norm fast path
- * (triangle.py:107-146) plus upstream's `linear` + permute_final_dims that
- * build tri_bias for triangle.py:32.  heads must be 4.
- */
-BL_API int bl_layernorm_heads(const float *x, int64_t n, const float *weight, const float *bias, float eps,
-                              const void *w_heads, int64_t heads, int transpose, void *out,
-                              void *bias_planes, int64_t ld, void *stream);
-
-/*
- * Gate + mask the joint p|g projection (bf16 rows of pg_ld >= 512 elements:
- * p in columns 0..255, g in 256..511) into natural channel-first planes
- * a, b: bf16 [128][n][plane_ld], a[c][r][s] = bf16(gate(p, g)[r, s, c] * mask[r, s]).
- * Replaces the gate/pack/split + layout-copy stage of multiplication.py:103-119;
- * the outgoing and incoming products then read the same planes K-major or
- * MN-major (bl_batched_gemm) instead of transposed copies.
- */
-BL_API int bl_trimul_pack_planes(const void *pg, int64_t pg_ld, const float *mask, int64_t n,
-                                 int64_t plane_ld, void *a_planes, void *b_planes, void *stream);
-
-/*
  * Triangle-attention input stage in one pass over the fp32 pair rows
  * x [n*n][128] (16-byte aligned):
  *   x_hat = bf16(LayerNorm(x))                                  (fp32 statistics)
@@ -268,16 +236,6 @@ BL_API int bl_trimul_output(const void *prod, int64_t n, int64_t ld, const float
  */
 BL_API int bl_swiglu_rows(const void *x, int64_t x_ld, int64_t rows, int64_t width, void *out,
                           int64_t out_ld, void *stream);
-
-/*
- * Triangle-bias planes from the pair-major projection tb (bf16, head h in
- * column h of rows of tb_ld): out[h][r][s] = tb[r*n + s][h], or the transpose
- * out[h][s][r] for the ending node; rows padded to ld (>= n).
- * Replaces the permute_final_dims of upstream TriangleAttention.forward that
- * feeds tri_bias into triangle.py:32.
- */
-BL_API int bl_triangle_bias_planes(const void *tb, int64_t tb_ld, int64_t heads, int64_t n,
-                                   int transpose, void *out, int64_t ld, void *stream);
 
 /*
  * Flash triangle attention with fused output gate (bf16):
