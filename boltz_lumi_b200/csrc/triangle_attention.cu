@@ -74,7 +74,7 @@ struct TcArgs {
   int64_t ld, so, si;
   const float *mask;
   int64_t ms_o, ms_k;
-  float inf, q_divisor;
+  float inf, q_scale;  // q_scale = fp32(1 / fp32(sqrt(d)))
   __nv_bfloat16 *out;
   int64_t out_ld;
   int n;
@@ -95,6 +95,11 @@ __device__ __forceinline__ uint32_t max_bf16x2(uint32_t a, uint32_t b) {
   uint32_t r;
   asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
+}
+__device__ __forceinline__ float fast_rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
@@ -259,8 +264,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t o_base = lane_base + kOCol + half * kOStride;
     float m_ref = -INFINITY;  // reference maximum of this half-row's exponentials
     // Upstream divides q by sqrt(d) after the projection and rounds to bf16
-    // (_prep_qkv(apply_scale=True), triangle.py:80): apply it to this thread's
-    // half of its Q row in place (elementwise, so the swizzle does not matter).
+    // (_prep_qkv(apply_scale=True), triangle.py:80); torch's CUDA division by a
+    // host scalar multiplies by the fp32 reciprocal, as done here on this
+    // thread's half of its Q row in place (elementwise: the swizzle does not matter).
     bool ok = warp_wait(q_full, 0, args.status, 0x20B);
     if (ok) {
       uint4 *q_row = reinterpret_cast<uint4 *>(smem + kQOff + row * 64) + half * 2;
@@ -270,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         uint32_t *w = &v.x;
 #pragma unroll
         for (int e = 0; e < 4; ++e)
-          w[e] = pack_bf16x2(__fdiv_rn(bf16_lo(w[e]), args.q_divisor), __fdiv_rn(bf16_hi(w[e]), args.q_divisor));
+          w[e] = pack_bf16x2(bf16_lo(w[e]) * args.q_scale, bf16_hi(w[e]) * args.q_scale);
         q_row[c] = v;
       }
       tc::fence_proxy_async_smem();
@@ -289,19 +295,32 @@ __global__ void __launch_bounds__(kThreads, 2)
       // Ordered rounding: t = bf16(bf16(bf16(s) + mask) + bias), packed per key pair.
       const int k0 = j * kBK + half * 32;
       const uint8_t *bias_row = smem + kStageOff + s * kStageBytes + kKBytes + kVBytes + row * 128;
-      const bool masked = tile_masked[j] != 0;
+      // 16-byte bias chunk c = keys 8c .. 8c + 7 of this half (128-byte swizzled row).
+      uint32_t bw[16];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 bv = *reinterpret_cast<const uint4 *>(bias_row + (((half * 4 + c) ^ (row & 7)) << 4));
+        bw[4 * c] = bv.x, bw[4 * c + 1] = bv.y, bw[4 * c + 2] = bv.z, bw[4 * c + 3] = bv.w;
+      }
+      // The mask term is uniform per key tile: two straight-line versions
+      // (a per-pair branch would split the unrolled block).
       uint32_t t[16];
+      if (tile_masked[j] == 0) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {  // 16-byte chunk = keys 8c .. 8c + 7 of this half
-        const int chunk = half * 4 + c;
-        const uint4 bv = *reinterpret_cast<const uint4 *>(bias_row + ((chunk ^ (row & 7)) << 4));
-        const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+        for (int pr = 0; pr < 16; ++pr)
+          t[pr] = add_bf16x2(cvt_bf16x2(__uint_as_float(sv[2 * pr]), __uint_as_float(sv[2 * pr + 1])), bw[pr]);
+      } else {
+        const uint4 *mb = reinterpret_cast<const uint4 *>(mask_bias + k0);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int pr = c * 4 + e;
-          uint32_t x = cvt_bf16x2(__uint_as_float(sv[2 * pr]), __uint_as_float(sv[2 * pr + 1]));
-          if (masked) x = add_bf16x2(x, *reinterpret_cast<const uint32_t *>(mask_bias + k0 + 2 * pr));
-          t[pr] = add_bf16x2(x, bw[e]);
+        for (int c = 0; c < 4; ++c) {
+          const uint4 m4 = mb[c];
+          const uint32_t mw[4] = {m4.x, m4.y, m4.z, m4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int pr = 4 * c + e;
+            const uint32_t x = cvt_bf16x2(__uint_as_float(sv[2 * pr]), __uint_as_float(sv[2 * pr + 1]));
+            t[pr] = add_bf16x2(add_bf16x2(x, mw[e]), bw[pr]);
+          }
         }
       }
       // Keys past n: excluded from the maximum here and zeroed in P below.
@@ -380,7 +399,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc::tmem_ld_wait();
       const int qi = q0 + row;
       if (qi < n) {
-        const float inv = 1.f / (__uint_as_float(l0[0]) * a0 + __uint_as_float(l1[0]) * a1);
+        const float inv = fast_rcp(__uint_as_float(l0[0]) * a0 + __uint_as_float(l1[0]) * a1);
         const int64_t pair = int64_t(outer) * args.so + int64_t(qi) * args.si;
         const uint4 *g4 = reinterpret_cast<const uint4 *>(args.g + pair * args.ld + h * kD + half * 16);
         uint4 *o4 = reinterpret_cast<uint4 *>(args.out + pair * args.out_ld + h * kD + half * 16);
@@ -394,7 +413,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int d = c * 8 + e * 2;
             const float v0 = (__uint_as_float(o0[d]) * a0 + __uint_as_float(o1[d]) * a1) * inv;
             const float v1 = (__uint_as_float(o0[d + 1]) * a0 + __uint_as_float(o1[d + 1]) * a1) * inv;
-            const float g0 = bf16r(sigmoidf_fast(bf16_lo(gw[e]))), g1 = bf16r(sigmoidf_fast(bf16_hi(gw[e])));
+            const float g0 = bf16r(fast_rcp(1.f + fast_exp2(bf16_lo(gw[e]) * -kLog2e)));
+            const float g1 = bf16r(fast_rcp(1.f + fast_exp2(bf16_hi(gw[e]) * -kLog2e)));
             w[e] = pack_bf16x2(bf16r(v0) * g0, bf16r(v1) * g1);
           }
           o4[c] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -454,7 +474,7 @@ extern "C" int bl_triangle_attention(const void *q, const void *k, const void *v
   args.ld = ld, args.so = so, args.si = si;
   args.mask = mask, args.ms_o = ms_o, args.ms_k = ms_k;
   args.inf = inf;
-  args.q_divisor = sqrtf(float(head_dim));
+  args.q_scale = 1.f / sqrtf(float(head_dim));
   args.out = static_cast<__nv_bfloat16 *>(out);
   args.out_ld = out_ld;
   args.n = int(n);
