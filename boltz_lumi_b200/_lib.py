@@ -41,6 +41,7 @@ SIGNATURES = {
     "bl_trimul_projection": [_p, c_int64, _p, _p, c_float, _p, _p, _p, c_int64, _p, _p],
     "bl_pair_transition": [_p, c_int64, _p, _p, c_float, _p, _p, _p, _p, _p],
     "bl_trimul_output": [_p, c_int64, c_int64, _p, _p, c_float, _p, _p, _p, _p, _p],
+    "bl_pair_bias": [_p, c_int64, _p, _p, c_float, _p, c_int64, _p, _p],
     "bl_swiglu_rows": [_p, c_int64, c_int64, c_int64, _p, c_int64, _p],
     "bl_triangle_attention": [_p, _p, _p, _p, c_int64, c_int64, c_int64, _p, c_int64, c_int64, _p, c_int64,
                               c_int64, c_float, c_int64, c_int64, c_int64, _p, c_int64, _p],

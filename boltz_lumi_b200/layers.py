@@ -12,7 +12,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
-from . import forwards, kernels
+from . import _lib, forwards, kernels
 
 
 def _inference_only(module):
@@ -147,19 +147,45 @@ class AttentionPairBias(nn.Module):
             self.proj_z = nn.Sequential(nn.LayerNorm(c_z), nn.Linear(c_z, num_heads, bias=False))
         self.proj_o = nn.Linear(c_s, c_s, bias=False)
 
+    def _joint_weights(self):
+        params = (self.proj_q.weight, self.proj_q.bias, self.proj_k.weight, self.proj_v.weight, self.proj_g.weight)
+
+        def build():
+            w = torch.cat([self.proj_q.weight, self.proj_k.weight, self.proj_v.weight, self.proj_g.weight], 0)
+            bias = torch.zeros(w.shape[0], device=w.device, dtype=w.dtype)
+            if self.proj_q.bias is not None:
+                bias[: self.c_s] = self.proj_q.bias
+            return dict(w=w.contiguous(), b=bias)
+
+        return forwards._cached(self, "_bl_joint_qkvg", params, build)
+
     def forward(self, s, z, mask, k_in):
         _inference_only(self)
         b = s.shape[0]
-        q = F.linear(s, self.proj_q.weight, self.proj_q.bias).view(b, -1, self.num_heads, self.head_dim)
-        k = F.linear(k_in, self.proj_k.weight).view(b, -1, self.num_heads, self.head_dim)
-        v = F.linear(k_in, self.proj_v.weight).view(b, -1, self.num_heads, self.head_dim)
+        if k_in is s:  # one GEMM for q | k | v | g (the block passes the same normed s)
+            joint = self._joint_weights()
+            q, k, v, g = F.linear(s, joint["w"], joint["b"]).split(self.c_s, dim=-1)
+        else:
+            q = F.linear(s, self.proj_q.weight, self.proj_q.bias)
+            k, v = F.linear(k_in, self.proj_k.weight), F.linear(k_in, self.proj_v.weight)
+            g = F.linear(s, self.proj_g.weight)
+        q = q.reshape(b, -1, self.num_heads, self.head_dim)
+        k = k.reshape(b, -1, self.num_heads, self.head_dim)
+        v = v.reshape(b, -1, self.num_heads, self.head_dim)
         if self.compute_pair_bias:
+            # LayerNorm(z) . W_z in one pass, written head-major [b, heads, N, N].
             ln, lin = self.proj_z[0], self.proj_z[1]
-            zn = kernels.layer_norm(z.float().contiguous(), ln.weight, ln.bias, ln.eps, out_dtype=torch.float32)
-            bias = F.linear(zn, lin.weight).permute(0, 3, 1, 2)
+            n = z.shape[1]
+            zf = z.float().contiguous()
+            bias = torch.empty(b, self.num_heads, n, n, device=z.device, dtype=torch.float32)
+            w_z = lin.weight.float().contiguous()
+            stream = torch.cuda.current_stream(z.device).cuda_stream
+            for i in range(b):
+                _lib.call("bl_pair_bias", zf[i].data_ptr(), n * n, _lib.ptr(ln.weight), _lib.ptr(ln.bias),
+                          float(ln.eps), w_z.data_ptr(), self.num_heads, bias[i].data_ptr(), stream)
         else:
             bias = z
-        g = torch.sigmoid(F.linear(s, self.proj_g.weight))
+        g = torch.sigmoid(g)
         attn = torch.einsum("bihd,bjhd->bhij", q, k) / math.sqrt(self.head_dim) + bias
         attn = attn + (1 - mask[:, None, None].float()) * -self.inf
         o = torch.einsum("bhij,bjhd->bihd", attn.softmax(dim=-1), v).reshape(b, -1, self.c_s)
@@ -173,8 +199,10 @@ class _FP32Transition(Transition):
         _inference_only(self)
         xn = kernels.layer_norm(x.contiguous(), self.norm.weight, self.norm.bias, self.norm.eps,
                                 out_dtype=torch.float32)
-        h = F.silu(F.linear(xn, self.fc1.weight)) * F.linear(xn, self.fc2.weight)
-        return F.linear(h, self.fc3.weight)
+        w12 = forwards._cached(self, "_bl_fc12", (self.fc1.weight, self.fc2.weight),
+                               lambda: torch.cat([self.fc1.weight, self.fc2.weight], 0).contiguous())
+        a, b = F.linear(xn, w12).split(self.fc1.weight.shape[0], dim=-1)
+        return F.linear(F.silu(a) * b, self.fc3.weight)
 
 
 class PairformerLayer(nn.Module):

@@ -229,6 +229,16 @@ BL_API int bl_trimul_output(const void *prod, int64_t n, int64_t ld, const float
                             void *out, void *stream);
 
 /*
+ * Pair bias of the single-track attention, fp32, in one pass over z:
+ *   out[h][r] = sum_c LayerNorm(z[r])[c] * w[h][c]     z [rows][128], w [heads][128], heads <= 16
+ * (the LayerNorm has fp32 statistics and optional affine ln_weight/ln_bias).
+ * Replaces upstream AttentionPairBias.proj_z (LayerNorm -> Linear(c_z, heads,
+ * bias=False) -> permute to [heads, N, N]) of the Pairformer block.
+ */
+BL_API int bl_pair_bias(const float *z, int64_t rows, const float *ln_weight, const float *ln_bias, float eps,
+                        const float *w, int64_t heads, float *out, void *stream);
+
+/*
  * Pair-transition activation on the joint fc1|fc2 projection:
  *   out[r][c] = bf16(bf16(silu(x[r][c])) * x[r][width + c]).
  * Replaces kernels/pair_hip.cu:42 `pair_silu_mul` on separate fc1/fc2

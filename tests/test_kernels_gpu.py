@@ -43,6 +43,24 @@ def test_layer_norm_rows(cols, in_dtype, out_dtype):
         assert_close(actual.float(), numerics.bf16_round(expected), atol=1e-6, rtol=2 * BF16_ULP)
 
 
+@pytest.mark.parametrize("rows,heads", [(1, 16), (1001, 16), (4096, 4), (37, 1)])
+def test_pair_bias(rows, heads):
+    """bl_pair_bias = LayerNorm(z) . W^T in fp32, written head-major [heads][rows]."""
+    from boltz_lumi_b200 import _lib
+
+    g = gen(7)
+    z = torch.randn(rows, 128, generator=g) * 2 + 0.3
+    w_ln, b_ln = torch.randn(128, generator=g) * 0.1 + 1, torch.randn(128, generator=g) * 0.1
+    w = torch.randn(heads, 128, generator=g) * 128 ** -0.5
+    expected = (torch.nn.functional.layer_norm(z.double(), (128,), w_ln.double(), b_ln.double(), 1e-5)
+                @ w.double().T).T.float()
+    out = torch.empty(heads, rows, device="cuda")
+    zc, wc, w_lnc, b_lnc = z.cuda(), w.cuda(), w_ln.cuda(), b_ln.cuda()  # referenced until the call returns
+    _lib.call("bl_pair_bias", zc.data_ptr(), rows, w_lnc.data_ptr(), b_lnc.data_ptr(), 1e-5,
+              wc.data_ptr(), heads, out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert_close(out.cpu(), expected, atol=1e-5, rtol=1e-5)
+
+
 @pytest.mark.parametrize("m", [1, 17, 1000, 4099])
 def test_norm_channel_first(m):
     g = gen(2)
