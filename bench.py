@@ -209,6 +209,23 @@ def algorithmic_work(name, a):
         return "bytes", rows * width * 6, f"bl_swiglu_rows[rows={rows},width={width}]"
     if name == "bl_gate":
         return "bytes", a[3] * 6, f"bl_gate[n={a[3]}]"
+    # Fused pair kernels: bytes each must move per pair row (128 channels).
+    if name == "bl_attention_projection":  # fp32 row in, q|k|v|g bf16 out, 4 bf16 bias values
+        n = a[1]
+        return "bytes", n * n * (512 + 1024 + 8), f"bl_attention_projection[n={n}]"
+    if name == "bl_trimul_projection":  # fp32 row in, 256 gated channels + x_hat (bf16) out
+        n = a[1]
+        return "bytes", n * n * (512 + 512 + 256), f"bl_trimul_projection[n={n}]"
+    if name == "bl_trimul_output":  # 128 plane values + x_hat in, z read-modify-write (or bf16 out)
+        n = a[1]
+        out = 1024 if a[8] else 256
+        return "bytes", n * n * (256 + 256 + out), f"bl_trimul_output[n={n}]"
+    if name == "bl_pair_transition":  # LN read + z read-modify-write (or bf16 out)
+        rows = a[1]
+        return "bytes", rows * (512 + (1024 if a[7] else 256)), f"bl_pair_transition[rows={rows}]"
+    if name == "bl_pair_bias":
+        rows, heads = a[1], a[6]
+        return "bytes", rows * (512 + 4 * heads), f"bl_pair_bias[rows={rows},heads={heads}]"
     return "bytes", 0.0, name
 
 
