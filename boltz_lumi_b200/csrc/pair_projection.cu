@@ -7,6 +7,8 @@
 //
 //   attention (triangle.py:32-104 / upstream TriangleAttention.forward):
 //     proj[r] = bf16(x_hat[r] W^T + bias)       W = [linear_q; linear_k; linear_v; linear_g]
+//     written as q_s | k | v | s_g with q_s = bf16(q * q_scale) (q / sqrt(d),
+//     _prep_qkv) and s_g = bf16(sigmoid(g)) (upstream _wrap_up's gate)
 //     tri_bias[h][q][k] = bf16(x_hat[(q, k)] . w_heads[h])   (transposed planes for the ending node)
 //   triangle multiplication (multiplication.py:48-120, multiplication_gate_hip.cu:16-20,41-58):
 //     a|b[c][i][k] = bf16(bf16(p_c * bf16(sigmoid(g_c))) * mask[i, k])   p = p_in(x_hat), g = g_in(x_hat)
@@ -70,6 +72,7 @@ struct ProjArgs {
   float eps;
   // attention
   const float *bias;  // [512] fp32 or null
+  float q_scale;      // applied to columns 0..127 (q)
   const __nv_bfloat16 *w_heads;  // [4][128]
   int transpose;
   __nv_bfloat16 *bias_planes;  // [4][n][bias_ld]
@@ -127,6 +130,29 @@ __device__ __forceinline__ float sigmoid_mufu(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(x * -1.4426950408889634f));
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.f + e));
   return r;
+}
+
+// One staged row of 64 projection columns (two 32-column TMEM loads) with the
+// bias added and rounded to bf16; KIND 1 then scales by q_scale and rounds,
+// KIND 2 applies the sigmoid and rounds.
+template <int KIND>
+__device__ __forceinline__ void stage_row(uint8_t *buf, int lane, const uint32_t (&r0)[32], const uint32_t (&r1)[32],
+                                          const float4 *bq, float q_scale) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const uint32_t *r = e < 4 ? r0 + 8 * e : r1 + 8 * (e - 4);
+    const float4 b0 = bq[2 * e], b1 = bq[2 * e + 1];
+    uint32_t w[4] = {cvt_bf16x2(__uint_as_float(r[0]) + b0.x, __uint_as_float(r[1]) + b0.y),
+                     cvt_bf16x2(__uint_as_float(r[2]) + b0.z, __uint_as_float(r[3]) + b0.w),
+                     cvt_bf16x2(__uint_as_float(r[4]) + b1.x, __uint_as_float(r[5]) + b1.y),
+                     cvt_bf16x2(__uint_as_float(r[6]) + b1.z, __uint_as_float(r[7]) + b1.w)};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if constexpr (KIND == 1) w[k] = cvt_bf16x2(bf16_lo(w[k]) * q_scale, bf16_hi(w[k]) * q_scale);
+      if constexpr (KIND == 2) w[k] = cvt_bf16x2(sigmoid_mufu(bf16_lo(w[k])), sigmoid_mufu(bf16_hi(w[k])));
+    }
+    *reinterpret_cast<uint4 *>(buf + lane * 128 + ((e ^ (lane & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
 }
 
 // One step of a butterfly reduce-scatter over N values per lane: lanes with
@@ -275,17 +301,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint8_t *buf = stage + (count & 1) * 4096;
             if (lane == 0) tc::bulk_wait_read<1>();
             __syncwarp();
-            // 16-byte chunk e of the staged row = columns 8 e .. 8 e + 7.
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const uint32_t *r = e < 4 ? r0 + 8 * e : r1 + 8 * (e - 4);
-              const float4 b0 = bq[2 * e], b1 = bq[2 * e + 1];
-              *reinterpret_cast<uint4 *>(buf + lane * 128 + ((e ^ (lane & 7)) * 16)) =
-                  make_uint4(cvt_bf16x2(__uint_as_float(r[0]) + b0.x, __uint_as_float(r[1]) + b0.y),
-                             cvt_bf16x2(__uint_as_float(r[2]) + b0.z, __uint_as_float(r[3]) + b0.w),
-                             cvt_bf16x2(__uint_as_float(r[4]) + b1.x, __uint_as_float(r[5]) + b1.y),
-                             cvt_bf16x2(__uint_as_float(r[6]) + b1.z, __uint_as_float(r[7]) + b1.w));
-            }
+            // 16-byte chunk e of the staged row = columns 8 e .. 8 e + 7.  q
+            // (chunk 0) leaves scaled, bf16(bf16(q) * q_scale); g (chunk 3)
+            // leaves activated, bf16(sigmoid(bf16(g + b))): the flash kernel's
+            // operands, with upstream's rounding points.
+            if (j == 0)
+              stage_row<1>(buf, lane, r0, r1, bq, args.q_scale);
+            else if (j == 3)
+              stage_row<2>(buf, lane, r0, r1, bq, args.q_scale);
+            else
+              stage_row<0>(buf, lane, r0, r1, bq, args.q_scale);
             tc::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
@@ -564,9 +589,9 @@ int check_common(const float *x, int64_t n, float eps, const void *w) {
 using namespace bl;
 
 extern "C" int bl_attention_projection(const float *x, int64_t n, const float *ln_weight, const float *ln_bias,
-                                       float eps, const void *w, const float *bias, const void *w_heads,
-                                       int transpose, void *proj, int64_t proj_ld, void *bias_planes,
-                                       int64_t bias_ld, void *stream) {
+                                       float eps, const void *w, const float *bias, float q_scale,
+                                       const void *w_heads, int transpose, void *proj, int64_t proj_ld,
+                                       void *bias_planes, int64_t bias_ld, void *stream) {
   if (n == 0) return BL_OK;
   if (int rc = check_common(x, n, eps, w)) return rc;
   BL_REQUIRE(w_heads && proj && bias_planes, "bl_attention_projection: null pointer");
@@ -588,7 +613,8 @@ extern "C" int bl_attention_projection(const float *x, int64_t n, const float *l
   a.x = x, a.rows = n * n, a.n = int(n);
   a.tiles = int((a.rows + kRows - 1) / kRows), a.tiles_per_i = 0;
   a.ln_w = ln_weight, a.ln_b = ln_bias, a.eps = eps;
-  a.bias = bias, a.w_heads = static_cast<const __nv_bfloat16 *>(w_heads), a.transpose = transpose != 0;
+  a.bias = bias, a.q_scale = q_scale;
+  a.w_heads = static_cast<const __nv_bfloat16 *>(w_heads), a.transpose = transpose != 0;
   a.bias_planes = static_cast<__nv_bfloat16 *>(bias_planes), a.bias_ld = bias_ld;
   a.status = device_status_ptr();
   BL_REQUIRE(a.status, "bl_attention_projection: device status word unavailable");

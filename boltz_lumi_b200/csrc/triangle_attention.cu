@@ -4,7 +4,10 @@
 //   s(b, c) = bf16(q_s(a, b) . k(a, c))                    q_s = bf16(q / sqrt(d))
 //   t(b, c) = bf16(bf16(s + inf * (mask(a, c) - 1)) + bias(h, b, c))
 //   o(a, b) = bf16(sum_c softmax_c(t) v(a, c))
-//   out(a, b) = bf16(o * bf16(sigmoid(g(a, b))))
+//   out(a, b) = bf16(o * s_g(a, b))                         s_g = bf16(sigmoid(g))
+// q_s and s_g arrive prepared (the projection kernel writes them), so the
+// kernel reads Q straight into the first MMA and the gate straight into the
+// epilogue.
 // This is the reference's ordered_triangle_forward (triangle.py:32-104 and
 // kernels/triangle_softmax.py:90-113) plus upstream _wrap_up's gate, without
 // materialising the [I, H, N, N] scores.  The ending node is the same
@@ -74,7 +77,7 @@ struct TcArgs {
   int64_t ld, so, si;
   const float *mask;
   int64_t ms_o, ms_k;
-  float inf, q_scale;  // q_scale = fp32(1 / fp32(sqrt(d)))
+  float inf;
   __nv_bfloat16 *out;
   int64_t out_ld;
   int n;
@@ -95,6 +98,27 @@ __device__ __forceinline__ uint32_t max_bf16x2(uint32_t a, uint32_t b) {
   uint32_t r;
   asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
+}
+// Shared-memory reads through 32-bit shared addresses (the generic pointer
+// arithmetic on the aligned dynamic window would otherwise hide the state space).
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ int lds32(uint32_t addr) {
+  int v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+// (x.lo, x.hi) * (s, s) + (c, c) on the packed fp32x2 pipe (sm_100).
+__device__ __forceinline__ void fma_f32x2(float &lo, float &hi, float s, float c) {
+  uint64_t x = (uint64_t(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+  const uint64_t sv = (uint64_t(__float_as_uint(s)) << 32) | __float_as_uint(s);
+  const uint64_t cv = (uint64_t(__float_as_uint(c)) << 32) | __float_as_uint(c);
+  asm("fma.rn.f32x2 %0, %0, %1, %2;" : "+l"(x) : "l"(sv), "l"(cv));
+  lo = __uint_as_float(uint32_t(x));
+  hi = __uint_as_float(uint32_t(x >> 32));
 }
 __device__ __forceinline__ float fast_rcp(float x) {
   float y;
@@ -124,9 +148,9 @@ __global__ void __launch_bounds__(kThreads, 2)
                         const TcArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t smem_base = tc::smem_u32(smem);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBarOff);
   uint64_t *q_full = bars + 0;
-  uint64_t *q_ready = bars + 1;              // Q scaled in place by the softmax warps
   uint64_t *st_full = bars + 2;              // [kStages] K, V, bias of a key tile landed
   uint64_t *st_empty = bars + 2 + kStages;   // [kStages] P.V of that tile completed
   uint64_t *s_full = bars + 2 + 2 * kStages; // [2] S tile in TMEM
@@ -148,7 +172,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (tid < kMaxTiles) tile_masked[tid] = 0;
   if (tid == 0) {
     tc::mbar_init(q_full, 1);
-    tc::mbar_init(q_ready, kSoftmaxWarps);
     for (int s = 0; s < kStages; ++s) {
       tc::mbar_init(&st_full[s], 1);
       tc::mbar_init(&st_empty[s], 1);
@@ -187,13 +210,19 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc::tma_load_3d(stage + kKBytes + kVBytes, &map_bias, &st_full[j], j * kBK, q0, h);
     }
   }
-  // Mask bias of this outer row (bf16; for mask in {0, 1} adding it rounds
-  // exactly like the fp32 value) and per-tile "any key masked" flags.
-  for (int key = tid; key < n_tiles * kBK; key += kThreads) {
-    const float mb =
-        key < n ? args.inf * (args.mask[int64_t(outer) * args.ms_o + int64_t(key) * args.ms_k] - 1.f) : 0.f;
-    mask_bias[key] = __float2bfloat16_rn(mb);
-    if (mb != 0.f) atomicOr(&tile_masked[key / kBK], 1);
+  // Mask bias of this outer row, 4 keys per thread (bf16; for mask in {0, 1}
+  // adding it rounds exactly like the fp32 value), and per-tile "any key
+  // masked" flags.
+  for (int k4 = tid * 4; k4 < n_tiles * kBK; k4 += kThreads * 4) {
+    float mb[4];
+    const float *mrow = args.mask + int64_t(outer) * args.ms_o;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int key = k4 + e;
+      mb[e] = key < n ? args.inf * (__ldg(mrow + int64_t(key) * args.ms_k) - 1.f) : 0.f;
+    }
+    *reinterpret_cast<uint2 *>(mask_bias + k4) = make_uint2(pack_bf16x2(mb[0], mb[1]), pack_bf16x2(mb[2], mb[3]));
+    if (mb[0] != 0.f || mb[1] != 0.f || mb[2] != 0.f || mb[3] != 0.f) atomicOr(&tile_masked[k4 / kBK], 1);
   }
   tc::fence_proxy_async_smem();
   tc::tc_fence_before();
@@ -221,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       constexpr uint32_t idesc_pv = tc::idesc_bf16(128, 48, false, true);
       const uint32_t q_addr = tc::smem_u32(smem + kQOff);
       const uint32_t ones_addr = tc::smem_u32(smem + kOnesOff);
-      bool ok = tc::mbar_wait(q_ready, 0, args.status, 0x202);
+      bool ok = tc::mbar_wait(q_full, 0, args.status, 0x202);
       auto issue_s = [&](int j) {
         const int s = j % kStages, b = j & 1;
         if (!tc::mbar_wait(&st_full[s], (j / kStages) & 1, args.status, 0x203)) return false;
@@ -263,26 +292,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
     const uint32_t o_base = lane_base + kOCol + half * kOStride;
     float m_ref = -INFINITY;  // reference maximum of this half-row's exponentials
-    // Upstream divides q by sqrt(d) after the projection and rounds to bf16
-    // (_prep_qkv(apply_scale=True), triangle.py:80); torch's CUDA division by a
-    // host scalar multiplies by the fp32 reciprocal, as done here on this
-    // thread's half of its Q row in place (elementwise: the swizzle does not matter).
-    bool ok = warp_wait(q_full, 0, args.status, 0x20B);
-    if (ok) {
-      uint4 *q_row = reinterpret_cast<uint4 *>(smem + kQOff + row * 64) + half * 2;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint4 v = q_row[c];
-        uint32_t *w = &v.x;
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          w[e] = pack_bf16x2(bf16_lo(w[e]) * args.q_scale, bf16_hi(w[e]) * args.q_scale);
-        q_row[c] = v;
-      }
-      tc::fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(q_ready);
-    }
+    bool ok = true;
     for (int j = 0; j < n_tiles && ok; ++j) {
       const int s = j % kStages, b = j & 1;
       if (!(ok = warp_wait(&s_full[b], (j >> 1) & 1, args.status, 0x206))) break;
@@ -294,26 +304,25 @@ __global__ void __launch_bounds__(kThreads, 2)
 
       // Ordered rounding: t = bf16(bf16(bf16(s) + mask) + bias), packed per key pair.
       const int k0 = j * kBK + half * 32;
-      const uint8_t *bias_row = smem + kStageOff + s * kStageBytes + kKBytes + kVBytes + row * 128;
+      const uint32_t bias_row = smem_base + kStageOff + s * kStageBytes + kKBytes + kVBytes + row * 128;
       // 16-byte bias chunk c = keys 8c .. 8c + 7 of this half (128-byte swizzled row).
       uint32_t bw[16];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        const uint4 bv = *reinterpret_cast<const uint4 *>(bias_row + (((half * 4 + c) ^ (row & 7)) << 4));
+        const uint4 bv = lds128(bias_row + (((half * 4 + c) ^ (row & 7)) << 4));
         bw[4 * c] = bv.x, bw[4 * c + 1] = bv.y, bw[4 * c + 2] = bv.z, bw[4 * c + 3] = bv.w;
       }
       // The mask term is uniform per key tile: two straight-line versions
       // (a per-pair branch would split the unrolled block).
       uint32_t t[16];
-      if (tile_masked[j] == 0) {
+      if (lds32(smem_base + kFlagOff + 4 * j) == 0) {
 #pragma unroll
         for (int pr = 0; pr < 16; ++pr)
           t[pr] = add_bf16x2(cvt_bf16x2(__uint_as_float(sv[2 * pr]), __uint_as_float(sv[2 * pr + 1])), bw[pr]);
       } else {
-        const uint4 *mb = reinterpret_cast<const uint4 *>(mask_bias + k0);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          const uint4 m4 = mb[c];
+          const uint4 m4 = lds128(smem_base + kMaskOff + 2 * k0 + 16 * c);
           const uint32_t mw[4] = {m4.x, m4.y, m4.z, m4.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -366,8 +375,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       // P (bf16x2 per key pair) over the first 16 columns of this S half.
       uint32_t p[16];
 #pragma unroll
-      for (int pr = 0; pr < 16; ++pr)
-        p[pr] = cvt_bf16x2(fast_exp2(fmaf(bf16_lo(t[pr]), kLog2e, -ml)), fast_exp2(fmaf(bf16_hi(t[pr]), kLog2e, -ml)));
+      for (int pr = 0; pr < 16; ++pr) {
+        float x0 = bf16_lo(t[pr]), x1 = bf16_hi(t[pr]);
+        fma_f32x2(x0, x1, kLog2e, -ml);
+        p[pr] = cvt_bf16x2(fast_exp2(x0), fast_exp2(x1));
+      }
       if (tail) {
 #pragma unroll
         for (int pr = 0; pr < 16; ++pr) {
@@ -413,8 +425,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int d = c * 8 + e * 2;
             const float v0 = (__uint_as_float(o0[d]) * a0 + __uint_as_float(o1[d]) * a1) * inv;
             const float v1 = (__uint_as_float(o0[d + 1]) * a0 + __uint_as_float(o1[d + 1]) * a1) * inv;
-            const float g0 = bf16r(fast_rcp(1.f + fast_exp2(bf16_lo(gw[e]) * -kLog2e)));
-            const float g1 = bf16r(fast_rcp(1.f + fast_exp2(bf16_hi(gw[e]) * -kLog2e)));
+            const float g0 = bf16_lo(gw[e]), g1 = bf16_hi(gw[e]);  // bf16(sigmoid(g)) from the projection
             w[e] = pack_bf16x2(bf16r(v0) * g0, bf16r(v1) * g1);
           }
           o4[c] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -474,7 +485,6 @@ extern "C" int bl_triangle_attention(const void *q, const void *k, const void *v
   args.ld = ld, args.so = so, args.si = si;
   args.mask = mask, args.ms_o = ms_o, args.ms_k = ms_k;
   args.inf = inf;
-  args.q_scale = 1.f / sqrtf(float(head_dim));
   args.out = static_cast<__nv_bfloat16 *>(out);
   args.out_ld = out_ld;
   args.n = int(n);

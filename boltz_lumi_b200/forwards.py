@@ -23,6 +23,8 @@ from . import _lib, kernels
 from ._lib import call, stream_of
 
 _BF16 = torch.bfloat16
+# fp32(1 / fp32(sqrt(32))): the factor torch's CUDA kernel applies for q / sqrt(32).
+_Q_SCALE = float(torch.tensor(1.0, dtype=torch.float32) / torch.tensor(32.0, dtype=torch.float32).sqrt())
 
 def _pad8(n):
     return (n + 7) // 8 * 8
@@ -128,13 +130,15 @@ def triangle_attention_forward(self, x, mask=None, chunk_size=None, use_kernels=
     for b in range(batch):
         xb = x[b].reshape(rows, 128).float().contiguous()
         bias = torch.empty(4, n, n_pad, device=x.device, dtype=_BF16)
-        proj = torch.empty(rows, 512, device=x.device, dtype=_BF16)  # q | k | v | g (+ g bias)
+        proj = torch.empty(rows, 512, device=x.device, dtype=_BF16)  # q_s | k | v | sigmoid(g)
         # LayerNorm, the q/k/v/g projection and the 128 -> 4 triangle-bias
         # projection in one pass; bias planes are [h][query][key] (transposed
         # for the ending node).
+        # q leaves as bf16(q * fp32(1 / sqrt(32))) (torch's CUDA division by a
+        # host scalar) and g as bf16(sigmoid(g)).
         call("bl_attention_projection", xb.data_ptr(), n, _f32(ln.weight).data_ptr(), _f32(ln.bias).data_ptr(),
-             float(ln.eps), w["w_in"].data_ptr(), w["b_in"].data_ptr(), w["w_heads"].data_ptr(), int(not starting),
-             proj.data_ptr(), 512, bias.data_ptr(), n_pad, stream)
+             float(ln.eps), w["w_in"].data_ptr(), w["b_in"].data_ptr(), _Q_SCALE, w["w_heads"].data_ptr(),
+             int(not starting), proj.data_ptr(), 512, bias.data_ptr(), n_pad, stream)
         gated = torch.empty(rows, 128, device=x.device, dtype=_BF16)
         so, si = (n, 1) if starting else (1, n)
         ms_o, ms_k = (n, 1) if starting else (1, n)

@@ -171,7 +171,8 @@ BL_API int bl_linear_fused(const void *a, int64_t a_ld, const void *a2, int64_t 
  * Triangle-attention input stage in one pass over the fp32 pair rows
  * x [n*n][128] (16-byte aligned):
  *   x_hat = bf16(LayerNorm(x))                                  (fp32 statistics)
- *   proj[r][0:512] = bf16(x_hat[r] . w^T + bias)                w bf16 [512][128] = q | k | v | g rows
+ *   y[r][0:512] = bf16(x_hat[r] . w^T + bias)                   w bf16 [512][128] = q | k | v | g rows
+ *   proj[r] = bf16(y_q * q_scale) | y_k | y_v | bf16(sigmoid(y_g))  (the flash kernel's operands)
  *   bias_planes[h][q][k] = bf16(x_hat[q*n + k] . w_heads[h])    (transpose = 0, starting node)
  *   bias_planes[h][k][q] = same                                 (transpose = 1, ending node)
  * bias (fp32 [512]) may be NULL; w_heads is bf16 [4][128]; proj rows are
@@ -181,9 +182,9 @@ BL_API int bl_linear_fused(const void *a, int64_t a_ld, const void *a2, int64_t 
  * triangle-bias `linear` that feed ordered_triangle_forward (triangle.py:32).
  */
 BL_API int bl_attention_projection(const float *x, int64_t n, const float *ln_weight, const float *ln_bias,
-                                   float eps, const void *w, const float *bias, const void *w_heads,
-                                   int transpose, void *proj, int64_t proj_ld, void *bias_planes,
-                                   int64_t bias_ld, void *stream);
+                                   float eps, const void *w, const float *bias, float q_scale,
+                                   const void *w_heads, int transpose, void *proj, int64_t proj_ld,
+                                   void *bias_planes, int64_t bias_ld, void *stream);
 
 /*
  * Triangle-multiplication input stage in one pass over the fp32 pair rows
@@ -249,10 +250,11 @@ BL_API int bl_swiglu_rows(const void *x, int64_t x_ld, int64_t rows, int64_t wid
 
 /*
  * Flash triangle attention with fused output gate (bf16):
- *   out(a, b) = bf16(bf16(softmax_c(bf16(bf16(q_s . k + inf*(mask-1)) + bias)) v)
- *                    * bf16(sigmoid(g)))
- * Replaces triangle.py:139 `ordered_triangle_forward` (q k^T, ordered bias
- * softmax, p v) and the gate of upstream Attention._wrap_up.  q, k, v, g:
+ *   out(a, b) = bf16(bf16(softmax_c(bf16(bf16(bf16(q_s . k) + inf*(mask-1)) + bias)) v) * s_g)
+ * where q_s = bf16(q / sqrt(32)) and s_g = bf16(sigmoid(g)) are passed in
+ * already prepared (bl_attention_projection writes them).  Replaces
+ * triangle.py:139 `ordered_triangle_forward` (q k^T, ordered bias softmax,
+ * p v) and the gate of upstream Attention._wrap_up.  q_s, k, v, s_g:
  * bf16 pair rows of ld elements, head h at columns h*32..h*32+31, pair row of
  * (outer a, inner b) = a*so + b*si (starting node: so = n, si = 1; ending
  * node: so = 1, si = n).  bias(h, b, c) at bias + h*bias_hs + b*bias_ld + c.
