@@ -198,8 +198,10 @@ def algorithmic_work(name, a):
         batch, m, n, k = a[11], a[12], a[13], a[14]
         return "flops", 2.0 * batch * m * n * k, f"bl_batched_gemm[b={batch},m={m},n={n},k={k}]"
     if name == "bl_triangle_attention":
-        heads, d, n = a[14], a[15], a[16]
-        return "flops", 4.0 * n ** 3 * heads * d, f"bl_triangle_attention[n={n},heads={heads},d={d}]"
+        heads, d, n, n_outer = a[14], a[15], a[16], a[17]
+        label = f"bl_triangle_attention[n={n},heads={heads},d={d}]" if n_outer == n else \
+            f"bl_triangle_attention[n={n},n_outer={n_outer},heads={heads},d={d}]"
+        return "flops", 4.0 * n * n * n_outer * heads * d, label
     if name == "bl_layernorm":
         size = {0: 4, 1: 2}
         rows, cols = a[2], a[3]
@@ -211,15 +213,15 @@ def algorithmic_work(name, a):
         return "bytes", a[3] * 6, f"bl_gate[n={a[3]}]"
     # Fused pair kernels: bytes each must move per pair row (128 channels).
     if name == "bl_attention_projection":  # fp32 row in, q|k|v|g bf16 out, 4 bf16 bias values
-        n = a[1]
-        return "bytes", n * n * (512 + 1024 + 8), f"bl_attention_projection[n={n}]"
+        n, rows = a[1], a[1] * a[2]
+        return "bytes", rows * (512 + 1024 + 8), f"bl_attention_projection[n={n}]"
     if name == "bl_trimul_projection":  # fp32 row in, 256 gated channels + x_hat (bf16) out
-        n = a[1]
-        return "bytes", n * n * (512 + 512 + 256), f"bl_trimul_projection[n={n}]"
+        n, rows = a[1], a[1] * a[2]
+        return "bytes", rows * (512 + 512 + 256), f"bl_trimul_projection[n={n}]"
     if name == "bl_trimul_output":  # 128 plane values + x_hat in, z read-modify-write (or bf16 out)
-        n = a[1]
-        out = 1024 if a[8] else 256
-        return "bytes", n * n * (256 + 256 + out), f"bl_trimul_output[n={n}]"
+        n, rows = a[1], a[1] * a[2]
+        out = 1024 if a[9] else 256
+        return "bytes", rows * (256 + 256 + out), f"bl_trimul_output[n={n}]"
     if name == "bl_pair_transition":  # LN read + z read-modify-write (or bf16 out)
         rows = a[1]
         return "bytes", rows * (512 + (1024 if a[7] else 256)), f"bl_pair_transition[rows={rows}]"

@@ -37,15 +37,15 @@ SIGNATURES = {
                         c_int64, c_int64, c_int64, c_int64, _p, _p],
     "bl_linear_fused": [_p, c_int64, _p, c_int64, c_int64, _p, c_int64, c_int64, c_int64, c_int64, _p, c_int, _p,
                         c_int64, _p, c_int64, _p],
-    "bl_attention_projection": [_p, c_int64, _p, _p, c_float, _p, _p, c_float, _p, c_int, _p, c_int64, _p, c_int64,
-                                _p],
-    "bl_trimul_projection": [_p, c_int64, _p, _p, c_float, _p, _p, _p, c_int64, _p, _p],
+    "bl_attention_projection": [_p, c_int64, c_int64, _p, _p, c_float, _p, _p, c_float, _p, c_int, _p, c_int64, _p,
+                                c_int64, c_int64, _p],
+    "bl_trimul_projection": [_p, c_int64, c_int64, _p, _p, c_float, _p, _p, _p, c_int64, _p, _p],
     "bl_pair_transition": [_p, c_int64, _p, _p, c_float, _p, _p, _p, _p, _p],
-    "bl_trimul_output": [_p, c_int64, c_int64, _p, _p, c_float, _p, _p, _p, _p, _p],
+    "bl_trimul_output": [_p, c_int64, c_int64, c_int64, _p, _p, c_float, _p, _p, _p, _p, _p],
     "bl_pair_bias": [_p, c_int64, _p, _p, c_float, _p, c_int64, _p, _p],
     "bl_swiglu_rows": [_p, c_int64, c_int64, c_int64, _p, c_int64, _p],
     "bl_triangle_attention": [_p, _p, _p, _p, c_int64, c_int64, c_int64, _p, c_int64, c_int64, _p, c_int64,
-                              c_int64, c_float, c_int64, c_int64, c_int64, _p, c_int64, _p],
+                              c_int64, c_float, c_int64, c_int64, c_int64, c_int64, _p, c_int64, _p],
     "bl_pair_transition_static": [_p, c_int64, _p, _p, c_float, _p, _p, _p, _p],
 }
 _RESTYPES = {"bl_last_error": ctypes.c_char_p}

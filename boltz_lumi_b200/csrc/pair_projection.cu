@@ -75,8 +75,8 @@ struct ProjArgs {
   float q_scale;      // applied to columns 0..127 (q)
   const __nv_bfloat16 *w_heads;  // [4][128]
   int transpose;
-  __nv_bfloat16 *bias_planes;  // [4][n][bias_ld]
-  int64_t bias_ld;
+  __nv_bfloat16 *bias_planes;  // head h at bias_planes + h * bias_hs, rows of bias_ld
+  int64_t bias_ld, bias_hs;
   // triangle multiplication
   const float *mask;  // [rows]
   __nv_bfloat16 *xn;  // [rows][128]
@@ -429,7 +429,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // 16-byte chunk (lane % 16) / 2, byte (lane % 2) * 8 within it.
     const uint32_t a_lane_off = (lane >> 4) * kKBlockBytes + (lane & 1) * 8;
     const uint32_t a_chunk = (lane & 15) >> 1;
-    const int64_t plane = int64_t(args.n) * args.bias_ld;
     const int row_lo = lw * kLnRowsPerWarp;
 
     // Rows rbase .. rbase + 7 of tile t (zeros past the valid rows).
@@ -507,7 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int row = int(t.row0) + tr;  // n * n < 2^31
             const int q = row / args.n, k = row - q * args.n;
             const int64_t at = args.transpose ? int64_t(k) * args.bias_ld + q : int64_t(q) * args.bias_ld + k;
-            args.bias_planes[((lane >> 1) & 3) * plane + at] = __float2bfloat16_rn(d);
+            args.bias_planes[((lane >> 1) & 3) * args.bias_hs + at] = __float2bfloat16_rn(d);
           }
         }
       }
@@ -575,8 +574,8 @@ int launch_projection(const CUtensorMap &map_w, const CUtensorMap &map_out, cons
   return BL_OK;
 }
 
-int check_common(const float *x, int64_t n, float eps, const void *w) {
-  BL_REQUIRE(n >= 0 && n * n < (1ll << 31), "pair projection: bad n");
+int check_common(const float *x, int64_t n, int64_t n_outer, float eps, const void *w) {
+  BL_REQUIRE(n >= 0 && n_outer >= 0 && n_outer <= n && n * n < (1ll << 31), "pair projection: bad n / n_outer");
   BL_REQUIRE(eps > 0.f, "pair projection: eps must be positive");
   BL_REQUIRE(x && w, "pair projection: null pointer");
   BL_REQUIRE(aligned_to(x, 16) && aligned_to(w, 16), "pair projection: x and w must be 16-byte aligned");
@@ -588,21 +587,23 @@ int check_common(const float *x, int64_t n, float eps, const void *w) {
 
 using namespace bl;
 
-extern "C" int bl_attention_projection(const float *x, int64_t n, const float *ln_weight, const float *ln_bias,
-                                       float eps, const void *w, const float *bias, float q_scale,
-                                       const void *w_heads, int transpose, void *proj, int64_t proj_ld,
-                                       void *bias_planes, int64_t bias_ld, void *stream) {
-  if (n == 0) return BL_OK;
-  if (int rc = check_common(x, n, eps, w)) return rc;
+extern "C" int bl_attention_projection(const float *x, int64_t n, int64_t n_outer, const float *ln_weight,
+                                       const float *ln_bias, float eps, const void *w, const float *bias,
+                                       float q_scale, const void *w_heads, int transpose, void *proj,
+                                       int64_t proj_ld, void *bias_planes, int64_t bias_ld, int64_t bias_hs,
+                                       void *stream) {
+  if (n == 0 || n_outer == 0) return BL_OK;
+  if (int rc = check_common(x, n, n_outer, eps, w)) return rc;
   BL_REQUIRE(w_heads && proj && bias_planes, "bl_attention_projection: null pointer");
   BL_REQUIRE(aligned_to(w_heads, 8), "bl_attention_projection: w_heads must be 8-byte aligned");
   BL_REQUIRE(aligned_to(proj, 16) && proj_ld % 8 == 0 && proj_ld >= kOut,
              "bl_attention_projection: proj rows must be 16-byte aligned and >= 512 wide");
-  BL_REQUIRE(bias_ld >= n, "bl_attention_projection: bias_ld must be >= n");
+  BL_REQUIRE(transpose ? (bias_ld >= n_outer && bias_hs >= n * bias_ld) : (bias_ld >= n && bias_hs >= n_outer * bias_ld),
+             "bl_attention_projection: bias planes too small");
   CUtensorMap map_w, map_out;
   BL_REQUIRE(weight_map(&map_w, w), "bl_attention_projection: cannot encode the weight map");
   {
-    uint64_t dims[2] = {uint64_t(kOut), uint64_t(n * n)};
+    uint64_t dims[2] = {uint64_t(kOut), uint64_t(n_outer * n)};
     uint64_t strides[1] = {uint64_t(proj_ld) * 2};
     uint32_t box[2] = {64, 32};
     BL_REQUIRE(encode_tmap(&map_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, proj, dims, strides, box,
@@ -610,39 +611,39 @@ extern "C" int bl_attention_projection(const float *x, int64_t n, const float *l
                "bl_attention_projection: cannot encode the output map");
   }
   ProjArgs a{};
-  a.x = x, a.rows = n * n, a.n = int(n);
+  a.x = x, a.rows = n_outer * n, a.n = int(n);
   a.tiles = int((a.rows + kRows - 1) / kRows), a.tiles_per_i = 0;
   a.ln_w = ln_weight, a.ln_b = ln_bias, a.eps = eps;
   a.bias = bias, a.q_scale = q_scale;
   a.w_heads = static_cast<const __nv_bfloat16 *>(w_heads), a.transpose = transpose != 0;
-  a.bias_planes = static_cast<__nv_bfloat16 *>(bias_planes), a.bias_ld = bias_ld;
+  a.bias_planes = static_cast<__nv_bfloat16 *>(bias_planes), a.bias_ld = bias_ld, a.bias_hs = bias_hs;
   a.status = device_status_ptr();
   BL_REQUIRE(a.status, "bl_attention_projection: device status word unavailable");
   return launch_projection<PROJ_ATTENTION>(map_w, map_out, a, as_stream(stream));
 }
 
-extern "C" int bl_trimul_projection(const float *x, int64_t n, const float *ln_weight, const float *ln_bias,
-                                    float eps, const void *w, const float *mask, void *planes, int64_t plane_ld,
-                                    void *xn, void *stream) {
-  if (n == 0) return BL_OK;
-  if (int rc = check_common(x, n, eps, w)) return rc;
+extern "C" int bl_trimul_projection(const float *x, int64_t n, int64_t n_outer, const float *ln_weight,
+                                    const float *ln_bias, float eps, const void *w, const float *mask, void *planes,
+                                    int64_t plane_ld, void *xn, void *stream) {
+  if (n == 0 || n_outer == 0) return BL_OK;
+  if (int rc = check_common(x, n, n_outer, eps, w)) return rc;
   BL_REQUIRE(mask && planes && xn, "bl_trimul_projection: null pointer");
   BL_REQUIRE(aligned_to(planes, 16) && aligned_to(xn, 16) && plane_ld % 8 == 0 && plane_ld >= n,
              "bl_trimul_projection: planes need 16-byte alignment and plane_ld % 8 == 0, >= n");
   CUtensorMap map_w, map_out;
   BL_REQUIRE(weight_map(&map_w, w), "bl_trimul_projection: cannot encode the weight map");
   {
-    uint64_t dims[3] = {uint64_t(plane_ld), uint64_t(n), 256};
-    uint64_t strides[2] = {uint64_t(plane_ld) * 2, uint64_t(n) * uint64_t(plane_ld) * 2};
+    uint64_t dims[3] = {uint64_t(plane_ld), uint64_t(n_outer), 256};
+    uint64_t strides[2] = {uint64_t(plane_ld) * 2, uint64_t(n_outer) * uint64_t(plane_ld) * 2};
     uint32_t box[3] = {64, 1, 32};  // 64 pairs x 32 channels, 128-byte rows
     BL_REQUIRE(encode_tmap(&map_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, planes, dims, strides, box,
                            CU_TENSOR_MAP_SWIZZLE_128B),
                "bl_trimul_projection: cannot encode the plane map");
   }
   ProjArgs a{};
-  a.x = x, a.rows = n * n, a.n = int(n);
+  a.x = x, a.rows = n_outer * n, a.n = int(n);
   a.tiles_per_i = int((n + kRows - 1) / kRows);
-  a.tiles = int(n) * a.tiles_per_i;
+  a.tiles = int(n_outer) * a.tiles_per_i;
   a.ln_w = ln_weight, a.ln_b = ln_bias, a.eps = eps;
   a.mask = mask, a.xn = static_cast<__nv_bfloat16 *>(xn);
   a.status = device_status_ptr();

@@ -441,9 +441,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
-bool pair_rows_map(CUtensorMap *map, const void *base, int64_t ld, int64_t so, int64_t si, int n, int box_rows) {
+bool pair_rows_map(CUtensorMap *map, const void *base, int64_t ld, int64_t so, int64_t si, int n, int n_outer,
+                   int box_rows) {
   // Element (column c, inner b, outer a) at base + (a*so + b*si)*ld + c.
-  uint64_t dims[3] = {uint64_t(kHeads * kD), uint64_t(n), uint64_t(n)};
+  uint64_t dims[3] = {uint64_t(kHeads * kD), uint64_t(n), uint64_t(n_outer)};
   uint64_t strides[2] = {uint64_t(si * ld * 2), uint64_t(so * ld * 2)};
   uint32_t box[3] = {uint32_t(kD), uint32_t(box_rows), 1};
   return encode_tmap(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
@@ -457,10 +458,11 @@ using namespace bl;
 extern "C" int bl_triangle_attention(const void *q, const void *k, const void *v, const void *g, int64_t ld,
                                         int64_t so, int64_t si, const void *bias, int64_t bias_ld, int64_t bias_hs,
                                         const float *mask, int64_t ms_o, int64_t ms_k, float inf, int64_t heads,
-                                        int64_t head_dim, int64_t n, void *out, int64_t out_ld, void *stream) {
+                                        int64_t head_dim, int64_t n, int64_t n_outer, void *out, int64_t out_ld,
+                                        void *stream) {
   BL_REQUIRE(head_dim == kD && heads == kHeads, "bl_triangle_attention: 4 heads x 32 supported");
-  BL_REQUIRE(n >= 0, "bl_triangle_attention: bad shape");
-  if (n == 0) return BL_OK;
+  BL_REQUIRE(n >= 0 && n_outer >= 0 && n_outer <= n, "bl_triangle_attention: bad shape");
+  if (n == 0 || n_outer == 0) return BL_OK;
   BL_REQUIRE(n <= kMaxTiles * kBK, "bl_triangle_attention: at most 4096 tokens");
   BL_REQUIRE(q && k && v && g && bias && mask && out, "bl_triangle_attention: null pointer");
   BL_REQUIRE(ld % 8 == 0 && out_ld % 8 == 0 && bias_ld % 8 == 0 && bias_ld >= n && bias_hs % 8 == 0,
@@ -469,8 +471,9 @@ extern "C" int bl_triangle_attention(const void *q, const void *k, const void *v
                  aligned_to(bias, 16) && aligned_to(out, 16),
              "bl_triangle_attention: pointers must be 16-byte aligned");
   CUtensorMap map_q, map_k, map_v, map_bias;
-  BL_REQUIRE(pair_rows_map(&map_q, q, ld, so, si, int(n), kBQ) && pair_rows_map(&map_k, k, ld, so, si, int(n), kBK) &&
-                 pair_rows_map(&map_v, v, ld, so, si, int(n), kBK),
+  BL_REQUIRE(pair_rows_map(&map_q, q, ld, so, si, int(n), int(n_outer), kBQ) &&
+                 pair_rows_map(&map_k, k, ld, so, si, int(n), int(n_outer), kBK) &&
+                 pair_rows_map(&map_v, v, ld, so, si, int(n), int(n_outer), kBK),
              "bl_triangle_attention: cannot encode the q/k/v tensor maps");
   {
     uint64_t dims[3] = {uint64_t(bias_ld), uint64_t(n), uint64_t(kHeads)};
@@ -493,7 +496,7 @@ extern "C" int bl_triangle_attention(const void *q, const void *k, const void *v
   const int n_tiles = int((n + kBK - 1) / kBK);
   const int smem = kMaskOff + n_tiles * kBK * 2 + 1024;
   BL_CUDA(ensure_smem_limit(reinterpret_cast<const void *>(tri_flash_tc_kernel), 232448));
-  dim3 grid(unsigned((n + kBQ - 1) / kBQ * kHeads), unsigned(n));
+  dim3 grid(unsigned((n + kBQ - 1) / kBQ * kHeads), unsigned(n_outer));
   tri_flash_tc_kernel<<<grid, kThreads, smem, as_stream(stream)>>>(map_q, map_k, map_v, map_bias, args);
   BL_LAUNCH_CHECK();
   return BL_OK;

@@ -313,11 +313,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 using namespace bl;
 
-extern "C" int bl_trimul_output(const void *prod, int64_t n, int64_t ld, const float *ln_weight,
+extern "C" int bl_trimul_output(const void *prod, int64_t n, int64_t n_outer, int64_t ld, const float *ln_weight,
                                 const float *ln_bias, float eps, const void *xn, const void *w_out, float *z,
                                 void *out, void *stream) {
-  BL_REQUIRE(n >= 0 && n * n < (1ll << 31), "bl_trimul_output: bad n");
-  if (n == 0) return BL_OK;
+  BL_REQUIRE(n >= 0 && n_outer >= 0 && n_outer <= n && n * n < (1ll << 31), "bl_trimul_output: bad n / n_outer");
+  if (n == 0 || n_outer == 0) return BL_OK;
   BL_REQUIRE(prod && xn && w_out, "bl_trimul_output: null pointer");
   BL_REQUIRE((z != nullptr) != (out != nullptr), "bl_trimul_output: exactly one of z (residual) and out");
   BL_REQUIRE(ld >= n && ld % 8 == 0 && eps > 0.f, "bl_trimul_output: ld must be >= n and a multiple of 8");
@@ -334,7 +334,7 @@ extern "C" int bl_trimul_output(const void *prod, int64_t n, int64_t ld, const f
                "bl_trimul_output: cannot encode the weight map");
   }
   {
-    uint64_t dims[3] = {uint64_t(kC), uint64_t(n), uint64_t(n)};
+    uint64_t dims[3] = {uint64_t(kC), uint64_t(n), uint64_t(n_outer)};
     uint64_t strides[2] = {uint64_t(kC) * 2, uint64_t(n) * kC * 2};
     uint32_t box[3] = {64, 128, 1};
     BL_REQUIRE(encode_tmap(&map_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, xn, dims, strides, box,
@@ -342,14 +342,14 @@ extern "C" int bl_trimul_output(const void *prod, int64_t n, int64_t ld, const f
                "bl_trimul_output: cannot encode the x_hat map");
   }
   if (z) {
-    uint64_t dims[3] = {uint64_t(kC), uint64_t(n), uint64_t(n)};
+    uint64_t dims[3] = {uint64_t(kC), uint64_t(n), uint64_t(n_outer)};
     uint64_t strides[2] = {uint64_t(kC) * 4, uint64_t(n) * kC * 4};
     uint32_t box[3] = {32, 32, 1};
     BL_REQUIRE(encode_tmap(&map_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, z, dims, strides, box,
                            CU_TENSOR_MAP_SWIZZLE_128B),
                "bl_trimul_output: cannot encode the z map");
   } else {
-    uint64_t dims[3] = {uint64_t(kC), uint64_t(n), uint64_t(n)};
+    uint64_t dims[3] = {uint64_t(kC), uint64_t(n), uint64_t(n_outer)};
     uint64_t strides[2] = {uint64_t(kC) * 2, uint64_t(n) * kC * 2};
     uint32_t box[3] = {32, 32, 1};
     BL_REQUIRE(encode_tmap(&map_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, dims, strides, box,
@@ -358,9 +358,9 @@ extern "C" int bl_trimul_output(const void *prod, int64_t n, int64_t ld, const f
   }
   OutArgs a{};
   a.prod = static_cast<const __nv_bfloat16 *>(prod);
-  a.plane = n * ld, a.ld = ld, a.n = int(n);
+  a.plane = n_outer * ld, a.ld = ld, a.n = int(n);
   a.tiles_per_i = int((n + kRows - 1) / kRows);
-  a.tiles = int(n) * a.tiles_per_i;
+  a.tiles = int(n_outer) * a.tiles_per_i;
   a.eps = eps;
   a.residual = z != nullptr;
   a.status = device_status_ptr();

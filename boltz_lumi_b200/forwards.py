@@ -136,16 +136,16 @@ def triangle_attention_forward(self, x, mask=None, chunk_size=None, use_kernels=
         # for the ending node).
         # q leaves as bf16(q * fp32(1 / sqrt(32))) (torch's CUDA division by a
         # host scalar) and g as bf16(sigmoid(g)).
-        call("bl_attention_projection", xb.data_ptr(), n, _f32(ln.weight).data_ptr(), _f32(ln.bias).data_ptr(),
+        call("bl_attention_projection", xb.data_ptr(), n, n, _f32(ln.weight).data_ptr(), _f32(ln.bias).data_ptr(),
              float(ln.eps), w["w_in"].data_ptr(), w["b_in"].data_ptr(), _Q_SCALE, w["w_heads"].data_ptr(),
-             int(not starting), proj.data_ptr(), 512, bias.data_ptr(), n_pad, stream)
+             int(not starting), proj.data_ptr(), 512, bias.data_ptr(), n_pad, n * n_pad, stream)
         gated = torch.empty(rows, 128, device=x.device, dtype=_BF16)
         so, si = (n, 1) if starting else (1, n)
         ms_o, ms_k = (n, 1) if starting else (1, n)
         base = proj.data_ptr()
         call("bl_triangle_attention", base, base + 128 * 2, base + 256 * 2, base + 384 * 2, width, so, si,
              bias.data_ptr(), n_pad, n * n_pad, mask[b].data_ptr(), ms_o, ms_k, float(getattr(self, "inf", 1e9)),
-             4, 32, n, gated.data_ptr(), 128, stream)
+             4, 32, n, n, gated.data_ptr(), 128, stream)
         del proj, bias
         if residual is not None:
             _linear_out(gated, w["w_out"], rows, 128, stream, bias=w["b_out"], residual=residual[b].view(rows, 128))
@@ -201,7 +201,7 @@ def triangle_multiplication_forward(self, x, mask, use_kernels=False, residual=N
         planes = torch.empty(256, n, n_pad, device=x.device, dtype=_BF16)
         # LayerNorm, p_in | g_in, the sigmoid gate and the mask in one pass,
         # written as channel planes a = planes[:128], b = planes[128:].
-        call("bl_trimul_projection", xb.data_ptr(), n, _f32(self.norm_in.weight).data_ptr(),
+        call("bl_trimul_projection", xb.data_ptr(), n, n, _f32(self.norm_in.weight).data_ptr(),
              _f32(self.norm_in.bias).data_ptr(), float(self.norm_in.eps), w["w_in"].data_ptr(), mask[b].data_ptr(),
              planes.data_ptr(), n_pad, xn.data_ptr(), stream)
         a, bp = planes[:128], planes[128:]
@@ -216,7 +216,7 @@ def triangle_multiplication_forward(self, x, mask, use_kernels=False, residual=N
         # LayerNorm over the product's channel planes, p_out, g_out(x_hat), the
         # gate and the residual add in one kernel.
         norm = self.norm_out
-        args = (prod.data_ptr(), n, n_pad, _f32(norm.weight).data_ptr(), _f32(norm.bias).data_ptr(),
+        args = (prod.data_ptr(), n, n, n_pad, _f32(norm.weight).data_ptr(), _f32(norm.bias).data_ptr(),
                 float(norm.eps), xn.data_ptr(), w["w_pg"].data_ptr())
         if residual is not None:
             call("bl_trimul_output", *args, residual[b].data_ptr(), None, stream)

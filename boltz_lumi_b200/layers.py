@@ -159,8 +159,26 @@ class AttentionPairBias(nn.Module):
 
         return forwards._cached(self, "_bl_joint_qkvg", params, build)
 
+    def pair_bias(self, z):
+        """LayerNorm(z) . W_z in one pass, head-major [b, heads, N, N] (fp32)."""
+        ln, lin = self.proj_z[0], self.proj_z[1]
+        b, n = z.shape[0], z.shape[1]
+        zf = z.float().contiguous()
+        bias = torch.empty(b, self.num_heads, n, n, device=z.device, dtype=torch.float32)
+        w_z = lin.weight.float().contiguous()
+        stream = torch.cuda.current_stream(z.device).cuda_stream
+        for i in range(b):
+            _lib.call("bl_pair_bias", zf[i].data_ptr(), n * n, _lib.ptr(ln.weight), _lib.ptr(ln.bias),
+                      float(ln.eps), w_z.data_ptr(), self.num_heads, bias[i].data_ptr(), stream)
+        return bias
+
     def forward(self, s, z, mask, k_in):
         _inference_only(self)
+        bias = self.pair_bias(z) if self.compute_pair_bias else z
+        return self.attend(s, bias, mask, k_in)
+
+    def attend(self, s, bias, mask, k_in):
+        """The attention given the pair bias [b, heads, N, N] (fp32)."""
         b = s.shape[0]
         if k_in is s:  # one GEMM for q | k | v | g (the block passes the same normed s)
             joint = self._joint_weights()
@@ -172,19 +190,6 @@ class AttentionPairBias(nn.Module):
         q = q.reshape(b, -1, self.num_heads, self.head_dim)
         k = k.reshape(b, -1, self.num_heads, self.head_dim)
         v = v.reshape(b, -1, self.num_heads, self.head_dim)
-        if self.compute_pair_bias:
-            # LayerNorm(z) . W_z in one pass, written head-major [b, heads, N, N].
-            ln, lin = self.proj_z[0], self.proj_z[1]
-            n = z.shape[1]
-            zf = z.float().contiguous()
-            bias = torch.empty(b, self.num_heads, n, n, device=z.device, dtype=torch.float32)
-            w_z = lin.weight.float().contiguous()
-            stream = torch.cuda.current_stream(z.device).cuda_stream
-            for i in range(b):
-                _lib.call("bl_pair_bias", zf[i].data_ptr(), n * n, _lib.ptr(ln.weight), _lib.ptr(ln.bias),
-                          float(ln.eps), w_z.data_ptr(), self.num_heads, bias[i].data_ptr(), stream)
-        else:
-            bias = z
         g = torch.sigmoid(g)
         attn = torch.einsum("bihd,bjhd->bhij", q, k) / math.sqrt(self.head_dim) + bias
         attn = attn + (1 - mask[:, None, None].float()) * -self.inf

@@ -1,0 +1,261 @@
+"""Row-sharded Pairformer block for large N (one process per GPU).
+
+The pair tensor z [N, N, 128] (fp32) is split by rows across P ranks: rank r
+holds rows I_r = [r N/P, (r + 1) N/P).  Every op then runs the same kernels as
+the single-GPU path on its slab, with the exchanges the op needs:
+
+* TriangleMultiplicationOutgoing (row layout): each rank projects its rows
+  into channel planes a_r, b_r; b is all-gathered, and O_c[I_r, :] =
+  a_r b_c^T is one per-channel GEMM per source rank (output columns I_p).
+* TriangleMultiplicationIncoming: run as the outgoing form on z^T (column
+  layout) with the two operand halves swapped:
+  z[i, j] += sum_k a[k, i] b[k, j]  ==  z'[j, i] += sum_k b'[j, k] a'[i, k],  z' = z^T.
+* TriangleAttentionStartingNode (row layout): local rows; the triangle bias
+  [4, N, N] (one row block per rank) is all-gathered.
+* TriangleAttentionEndingNode: the starting form on z^T (column layout), as
+  upstream runs it (triangle.py:131 transposes the pair axes).
+* Transition: pointwise per pair row, no exchange.
+* Single track: the pair bias LN(z) W_z is computed per row block and
+  all-gathered; the s update is replicated on every rank.
+
+Layout changes row <-> column are one all_to_all of the slab (each rank keeps
+1/P and sends (P - 1)/P of it) plus a local block transpose.  The collectives
+go through a small `Comm` interface: `TorchComm` wraps torch.distributed
+(NCCL over NVLink on a B200 box, gloo on CPU); `ThreadComm` emulates P ranks as
+threads of one process on one GPU, which is how the decomposition is checked
+against the unsharded block without several GPUs.
+"""
+
+import threading
+
+import torch
+
+from . import _lib, forwards, kernels
+from ._lib import call, stream_of
+from .forwards import _BF16, _Q_SCALE, _f32
+
+__all__ = ["Comm", "SingleComm", "TorchComm", "ThreadComm", "rows_to_columns", "ShardedPairformer"]
+
+
+# ---------------------------------------------------------------------------
+# Collectives
+# ---------------------------------------------------------------------------
+class Comm:
+    """The two collectives the sharded block needs."""
+
+    rank = 0
+    world = 1
+
+    def all_gather(self, t):
+        """[world, *t.shape]: entry p is rank p's tensor."""
+        raise NotImplementedError
+
+    def all_to_all(self, t):
+        """t is [world, ...] with chunk p addressed to rank p; returns [world, ...]
+        with chunk p received from rank p."""
+        raise NotImplementedError
+
+
+class TorchComm(Comm):
+    """torch.distributed collectives on an initialised process group."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+
+        self.dist, self.group = dist, group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+
+    def all_gather(self, t):
+        t = t.contiguous()
+        flat = t.view(-1)
+        out = torch.empty(self.world * flat.numel(), dtype=t.dtype, device=t.device)
+        self.dist.all_gather_into_tensor(out, flat, group=self.group)
+        return out.view((self.world,) + tuple(t.shape))
+
+    def all_to_all(self, t):
+        t = t.contiguous()
+        out = torch.empty_like(t)
+        self.dist.all_to_all_single(out, t, group=self.group)
+        return out
+
+
+class SingleComm(Comm):
+    """World of one (no process group needed)."""
+
+    def all_gather(self, t):
+        return t.contiguous().unsqueeze(0)
+
+    def all_to_all(self, t):
+        return t.contiguous()
+
+
+class _ThreadHub:
+    def __init__(self, world):
+        self.world = world
+        self.slots = [None] * world
+        self.barrier = threading.Barrier(world)
+
+
+class ThreadComm(Comm):
+    """P virtual ranks as threads of one process sharing one device.  Each
+    exchange synchronises the device, so it is for checking the decomposition,
+    not for speed."""
+
+    def __init__(self, hub, rank):
+        self.hub, self.rank, self.world = hub, rank, hub.world
+
+    @staticmethod
+    def group(world):
+        hub = _ThreadHub(world)
+        return [ThreadComm(hub, r) for r in range(world)]
+
+    def _exchange(self, t):
+        if t.is_cuda:
+            torch.cuda.synchronize()
+        self.hub.slots[self.rank] = t
+        self.hub.barrier.wait()
+        peers = list(self.hub.slots)
+        return peers
+
+    def _done(self):
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+        self.hub.barrier.wait()
+
+    def all_gather(self, t):
+        peers = self._exchange(t.contiguous())
+        out = torch.stack(peers)
+        self._done()
+        return out
+
+    def all_to_all(self, t):
+        peers = self._exchange(t.contiguous())
+        out = torch.stack([peers[p][self.rank] for p in range(self.world)])
+        self._done()
+        return out
+
+
+# ---------------------------------------------------------------------------
+# Layout
+# ---------------------------------------------------------------------------
+def rows_to_columns(slab, comm):
+    """Row slab [n_loc, N, C] of X (rows I_r) -> row slab of X^T (rows I_r of X^T,
+    i.e. columns I_r of X).  Applying it twice returns the original layout."""
+    n_loc, n, c = slab.shape
+    world = comm.world
+    send = slab.view(n_loc, world, n_loc, c).permute(1, 0, 2, 3)  # chunk p = X[I_r, I_p]
+    recv = comm.all_to_all(send)  # chunk p = X[I_p, I_r]
+    return recv.permute(2, 0, 1, 3).reshape(n_loc, n, c).contiguous()  # [j in I_r][i][c]
+
+
+def _gather_rows(local, comm):
+    """[..., n_loc, W] per rank -> [..., N, W] (row blocks concatenated in rank order)."""
+    g = comm.all_gather(local)  # [P, ..., n_loc, W]
+    lead = g.dim() - 3
+    perm = list(range(1, 1 + lead)) + [0, lead + 1, lead + 2]
+    out = g.permute(*perm)
+    return out.reshape(*out.shape[:lead], out.shape[lead] * out.shape[lead + 1], out.shape[-1])
+
+
+# ---------------------------------------------------------------------------
+# Per-op slab forwards (the single-GPU kernels on [n_loc, N] row slabs)
+# ---------------------------------------------------------------------------
+def _trimul_slab(module, x, mask_rows, comm, swap):
+    """z_slab += outgoing-form triangle multiplication of `module` on the row
+    slab x [n_loc, N, 128] (fp32, updated in place); `swap` exchanges the two
+    operand halves (the incoming op on the transposed tensor)."""
+    n_loc, n = x.shape[0], x.shape[1]
+    n_pad = forwards._pad8(n)
+    w = forwards._multiplication_weights(module)
+    stream = stream_of(x)
+    xn = torch.empty(n_loc * n, 128, device=x.device, dtype=_BF16)
+    planes = torch.empty(256, n_loc, n_pad, device=x.device, dtype=_BF16)
+    call("bl_trimul_projection", x.data_ptr(), n, n_loc, _f32(module.norm_in.weight).data_ptr(),
+         _f32(module.norm_in.bias).data_ptr(), float(module.norm_in.eps), w["w_in"].data_ptr(),
+         mask_rows.data_ptr(), planes.data_ptr(), n_pad, xn.data_ptr(), stream)
+    rows_op, cols_op = (planes[128:], planes[:128]) if swap else (planes[:128], planes[128:])
+    cols_all = comm.all_gather(cols_op.contiguous())  # [P, 128, n_loc, n_pad]
+    prod = torch.empty(128, n_loc, n_pad, device=x.device, dtype=_BF16)
+    plane = n_loc * n_pad
+    for p in range(comm.world):
+        # O_c[i in I_r, j in I_p] = sum_k rows_c[i, k] cols_c[p][j, k]
+        call("bl_batched_gemm", rows_op.data_ptr(), 0, n_pad, plane, cols_all[p].data_ptr(), 0, n_pad, plane,
+             prod.data_ptr() + p * n_loc * 2, n_pad, plane, 128, n_loc, n_loc, n, None, stream)
+    norm = module.norm_out
+    call("bl_trimul_output", prod.data_ptr(), n, n_loc, n_pad, _f32(norm.weight).data_ptr(),
+         _f32(norm.bias).data_ptr(), float(norm.eps), xn.data_ptr(), w["w_pg"].data_ptr(), x.data_ptr(), None,
+         stream)
+
+
+def _attention_slab(module, x, mask_rows, comm):
+    """z_slab += starting-node triangle attention of `module` on the row slab x."""
+    n_loc, n = x.shape[0], x.shape[1]
+    n_pad = forwards._pad8(n)
+    w = forwards._attention_weights(module)
+    stream = stream_of(x)
+    ln = module.layer_norm
+    proj = torch.empty(n_loc * n, 512, device=x.device, dtype=_BF16)
+    bias = torch.empty(4, n_loc, n_pad, device=x.device, dtype=_BF16)
+    call("bl_attention_projection", x.data_ptr(), n, n_loc, _f32(ln.weight).data_ptr(), _f32(ln.bias).data_ptr(),
+         float(ln.eps), w["w_in"].data_ptr(), w["b_in"].data_ptr(), _Q_SCALE, w["w_heads"].data_ptr(), 0,
+         proj.data_ptr(), 512, bias.data_ptr(), n_pad, n_loc * n_pad, stream)
+    bias_full = _gather_rows(bias, comm).contiguous()  # [4, N, n_pad]
+    gated = torch.empty(n_loc * n, 128, device=x.device, dtype=_BF16)
+    base = proj.data_ptr()
+    call("bl_triangle_attention", base, base + 128 * 2, base + 256 * 2, base + 384 * 2, 512, n, 1,
+         bias_full.data_ptr(), n_pad, n * n_pad, mask_rows.data_ptr(), n, 1, float(getattr(module, "inf", 1e9)),
+         4, 32, n, n_loc, gated.data_ptr(), 128, stream)
+    forwards._linear_out(gated, w["w_out"], n_loc * n, 128, stream, bias=w["b_out"], residual=x.view(n_loc * n, 128))
+
+
+class ShardedPairformer:
+    """One Pairformer block (`layers.PairformerLayer` weights) on a row slab.
+
+    forward(s, z_rows, mask, pair_mask) -> (s, z_rows): s [1, N, c_s] and the
+    masks are replicated; z_rows [n_loc, N, 128] fp32 holds this rank's rows
+    (rank r: rows r * n_loc ...) and the returned slab holds the updated rows
+    (the input slab is used as scratch).  N must be a multiple of 8 * world."""
+
+    def __init__(self, block, comm):
+        self.block, self.comm = block, comm
+
+    def forward(self, s, z_rows, mask, pair_mask):
+        comm, blk = self.comm, self.block
+        n_loc, n = z_rows.shape[0], z_rows.shape[1]
+        if n % (8 * comm.world) or n_loc * comm.world != n:
+            raise RuntimeError("row sharding needs N divisible by 8 * world and equal slabs")
+        r0 = comm.rank * n_loc
+        pm = pair_mask.reshape(n, n).float()
+        mask_rows = pm[r0:r0 + n_loc].contiguous()
+        mask_cols = pm.t()[r0:r0 + n_loc].contiguous()
+        _trimul_slab(blk.tri_mul_out, z_rows, mask_rows, comm, swap=False)
+        z_cols = rows_to_columns(z_rows, comm)
+        _trimul_slab(blk.tri_mul_in, z_cols, mask_cols, comm, swap=True)
+        z_rows = rows_to_columns(z_cols, comm)
+        _attention_slab(blk.tri_att_start, z_rows, mask_rows, comm)
+        z_cols = rows_to_columns(z_rows, comm)
+        _attention_slab(blk.tri_att_end, z_cols, mask_cols, comm)
+        z_rows = rows_to_columns(z_cols, comm)
+        forwards.transition_forward(blk.transition_z, z_rows, residual=z_rows)
+        s = self._single_track(s, z_rows, mask)
+        return s, z_rows
+
+    __call__ = forward
+
+    def _single_track(self, s, z_rows, mask):
+        """s += AttentionPairBias(LN(s), z) ; s += Transition(s): the pair bias
+        is computed per row block and gathered, the rest is replicated."""
+        blk, comm = self.block, self.comm
+        att = blk.attention
+        n_loc, n = z_rows.shape[0], z_rows.shape[1]
+        ln, lin = att.proj_z[0], att.proj_z[1]
+        w_z = lin.weight.float().contiguous()
+        bias_loc = torch.empty(att.num_heads, n_loc * n, device=z_rows.device, dtype=torch.float32)
+        call("bl_pair_bias", z_rows.data_ptr(), n_loc * n, _lib.ptr(ln.weight), _lib.ptr(ln.bias), float(ln.eps),
+             w_z.data_ptr(), att.num_heads, bias_loc.data_ptr(), stream_of(z_rows))
+        bias = _gather_rows(bias_loc.view(att.num_heads, n_loc, n), comm).unsqueeze(0)  # [1, H, N, N]
+        s_normed = kernels.layer_norm(s.contiguous(), blk.pre_norm_s.weight, blk.pre_norm_s.bias,
+                                      blk.pre_norm_s.eps, out_dtype=torch.float32)
+        s = s + att.attend(s_normed, bias, mask, s_normed)
+        return s + blk.transition_s(s)

@@ -169,37 +169,40 @@ BL_API int bl_linear_fused(const void *a, int64_t a_ld, const void *a2, int64_t 
 
 /*
  * Triangle-attention input stage in one pass over the fp32 pair rows
- * x [n*n][128] (16-byte aligned):
+ * x [n_outer*n][128] (16-byte aligned; n_outer = n for a whole pair tensor,
+ * fewer for a row slab of a sharded one):
  *   x_hat = bf16(LayerNorm(x))                                  (fp32 statistics)
  *   y[r][0:512] = bf16(x_hat[r] . w^T + bias)                   w bf16 [512][128] = q | k | v | g rows
  *   proj[r] = bf16(y_q * q_scale) | y_k | y_v | bf16(sigmoid(y_g))  (the flash kernel's operands)
  *   bias_planes[h][q][k] = bf16(x_hat[q*n + k] . w_heads[h])    (transpose = 0, starting node)
  *   bias_planes[h][k][q] = same                                 (transpose = 1, ending node)
  * bias (fp32 [512]) may be NULL; w_heads is bf16 [4][128]; proj rows are
- * proj_ld >= 512 elements (multiple of 8), bias planes bias_ld >= n.
+ * proj_ld >= 512 elements (multiple of 8); bias plane h at bias_planes + h*bias_hs,
+ * rows of bias_ld elements.
  * Replaces the layer_norm fast path (triangle.py:107-146), the q/k/v/g
  * linears of _prep_qkv (triangle.py:80, upstream Attention) and upstream's
  * triangle-bias `linear` that feed ordered_triangle_forward (triangle.py:32).
  */
-BL_API int bl_attention_projection(const float *x, int64_t n, const float *ln_weight, const float *ln_bias,
-                                   float eps, const void *w, const float *bias, float q_scale,
-                                   const void *w_heads, int transpose, void *proj, int64_t proj_ld,
-                                   void *bias_planes, int64_t bias_ld, void *stream);
+BL_API int bl_attention_projection(const float *x, int64_t n, int64_t n_outer, const float *ln_weight,
+                                   const float *ln_bias, float eps, const void *w, const float *bias,
+                                   float q_scale, const void *w_heads, int transpose, void *proj,
+                                   int64_t proj_ld, void *bias_planes, int64_t bias_ld, int64_t bias_hs,
+                                   void *stream);
 
 /*
  * Triangle-multiplication input stage in one pass over the fp32 pair rows
- * x [n*n][128]:
+ * x [n_outer*n][128] (outer index i < n_outer, inner k < n):
  *   x_hat = bf16(LayerNorm(x)) -> xn [n*n][128]
  *   p = x_hat . w[0:256]^T, g = x_hat . w[256:512]^T        (bf16 results; w = [p_in; g_in])
  *   planes[c][i][k] = bf16(bf16(p_c * bf16(sigmoid(g_c))) * mask[i*n + k])   c < 256
- * planes is bf16 [256][n][plane_ld] (channels 0..127 = a, 128..255 = b),
+ * planes is bf16 [256][n_outer][plane_ld] (channels 0..127 = a, 128..255 = b),
  * plane_ld >= n and a multiple of 8.  Replaces norm_in + p_in/g_in + the
  * gate/pack/split kernels and layout copies of multiplication.py:48-120
  * (multiplication_gate_hip.cu:16-58).
  */
-BL_API int bl_trimul_projection(const float *x, int64_t n, const float *ln_weight, const float *ln_bias,
-                                float eps, const void *w, const float *mask, void *planes, int64_t plane_ld,
-                                void *xn, void *stream);
+BL_API int bl_trimul_projection(const float *x, int64_t n, int64_t n_outer, const float *ln_weight,
+                                const float *ln_bias, float eps, const void *w, const float *mask, void *planes,
+                                int64_t plane_ld, void *xn, void *stream);
 
 /*
  * Pair transition in one pass over fp32 rows x [rows][128]:
@@ -217,15 +220,15 @@ BL_API int bl_pair_transition(const float *x, int64_t rows, const float *ln_weig
 /*
  * Output stage of the triangle multiplication:
  *   o_hat = bf16(LayerNorm(O)) over the 128 channels of the product planes
- *           prod bf16 [128][n][ld] (O_c[i][j] at c*n*ld + i*ld + j),
+ *           prod bf16 [128][n_outer][ld] (O_c[i][j] at c*n_outer*ld + i*ld + j, i < n_outer),
  *   y = bf16(bf16(o_hat p_out^T) * bf16(sigmoid(bf16(x_hat g_out^T))))
- * with x_hat = xn bf16 [n*n][128] and w_out = bf16 [256][128] (p_out rows then
- * g_out rows); then z += y (fp32 [n*n][128]) or out = y (bf16), exactly one
+ * with x_hat = xn bf16 [n_outer*n][128] and w_out = bf16 [256][128] (p_out rows
+ * then g_out rows); then z += y (fp32 [n_outer*n][128]) or out = y (bf16), exactly one
  * non-NULL.  ld is a multiple of 8, pointers 16-byte aligned.  Replaces
  * norm_out + p_out + g_out + the gate of multiplication.py:124-137 and the
  * Pairformer's residual add.
  */
-BL_API int bl_trimul_output(const void *prod, int64_t n, int64_t ld, const float *ln_weight,
+BL_API int bl_trimul_output(const void *prod, int64_t n, int64_t n_outer, int64_t ld, const float *ln_weight,
                             const float *ln_bias, float eps, const void *xn, const void *w_out, float *z,
                             void *out, void *stream);
 
@@ -259,15 +262,17 @@ BL_API int bl_swiglu_rows(const void *x, int64_t x_ld, int64_t rows, int64_t wid
  * (outer a, inner b) = a*so + b*si (starting node: so = n, si = 1; ending
  * node: so = 1, si = n).  bias(h, b, c) at bias + h*bias_hs + b*bias_ld + c.
  * mask(a, c) at mask + a*ms_o + c*ms_k (fp32).  out rows of out_ld elements
- * at the same pair rows.  heads must be 4 and head_dim 32, n <= 4096; all pointers
+ * at the same pair rows.  n is the key / query extent, n_outer the number of
+ * outer rows a processed (n for a whole pair tensor, fewer for a row slab).
+ * heads must be 4 and head_dim 32, n <= 4096; all pointers
  * 16-byte aligned, ld / out_ld / bias_ld / bias_hs multiples of 8.  Runs on
  * tcgen05 tensor cores (scores and P in TMEM, TMA-fed key tiles).
  */
 BL_API int bl_triangle_attention(const void *q, const void *k, const void *v, const void *g, int64_t ld,
                                  int64_t so, int64_t si, const void *bias, int64_t bias_ld,
                                  int64_t bias_hs, const float *mask, int64_t ms_o, int64_t ms_k,
-                                 float inf, int64_t heads, int64_t head_dim, int64_t n, void *out,
-                                 int64_t out_ld, void *stream);
+                                 float inf, int64_t heads, int64_t head_dim, int64_t n, int64_t n_outer,
+                                 void *out, int64_t out_ld, void *stream);
 
 /*
  * Pair transition (LayerNorm -> fc1|fc2 -> SwiGLU -> fc3, the bf16-autocast
