@@ -50,6 +50,8 @@ def parse_args():
     p.add_argument("--n", type=int, default=N_TOKENS, help="tokens (default 512, the metric's config)")
     p.add_argument("--e2e-steps", type=int, default=12)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--sharded", action="store_true",
+                   help="one block at --n (default 2048) row-sharded over the ranks (strong scaling)")
     return p.parse_args()
 
 
@@ -474,10 +476,105 @@ def traffic_for(label):
     return None
 
 
+def run_sharded(args):
+    """One Pairformer block at N (default 2048) row-sharded over the ranks:
+    each rank holds N / world rows of z, the collectives run on NCCL over
+    NVLink.  Total work per step is fixed (strong scaling); value = device
+    time per block, max over ranks."""
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    from boltz_lumi_b200 import _lib, layers
+    from boltz_lumi_b200.sharded import ShardedPairformer, SingleComm, TorchComm
+
+    if world > 1:
+        import datetime
+        import torch.distributed as dist_mod
+
+        dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        dist = dist_mod
+    comm = TorchComm() if dist is not None else SingleComm()
+    n = args.n if args.n != N_TOKENS else 2048
+    n_loc = n // world
+    block = seeded_block(layers.PairformerLayer).to(device)
+    s_h, z_h, mask_h, pmask_h = synthetic_inputs(n, seed=1000)  # one block, split by rows
+    zr_h = z_h[0, rank * n_loc:(rank + 1) * n_loc].contiguous()
+    s, mask, pmask = s_h.to(device), mask_h.to(device), pmask_h.to(device)
+    z_rows = zr_h.to(device)
+    sharded = ShardedPairformer(block, comm)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    with torch.inference_mode():
+        for _ in range(max(args.warmup, 3)):
+            s, z_rows = sharded(s, z_rows, mask, pmask)
+        torch.cuda.synchronize()
+        observer = _lib.CallObserver(timed=())
+        _lib.set_observer(observer)
+        clocks = ClockSampler(device)
+        barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            s, z_rows = sharded(s, z_rows, mask, pmask)
+        end.record()
+        torch.cuda.synchronize()
+        _lib.set_observer(None)
+        barrier()
+        clock_info = clocks.stop()
+        ms = max_over_ranks(start.elapsed_time(end), dist, device) / args.steps
+        launches = observer.calls
+        # End to end: this rank's rows and s in from pinned memory, back out, every step.
+        zr_pin, s_pin = zr_h.pin_memory(), s_h.pin_memory()
+        z_back, s_back = torch.empty_like(zr_pin).pin_memory(), torch.empty_like(s_pin).pin_memory()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.e2e_steps):
+            zd, sd = zr_pin.to(device, non_blocking=True), s_pin.to(device, non_blocking=True)
+            so, zo = sharded(sd, zd, mask, pmask)
+            z_back.copy_(zo, non_blocking=True)
+            s_back.copy_(so, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        e2e = max_over_ranks(e0.elapsed_time(e1), dist, device) / args.e2e_steps
+        assert torch.isfinite(z_back).all() and torch.isfinite(s_back).all(), "non-finite block output"
+    if rank == 0:
+        flops = 4.0 * n ** 3 * 4 * 32 * 2 + 2 * 2.0 * 128 * n ** 3 + 2.0 * n * n * (128 * 1024 + 512 * 128)
+        line = {
+            "metric": f"Pairformer ms/block at N={n} row-sharded bf16", "value": round(ms, 4), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) inputs, N(0,1/128) weights)",
+            "config": {"workload": f"one Pairformer block N={n}, z rows split over {world} GPU(s) "
+                                   "(all_to_all row/column transposes, all_gather of planes and biases, NCCL)",
+                       "tokens": n, "rows_per_gpu": n_loc, "parallelism": f"row-sharded x{world}",
+                       "l2": "inputs larger than L2 (z slab >= 256 MiB fp32)"},
+            "e2e": {"value": round(e2e, 4), "unit": UNIT, "h2d_bytes_per_step": zr_pin.numel() * 4 + s_pin.numel() * 4,
+                    "d2h_bytes_per_step": zr_pin.numel() * 4 + s_pin.numel() * 4, "steps": args.e2e_steps},
+            "gpu_launches": launches,
+            "tensor_tflops_pair_ops": round(flops / (ms * 1e-3) / 1e12, 1),
+            "clocks": clock_info,
+            "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.sharded:
+        return run_sharded(args)
     return run_b200(args)
 
 
