@@ -9,7 +9,7 @@
 // triangle.py:194,208, pair_transition.py:158-165) and fuses what follows them:
 //
 //   EPI_STORE          C = bf16(acc + bias)
-//   EPI_RESIDUAL       Z += bf16(acc + bias)                 (fp32 Z, the pair tensor)
+//   EPI_RESIDUAL       Z += bf16(acc + bias)                 (fp32 Z, the pair tensor; TMA reduce-add)
 //   EPI_GATE_STORE     C[:, c] = bf16(bf16(acc[c]) * bf16(sigmoid(bf16(acc[w + c]))))
 //   EPI_GATE_RESIDUAL  Z[:, c] += that value                  (w = BN / 2)
 // The gate forms are the output gate of the triangle multiplication
@@ -20,8 +20,8 @@
 //   warp 1      TMEM allocation + single-thread tcgen05.mma issue
 //   warps 2..5  epilogue: tcgen05.ld -> math -> swizzled staging -> TMA store
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
-// of tile t overlaps the main loop of tile t+1.  Residual epilogues TMA-load
-// the fp32 Z tile while the tile's MMAs run and TMA-store it back.
+// of tile t overlaps the main loop of tile t+1.  Residual epilogues add into
+// the fp32 Z with TMA reduce-add (no Z load on the SM).
 #include "tc.cuh"
 
 namespace bl {
@@ -76,10 +76,9 @@ template <int BN, int EPI> struct GemmShape {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = kResidual ? 3 : (BN == 256 ? 3 : 5);
+  static constexpr int kStages = BN == 256 ? 3 : 5;
   static constexpr int kRingBytes = kStages * kStageBytes;
-  // Residual: every 32-column fp32 chunk of the warp's 32 rows is resident at once.
-  static constexpr int kStagingPerWarp = kResidual ? (kOutWidth / 32) * kStagingBytes : 2 * kStagingBytes;
+  static constexpr int kStagingPerWarp = 2 * kStagingBytes;  // double-buffered 4 KB boxes
   static constexpr int kStagingTotal = 4 * kStagingPerWarp;
   static constexpr int kBarrierOffset = kRingBytes + kStagingTotal;
   static constexpr int kSmemBytes = kBarrierOffset + 256 + 1024;  // barriers + alignment slack
@@ -103,8 +102,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *empty = full + S::kStages;
   uint64_t *acc_full = empty + S::kStages;
   uint64_t *acc_empty = acc_full + 2;
-  uint64_t *z_full = acc_empty + 2;  // one per epilogue warp
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(z_full + 4);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_per_batch = args.tiles_m * args.tiles_n;
@@ -120,7 +118,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::mbar_init(&acc_full[b], 1);
       tc::mbar_init(&acc_empty[b], 4);
     }
-    for (int w = 0; w < 4; ++w) tc::mbar_init(&z_full[w], 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tma_a);
     tc::prefetch_tmap(&tma_a2);
@@ -209,29 +206,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     uint8_t *staging = smem + S::kRingBytes + quarter * S::kStagingPerWarp;
     int acc = 0;
-    uint32_t acc_phase = 0, z_phase = 0;
+    uint32_t acc_phase = 0;
     int chunk_count = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
       const int b = tile / tiles_per_batch, rem = tile % tiles_per_batch;
       const int m0 = (rem / args.tiles_n) * kBM, n0 = (rem % args.tiles_n) * BN;
       const int row0 = m0 + quarter * 32;
-      if constexpr (S::kResidual) {
-        // Fetch this warp's fp32 Z rows while the tile's MMAs run (the previous
-        // tile's stores must have finished reading the staging first).
-        if (lane == 0) {
-          tc::bulk_wait_read<0>();
-          tc::mbar_arrive_expect_tx(&z_full[quarter], S::kOutWidth / 32 * kStagingBytes);
-#pragma unroll
-          for (int cc = 0; cc < S::kOutWidth / 32; ++cc)
-            tc::tma_load_2d(staging + cc * kStagingBytes, &tma_c, &z_full[quarter], cc * 32, row0);
-        }
-      }
       if (!tc::mbar_wait(&acc_full[acc], acc_phase, args.status, 0x104)) break;
       tc::tc_fence_after();
       const uint32_t tbase = tc::tmem_addr(tmem_base, quarter * 32, acc * BN);
       if constexpr (S::kResidual) {
-        if (!tc::mbar_wait(&z_full[quarter], z_phase, args.status, 0x105)) break;
-        z_phase ^= 1u;
+        // Z += y as a TMA reduce-add of each [32 rows][32 fp32] box: the SM
+        // never loads Z (the add happens at L2, fp32 round-to-nearest).
 #pragma unroll 1
         for (int cc = 0; cc < S::kOutWidth / 32; ++cc) {
           uint32_t r[32];
@@ -240,33 +226,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (S::kGate) {
             uint32_t gr[32];
             tc::tmem_ld_32x32b_x32(tbase + S::kOutWidth + cc * 32, gr);
-            tc::tmem_ld_wait();
+            tc::tmem_ld_wait_regs(r, gr);
 #pragma unroll
             for (int j = 0; j < 32; ++j) out[j] = gate_pair(__uint_as_float(r[j]), __uint_as_float(gr[j]));
           } else {
             tc::tmem_ld_wait();
+            const int c0 = n0 + cc * 32;
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              const int c = n0 + cc * 32 + j;
-              out[j] = bf16r(__uint_as_float(r[j]) + (args.bias && c < args.n ? args.bias[c] : 0.f));
+              const int c = c0 + j;
+              out[j] = bf16r(__uint_as_float(r[j]) + (args.bias && c < args.n ? __ldg(args.bias + c) : 0.f));
             }
           }
-          uint8_t *buf = staging + cc * kStagingBytes;
+          uint8_t *buf = staging + (chunk_count & 1) * kStagingBytes;
+          if (lane == 0) tc::bulk_wait_read<1>();
+          __syncwarp();
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float4 *p = reinterpret_cast<float4 *>(buf + lane * 128 + ((j ^ (lane & 7)) * 16));
-            float4 zv = *p;
-            zv.x += out[4 * j], zv.y += out[4 * j + 1], zv.z += out[4 * j + 2], zv.w += out[4 * j + 3];
-            *p = zv;
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4 *>(buf + lane * 128 + ((j ^ (lane & 7)) * 16)) =
+                make_float4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]);
+          tc::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tc::tma_reduce_add_2d(&tma_c, buf, cc * 32, row0);
+            tc::bulk_commit();
           }
-        }
-        tc::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-#pragma unroll
-          for (int cc = 0; cc < S::kOutWidth / 32; ++cc)
-            tc::tma_store_2d(&tma_c, staging + cc * kStagingBytes, cc * 32, row0);
-          tc::bulk_commit();
+          ++chunk_count;
         }
       } else {
 #pragma unroll 1
