@@ -1,6 +1,6 @@
 // Pair bias of the single-track attention in one pass over z (fp32):
 //
-//   bias[h][r] = sum_c LayerNorm(z[r])[c] * w[h][c]        h < 16, r < rows
+//   bias[h][r] = sum_c LayerNorm(z[r])[c] * w[h][c]        h < heads <= 16, r < rows
 //
 // i.e. proj_z = LayerNorm(c_z) -> Linear(c_z, heads, bias=False) ->
 // permute to [heads, N, N] of upstream AttentionPairBias (the Pairformer
@@ -8,95 +8,100 @@
 // the normalised fp32 pair tensor (128 MiB at N = 512), a GEMM reading it
 // back, and a strided permute consumed by a non-vectorised add.
 //
-// One warp per two rows: each lane holds 4 channels of both rows and the
-// matching 4 weights of every head; the 32 partial head sums are reduced
-// with a butterfly reduce-scatter so lane L ends with (row L / 16, head L % 16).
+// One thread per pair row.  A CTA stages 128 rows (64 KB of fp32) in shared
+// memory with coalesced 16-byte loads, then each thread computes its row's
+// statistics and the heads dot products from shared memory with no
+// cross-lane reductions: 2048 FMA per row against weights read as
+// same-address (broadcast) shared loads.
 #include "common.cuh"
 
 namespace bl {
 namespace {
 
 constexpr int kHeads = 16;
+constexpr int kC = 128;
+constexpr int kRowsPerCta = 128;
+constexpr int kRowStride = kC + 4;  // floats; 528-byte rows keep the per-thread row reads conflict-free
 
-template <int HALF> __device__ __forceinline__ void reduce_scatter_step(float (&v)[32], int lane) {
-  const bool upper = (lane & HALF) != 0;
-#pragma unroll
-  for (int i = 0; i < HALF; ++i) {
-    const float send = upper ? v[i] : v[i + HALF];
-    const float keep = upper ? v[i + HALF] : v[i];
-    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, HALF);
+__global__ void __launch_bounds__(kRowsPerCta) pair_bias_kernel(const float *z, int64_t rows, const float *ln_w,
+                                                                const float *ln_b, float eps, const float *w,
+                                                                int heads, float *out) {
+  extern __shared__ float4 smem4[];
+  float *tile = reinterpret_cast<float *>(smem4);           // [128][kRowStride]
+  float *ws = tile + kRowsPerCta * kRowStride;              // [kC][kHeads]: w transposed, zero past `heads`
+  float *lnw = ws + kC * kHeads, *lnb = lnw + kC;
+  const int t = threadIdx.x;
+  for (int i = t; i < kC * kHeads; i += kRowsPerCta) {
+    const int c = i / kHeads, h = i % kHeads;
+    ws[i] = h < heads ? w[h * kC + c] : 0.f;
   }
-}
-
-__global__ void __launch_bounds__(256) pair_bias_kernel(const float *z, int64_t rows, const float *ln_w,
-                                                        const float *ln_b, float eps, const float *w, int heads,
-                                                        float *out) {
-  const int lane = threadIdx.x & 31;
-  float lw[4], lb[4], wh[kHeads][4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    lw[e] = ln_w ? ln_w[lane * 4 + e] : 1.f;
-    lb[e] = ln_b ? ln_b[lane * 4 + e] : 0.f;
+  for (int c = t; c < kC; c += kRowsPerCta) {
+    lnw[c] = ln_w ? ln_w[c] : 1.f;
+    lnb[c] = ln_b ? ln_b[c] : 0.f;
   }
-#pragma unroll
-  for (int h = 0; h < kHeads; ++h) {
-    const float4 x = h < heads ? *reinterpret_cast<const float4 *>(w + h * 128 + lane * 4) : make_float4(0, 0, 0, 0);
-    wh[h][0] = x.x, wh[h][1] = x.y, wh[h][2] = x.z, wh[h][3] = x.w;
-  }
-  const int64_t pairs = (rows + 1) / 2;
-  const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t p = blockIdx.x * int64_t(blockDim.x >> 5) + (threadIdx.x >> 5); p < pairs; p += warps) {
-    const int64_t r0 = 2 * p;
-    float v[2][4];
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const float4 x = r0 + q < rows ? *reinterpret_cast<const float4 *>(z + (r0 + q) * 128 + lane * 4)
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-      v[q][0] = x.x, v[q][1] = x.y, v[q][2] = x.z, v[q][3] = x.w;
+  for (int64_t r0 = int64_t(blockIdx.x) * kRowsPerCta; r0 < rows; r0 += int64_t(gridDim.x) * kRowsPerCta) {
+    const int valid = rows - r0 < kRowsPerCta ? int(rows - r0) : kRowsPerCta;
+    __syncthreads();  // previous tile's readers are done (and the constants are in place)
+    // Coalesced staging with asynchronous copies (all 32 of a thread in flight
+    // at once): 32 consecutive threads copy one 512-byte row; rows past the
+    // end are zero-filled.
+    const float *src = z + r0 * kC;
+#pragma unroll 8
+    for (int i = t; i < kRowsPerCta * (kC / 4); i += kRowsPerCta) {
+      const int r = i / (kC / 4), c4 = i % (kC / 4);
+      const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(tile + r * kRowStride + 4 * c4));
+      const float *g = src + (r < valid ? i * 4 : 0);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(g), "r"(r < valid ? 16 : 0)
+                   : "memory");
     }
-    float mean[2], var[2];
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    const float *row = tile + t * kRowStride;
+    // Statistics: mean, then the mean of squared deviations (fp32, four partial sums).
+    float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+    for (int c = 0; c < kC; c += 4) {
+      const float4 v = *reinterpret_cast<const float4 *>(row + c);
+      s4[0] += v.x, s4[1] += v.y, s4[2] += v.z, s4[3] += v.w;
+    }
+    const float mean = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.f / kC);
+    float q4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+    for (int c = 0; c < kC; c += 4) {
+      const float4 v = *reinterpret_cast<const float4 *>(row + c);
+      const float d0 = v.x - mean, d1 = v.y - mean, d2 = v.z - mean, d3 = v.w - mean;
+      q4[0] += d0 * d0, q4[1] += d1 * d1, q4[2] += d2 * d2, q4[3] += d3 * d3;
+    }
+    const float rstd = rsqrtf(((q4[0] + q4[1]) + (q4[2] + q4[3])) * (1.f / kC) + eps);
+    float acc[kHeads];
 #pragma unroll
-    for (int q = 0; q < 2; ++q) mean[q] = (v[q][0] + v[q][1]) + (v[q][2] + v[q][3]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int q = 0; q < 2; ++q) mean[q] += __shfl_xor_sync(0xffffffffu, mean[q], o);
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      mean[q] *= 1.f / 128.f;
-      float sq = 0.f;
+    for (int h = 0; h < kHeads; ++h) acc[h] = 0.f;
+#pragma unroll 2
+    for (int c = 0; c < kC; c += 4) {
+      const float4 v = *reinterpret_cast<const float4 *>(row + c);  // 16-byte reads: no bank conflicts
+      const float4 gw = *reinterpret_cast<const float4 *>(lnw + c), gb = *reinterpret_cast<const float4 *>(lnb + c);
+      const float y[4] = {(v.x - mean) * rstd * gw.x + gb.x, (v.y - mean) * rstd * gw.y + gb.y,
+                          (v.z - mean) * rstd * gw.z + gb.z, (v.w - mean) * rstd * gw.w + gb.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float d = v[q][e] - mean[q];
-        sq += d * d;
+        const float4 *wc = reinterpret_cast<const float4 *>(ws + (c + e) * kHeads);  // same address in every lane
+#pragma unroll
+        for (int q = 0; q < kHeads / 4; ++q) {
+          const float4 wv = wc[q];
+          acc[4 * q] += y[e] * wv.x, acc[4 * q + 1] += y[e] * wv.y;
+          acc[4 * q + 2] += y[e] * wv.z, acc[4 * q + 3] += y[e] * wv.w;
+        }
       }
-      var[q] = sq;
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int q = 0; q < 2; ++q) var[q] += __shfl_xor_sync(0xffffffffu, var[q], o);
-    float part[32];  // index q * 16 + h
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const float rstd = rsqrtf(var[q] * (1.f / 128.f) + eps);
-      float y[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) y[e] = (v[q][e] - mean[q]) * rstd * lw[e] + lb[e];
+    if (t < valid) {
 #pragma unroll
       for (int h = 0; h < kHeads; ++h)
-        part[q * 16 + h] = (y[0] * wh[h][0] + y[1] * wh[h][1]) + (y[2] * wh[h][2] + y[3] * wh[h][3]);
+        if (h < heads) out[int64_t(h) * rows + r0 + t] = acc[h];
     }
-    reduce_scatter_step<16>(part, lane);
-    reduce_scatter_step<8>(part, lane);
-    reduce_scatter_step<4>(part, lane);
-    reduce_scatter_step<2>(part, lane);
-    reduce_scatter_step<1>(part, lane);
-    const int64_t row = r0 + (lane >> 4);
-    const int h = lane & 15;
-    if (row < rows && h < heads) out[int64_t(h) * rows + row] = part[0];
   }
 }
+
+constexpr int kSmemBytes = (kRowsPerCta * kRowStride + kC * kHeads + 2 * kC) * 4;
 
 }  // namespace
 }  // namespace bl
@@ -108,11 +113,12 @@ extern "C" int bl_pair_bias(const float *z, int64_t rows, const float *ln_weight
   BL_REQUIRE(rows >= 0 && heads >= 1 && heads <= kHeads, "bl_pair_bias: rows >= 0 and 1 <= heads <= 16");
   if (rows == 0) return BL_OK;
   BL_REQUIRE(z && w && out && eps > 0.f, "bl_pair_bias: null pointer or eps <= 0");
-  BL_REQUIRE(aligned_to(z, 16) && aligned_to(w, 16), "bl_pair_bias: z and w must be 16-byte aligned");
-  const int64_t pairs = (rows + 1) / 2;
-  int64_t blocks = (pairs + 7) / 8, cap = int64_t(num_sms()) * 8;
-  pair_bias_kernel<<<int(blocks < cap ? blocks : cap), 256, 0, as_stream(stream)>>>(z, rows, ln_weight, ln_bias, eps,
-                                                                                   w, int(heads), out);
+  BL_REQUIRE(aligned_to(z, 16), "bl_pair_bias: z must be 16-byte aligned");
+  BL_CUDA(ensure_smem_limit(reinterpret_cast<const void *>(pair_bias_kernel), kSmemBytes));
+  const int64_t tiles = (rows + kRowsPerCta - 1) / kRowsPerCta;
+  const int64_t cap = int64_t(num_sms()) * 3;  // three 75 KB CTAs per SM
+  pair_bias_kernel<<<int(tiles < cap ? tiles : cap), kRowsPerCta, kSmemBytes, as_stream(stream)>>>(
+      z, rows, ln_weight, ln_bias, eps, w, int(heads), out);
   BL_LAUNCH_CHECK();
   return BL_OK;
 }
