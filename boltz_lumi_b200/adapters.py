@@ -80,14 +80,42 @@ def _conditioned_transition(self, a, s):
     return forwards.conditioned_transition_forward(self, a.contiguous(), s.contiguous())
 
 
+def _token_attention(self, s, z, mask, k_in, multiplicity=1):
+    cls = type(self)
+    if (not _inference(self, s, z, mask, k_in) or self.compute_pair_bias or torch.is_autocast_enabled("cuda")):
+        return cls.forward(self, s, z, mask, k_in, multiplicity)
+    bias = self.proj_z(z)
+    if (not forwards.token_attention_supported(self, s, k_in, bias)
+            or bias.shape[0] * multiplicity not in (s.shape[0], 1)
+            or (mask is not None and tuple(mask.shape) != tuple(s.shape[:2]))):
+        return cls.forward(self, s, z, mask, k_in, multiplicity)
+    return forwards.attend_with_bias(self, s, bias, mask, k_in)
+
+
+def _sample(self, *args, **kwargs):
+    """``AtomDiffusion.sample`` with the token-transformer bias packed dense
+    once per prediction (the reference's optimized_sample, diffusion.py:13-18)."""
+    sample = type(self).sample
+    conditioning = kwargs.get("diffusion_conditioning")
+    if torch.is_grad_enabled() or self.training or not conditioning or "token_trans_bias" not in conditioning:
+        return sample(self, *args, **kwargs)
+    conditioning = dict(conditioning)
+    conditioning["token_trans_bias"] = forwards.prepare_token_bias(conditioning["token_trans_bias"])
+    kwargs["diffusion_conditioning"] = conditioning
+    return sample(self, *args, **kwargs)
+
+
 def install(model, require_device=True):
     """Rebind the hot-path forwards of ``model`` in place; idempotent.
 
     Returns the number of modules rebound.  Like the reference, modules are
     matched by class name: every TriangleAttention / TriangleAttentionEndingNode
     and TriangleMultiplication{Incoming,Outgoing}, every ``*.transition_z``
-    Transition, and the AdaLN / ConditionedTransitionBlock modules under
-    ``structure_module.score_model``.
+    Transition, the AdaLN / ConditionedTransitionBlock modules under
+    ``structure_module.score_model`` and the AttentionPairBias modules under
+    ``structure_module.score_model.token_transformer``; and, like the
+    reference (adapters.py:46), wraps ``structure_module.sample`` so the token
+    bias is packed once per prediction.
     """
     if getattr(model, "_b200_optimized", False):
         return 0
@@ -108,6 +136,12 @@ def install(model, require_device=True):
         elif cls in _DIFFUSION and name.startswith("structure_module.score_model."):
             module.forward = MethodType(_adaln if cls == "AdaLN" else _conditioned_transition, module)
             count += 1
+        elif cls == "AttentionPairBias" and name.startswith("structure_module.score_model.token_transformer."):
+            module.forward = MethodType(_token_attention, module)
+            count += 1
+    structure = getattr(model, "structure_module", None)
+    if structure is not None and callable(getattr(type(structure), "sample", None)):
+        structure.sample = MethodType(_sample, structure)
     model._b200_optimized = True
     return count
 
@@ -116,6 +150,10 @@ def uninstall(model):
     """Restore the class forwards rebound by :func:`install`."""
     for _, module in model.named_modules():
         if "forward" in module.__dict__ and getattr(module.forward, "__func__", None) in (
-                _triangle_attention, _triangle_multiplication, _pair_transition, _adaln, _conditioned_transition):
+                _triangle_attention, _triangle_multiplication, _pair_transition, _adaln, _conditioned_transition,
+                _token_attention):
             del module.forward
+    structure = getattr(model, "structure_module", None)
+    if structure is not None and getattr(structure.__dict__.get("sample"), "__func__", None) is _sample:
+        del structure.sample
     model._b200_optimized = False

@@ -1,0 +1,241 @@
+// Attention core of the diffusion token transformer's AttentionPairBias, fp32:
+//
+//   o[b, q, h] = sigmoid(g[b, q, h]) * sum_k softmax_k(s) v[b, k, h],
+//   s(q, k) = (q[b, q, h] . k[b, k, h]) * scale + bias[b', h, q, k] + inf * (mask[b, k] - 1)
+//
+// upstream attentionv2 with a prepared (dense) pair bias, which the reference
+// runs unfused in fp32 with autocast off (pair_bias.py:28-36: einsum,
+// + bias, + mask term, softmax, einsum, then the sigmoid gate).  The [B, H, N, N] scores never reach
+// HBM here.  b' = b / bias_batch_div lets one bias serve the `multiplicity`
+// diffusion samples of an input without repeating it.
+//
+// fp32 rules out the bf16 tensor cores, so this is a CUDA-core flash kernel:
+// one CTA = 64 queries of one (batch, head), 128 threads; each thread owns 4
+// queries x 8 keys of every 64-key tile (S accumulated with 16-byte shared
+// loads, 10 FMA per load) and 4 queries x head_dim/8 output dims.  K / V
+// tiles are double-buffered with cp.async; P goes through shared memory for
+// the P.V product; online softmax in fp32 with the MUFU exponent.
+#include "common.cuh"
+
+namespace bl {
+namespace {
+
+constexpr int kBQ = 64, kBK = 64, kThreads = 128;
+constexpr int kMaxD = 64;
+
+struct TokArgs {
+  const float *q, *k, *v, *g;  // g (gate logits) may be null
+  int64_t sb, si, sh;  // element strides of q/k/v/g: batch, token, head (dims contiguous)
+  const float *bias;
+  int64_t bias_sb, bias_sh, bias_sq, bias_sk;
+  int bias_div;
+  const float *mask;  // [B][N] at mask + b * mask_sb + k, or null
+  int64_t mask_sb;
+  float scale, inf;
+  int heads, n, d;
+  float *out;  // [B][N][H][d] contiguous
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads) token_attention_kernel(const TokArgs a) {
+  constexpr int kLd = D + 4;        // padded row (floats): conflict-free 16-byte row reads
+  constexpr int kDpt = D / 8;       // output dims per thread
+  extern __shared__ float4 smem4[];
+  float *qs = reinterpret_cast<float *>(smem4);  // [64][kLd]
+  float *ks = qs + kBQ * kLd;                    // [2][64][kLd]
+  float *vs = ks + 2 * kBK * kLd;                // [2][64][kLd]
+  float *ps = vs + 2 * kBK * kLd;                // [64][kBK + 4]
+  constexpr int kPld = kBK + 4;
+
+  const int t = threadIdx.x, tq = t >> 3, tk = t & 7;
+  const int q0 = blockIdx.x * kBQ, h = blockIdx.y, b = blockIdx.z;
+  const int n = a.n;
+  const float *qb = a.q + b * a.sb + h * a.sh, *kb = a.k + b * a.sb + h * a.sh, *vb = a.v + b * a.sb + h * a.sh;
+  const float *bias = a.bias + int64_t(b / a.bias_div) * a.bias_sb + h * a.bias_sh;
+  const float *mask = a.mask ? a.mask + b * a.mask_sb : nullptr;
+
+  // Q tile (rows past n are zero) and the first K / V tile.
+  constexpr int kChunks = D / 4;  // 16-byte chunks per row
+  for (int i = t; i < kBQ * kChunks; i += kThreads) {
+    const int r = i / kChunks, c = i % kChunks;
+    const bool ok = q0 + r < n;
+    cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(qs + r * kLd + 4 * c)),
+               qb + (ok ? int64_t(q0 + r) * a.si + 4 * c : 0), ok);
+  }
+  auto load_kv = [&](int tile, int buf) {
+    const int k0 = tile * kBK;
+    for (int i = t; i < kBK * kChunks; i += kThreads) {
+      const int r = i / kChunks, c = i % kChunks;
+      const bool ok = k0 + r < n;
+      const int64_t off = ok ? int64_t(k0 + r) * a.si + 4 * c : 0;
+      cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(ks + (buf * kBK + r) * kLd + 4 * c)), kb + off, ok);
+      cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(vs + (buf * kBK + r) * kLd + 4 * c)), vb + off, ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  const int n_tiles = (n + kBK - 1) / kBK;
+  load_kv(0, 0);
+
+  float m[4], l[4], o[4][kDpt];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m[i] = -INFINITY, l[i] = 0.f;
+#pragma unroll
+    for (int e = 0; e < kDpt; ++e) o[i][e] = 0.f;
+  }
+  constexpr float kLog2e = 1.4426950408889634f;
+
+  for (int tile = 0; tile < n_tiles; ++tile) {
+    const int buf = tile & 1, k0 = tile * kBK;
+    if (tile + 1 < n_tiles) {
+      load_kv(tile + 1, buf ^ 1);  // the buffer was released by the barrier that ended tile - 1
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+
+    // S = Q K^T for 4 queries (4 tq + i) x 8 keys (tk + 8 j).
+    float s[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s[i][j] = 0.f;
+    const float *kt = ks + buf * kBK * kLd;
+#pragma unroll 2
+    for (int e = 0; e < D; e += 4) {
+      float4 qv[4], kv[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4 *>(qs + (4 * tq + i) * kLd + e);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) kv[j] = *reinterpret_cast<const float4 *>(kt + (tk + 8 * j) * kLd + e);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          s[i][j] += qv[i].x * kv[j].x + qv[i].y * kv[j].y + qv[i].z * kv[j].z + qv[i].w * kv[j].w;
+    }
+    // Scale, bias, mask; then the online softmax over the 8 lanes of each query row.
+    float mk[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int key = k0 + tk + 8 * j;
+      mk[j] = key < n ? (mask ? a.inf * (mask[key] - 1.f) : 0.f) : -INFINITY;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int qi = q0 + 4 * tq + i;
+      const float *brow = bias + int64_t(qi < n ? qi : 0) * a.bias_sq;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int key = k0 + tk + 8 * j;
+        const float bv = key < n ? __ldg(brow + int64_t(key) * a.bias_sk) : 0.f;
+        s[i][j] = s[i][j] * a.scale + bv + mk[j];
+        mx = fmaxf(mx, s[i][j]);
+      }
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_new = fmaxf(m[i], mx);
+      const float alpha = exp2f((m[i] - m_new) * kLog2e);  // 0 on the first tile (m = -inf)
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float p = exp2f((s[i][j] - m_new) * kLog2e);  // padding keys: exp2(-inf) = 0
+        sum += p;
+        ps[(4 * tq + i) * kPld + tk + 8 * j] = p;
+      }
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      l[i] = l[i] * alpha + sum;
+      m[i] = m_new;
+#pragma unroll
+      for (int e = 0; e < kDpt; ++e) o[i][e] *= alpha;
+    }
+    __syncwarp();  // a query row's P is written and read by the same 8 lanes
+    // O += P V: 4 queries x kDpt contiguous dims (tk * kDpt ...).
+    const float *vt = vs + buf * kBK * kLd + tk * kDpt;
+#pragma unroll 4
+    for (int kk = 0; kk < kBK; kk += 4) {
+      float4 pv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pv[i] = *reinterpret_cast<const float4 *>(ps + (4 * tq + i) * kPld + kk);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float vv[kDpt];
+#pragma unroll
+        for (int e = 0; e < kDpt; ++e) vv[e] = vt[(kk + u) * kLd + e];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float p = u == 0 ? pv[i].x : u == 1 ? pv[i].y : u == 2 ? pv[i].z : pv[i].w;
+#pragma unroll
+          for (int e = 0; e < kDpt; ++e) o[i][e] += p * vv[e];
+        }
+      }
+    }
+    __syncthreads();  // K / V buffer `buf` and P are free for the next tile
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int qi = q0 + 4 * tq + i;
+    if (qi >= n) continue;
+    const float inv = 1.f / l[i];
+    float *dst = a.out + ((int64_t(b) * n + qi) * a.heads + h) * D + tk * kDpt;
+    const float *gr = a.g ? a.g + b * a.sb + h * a.sh + int64_t(qi) * a.si + tk * kDpt : nullptr;
+#pragma unroll
+    for (int e = 0; e < kDpt; ++e) {
+      const float y = o[i][e] * inv;
+      dst[e] = gr ? y * (1.f / (1.f + expf(-gr[e]))) : y;
+    }
+  }
+}
+
+template <int D> int launch_token(const TokArgs &a, int batch, cudaStream_t stream) {
+  constexpr int kLd = D + 4;
+  const int smem = (kBQ * kLd + 4 * kBK * kLd + kBQ * (kBK + 4)) * 4;
+  BL_CUDA(ensure_smem_limit(reinterpret_cast<const void *>(token_attention_kernel<D>), smem));
+  dim3 grid((a.n + kBQ - 1) / kBQ, a.heads, batch);
+  token_attention_kernel<D><<<grid, kThreads, smem, stream>>>(a);
+  BL_LAUNCH_CHECK();
+  return BL_OK;
+}
+
+}  // namespace
+}  // namespace bl
+
+using namespace bl;
+
+extern "C" int bl_token_attention(const float *q, const float *k, const float *v, const float *g, int64_t sb,
+                                  int64_t si, int64_t sh,
+                                  const float *bias, int64_t bias_sb, int64_t bias_sh, int64_t bias_sq,
+                                  int64_t bias_sk, int64_t bias_batch_div, const float *mask, int64_t mask_sb,
+                                  float scale, float inf, int64_t batch, int64_t heads, int64_t n, int64_t head_dim,
+                                  float *out, void *stream) {
+  BL_REQUIRE(batch >= 0 && heads > 0 && n >= 0, "bl_token_attention: bad shape");
+  if (batch == 0 || n == 0) return BL_OK;
+  BL_REQUIRE(head_dim == 24 || head_dim == 32 || head_dim == 48 || head_dim == 64,
+             "bl_token_attention: head_dim 24, 32, 48 or 64");
+  BL_REQUIRE(q && k && v && bias && out && bias_batch_div >= 1, "bl_token_attention: null pointer");
+  BL_REQUIRE(aligned_to(q, 16) && aligned_to(k, 16) && aligned_to(v, 16) && aligned_to(g, 4) && si % 4 == 0 &&
+                 sh % 4 == 0 &&
+                 sb % 4 == 0,
+             "bl_token_attention: q/k/v rows must be 16-byte aligned");
+  BL_REQUIRE(n < (1 << 20) && heads < 65536 && batch < 65536, "bl_token_attention: shape too large");
+  TokArgs a{};
+  a.q = q, a.k = k, a.v = v, a.g = g, a.sb = sb, a.si = si, a.sh = sh;
+  a.bias = bias, a.bias_sb = bias_sb, a.bias_sh = bias_sh, a.bias_sq = bias_sq, a.bias_sk = bias_sk;
+  a.bias_div = int(bias_batch_div);
+  a.mask = mask, a.mask_sb = mask_sb;
+  a.scale = scale, a.inf = inf;
+  a.heads = int(heads), a.n = int(n), a.d = int(head_dim);
+  a.out = out;
+  cudaStream_t s = as_stream(stream);
+  if (head_dim == 24) return launch_token<24>(a, int(batch), s);
+  if (head_dim == 32) return launch_token<32>(a, int(batch), s);
+  if (head_dim == 48) return launch_token<48>(a, int(batch), s);
+  return launch_token<64>(a, int(batch), s);
+}

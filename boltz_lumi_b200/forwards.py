@@ -312,6 +312,87 @@ def conditioned_transition_forward(self, a, s):
 
 
 # ---------------------------------------------------------------------------
+# AttentionPairBias with a given (prepared) bias: diffusion token transformer
+# ---------------------------------------------------------------------------
+_TOKEN_HEAD_DIMS = (24, 32, 48, 64)
+
+
+def prepare_token_bias(value):
+    """The diffusion token bias [B, N, N, L*H] with dense head-major storage.
+
+    Same logical shape and values (fp32); only the memory order changes to
+    [B, L*H, N, N], so each layer's [B, H, N, N] slice is read row by row by
+    the attention kernel (the reference's prepare_token_bias, pair_bias.py:6-12).
+    """
+    return value.permute(0, 3, 1, 2).contiguous().float().permute(0, 2, 3, 1)
+
+
+def _qkvg_weights(module):
+    """proj_q | proj_k | proj_v | proj_g stacked into one [4 c_s, c_s] weight
+    (proj_q's bias, zeros for the others), rebuilt when a source changes."""
+    params = (module.proj_q.weight, module.proj_q.bias, module.proj_k.weight, module.proj_v.weight,
+              module.proj_g.weight)
+
+    def build():
+        w = torch.cat([module.proj_q.weight, module.proj_k.weight, module.proj_v.weight, module.proj_g.weight], 0)
+        bias = torch.zeros(w.shape[0], device=w.device, dtype=w.dtype)
+        if module.proj_q.bias is not None:
+            bias[: module.c_s] = module.proj_q.bias
+        return w.contiguous(), bias
+
+    return _cached(module, "_bl_joint_qkvg", params, build)
+
+
+def token_attention_supported(module, s, k_in, bias):
+    """Shapes and dtypes the fused fp32 token attention covers."""
+    heads, d = module.num_heads, module.head_dim
+    return (d in _TOKEN_HEAD_DIMS and heads * d == module.c_s and s.dim() == 3 and s.dtype == torch.float32
+            and k_in.dtype == torch.float32 and k_in.shape == s.shape and s.shape[-1] == module.c_s
+            and bias.dim() == 4 and tuple(bias.shape[1:]) == (heads, s.shape[1], s.shape[1])
+            and bias.shape[0] >= 1 and s.shape[0] % bias.shape[0] == 0
+            and all(p.bias is None for p in (module.proj_k, module.proj_v, module.proj_g)))
+
+
+def attend_with_bias(self, s, bias, mask, k_in):
+    """Upstream attentionv2 ``AttentionPairBias`` after ``proj_z``: projections,
+    fused fp32 attention with bias, key mask and sigmoid gate, then ``proj_o``.
+
+    ``bias`` is fp32 [B', H, N, N] (any strides, B' dividing the batch: sample
+    ``b`` reads bias ``b // (B / B')``).  When ``k_in is s`` the four input
+    projections run as one GEMM over stacked weights.
+    """
+    b, n = s.shape[0], s.shape[1]
+    heads, d, c = self.num_heads, self.head_dim, self.c_s
+    with torch.autocast("cuda", enabled=False):
+        if k_in is s:
+            w, w_bias = _qkvg_weights(self)
+            q, k, v, g = F.linear(s, w, w_bias).view(b, n, 4, heads, d).unbind(2)
+        else:  # four contiguous [B, N, c_s] projections share one stride layout
+            q = F.linear(s, self.proj_q.weight, self.proj_q.bias).view(b, n, heads, d)
+            k = F.linear(k_in, self.proj_k.weight).view(b, n, heads, d)
+            v = F.linear(k_in, self.proj_v.weight).view(b, n, heads, d)
+            g = F.linear(s, self.proj_g.weight).view(b, n, heads, d)
+        out = kernels.token_attention(q, k, v, bias.float(), mask, self.inf, gate=g)
+    return self.proj_o(out.view(b, n, c))
+
+
+def token_attention_forward(self, s, z, mask, k_in, multiplicity=1):
+    """Upstream ``AttentionPairBias.forward(s, z, mask, k_in, multiplicity)``
+    with a prepared bias (the reference's prepared_forward, pair_bias.py:15-36).
+
+    ``z`` is the layer's slice of the dense token bias, [B, N, N, H]; upstream's
+    ``proj_z`` (a heads-first rearrange when ``compute_pair_bias`` is off)
+    turns it into the [B, H, N, N] view the kernel reads in place, and the
+    ``multiplicity`` diffusion samples of one input share one bias row
+    without the reference's ``repeat_interleave`` copy.
+    """
+    bias = self.proj_z(z)
+    if bias.shape[0] * multiplicity not in (s.shape[0], 1):
+        raise RuntimeError(f"bias batch {bias.shape[0]} x multiplicity {multiplicity} != batch {s.shape[0]}")
+    return attend_with_bias(self, s, bias, mask, k_in)
+
+
+# ---------------------------------------------------------------------------
 # Reference-compatible entry points (the reference rebinds pieces of modules)
 # ---------------------------------------------------------------------------
 def normalization_forward(self, x):
@@ -324,6 +405,9 @@ def normalization_forward(self, x):
 
 __all__ = [
     "adaln_forward",
+    "attend_with_bias",
+    "prepare_token_bias",
+    "token_attention_forward",
     "conditioned_transition_forward",
     "normalization_forward",
     "transition_forward",

@@ -223,3 +223,51 @@ def bmm(a, b_t, bias=None, out=None):
     call("bl_batched_gemm", a.data_ptr(), int(a_mn), a_ld, a_bs, b_t.data_ptr(), int(b_mn), b_ld, b_bs,
          out.data_ptr(), out.stride(1), out.stride(0), batch, m, n, k, ptr(bias), stream_of(a))
     return out
+
+
+def attention_scale(head_dim):
+    """fp32(1 / fp32(sqrt(head_dim))): the factor torch's CUDA division by the
+    Python scalar ``head_dim ** 0.5`` applies (pair_bias.py:31)."""
+    return float(torch.tensor(1.0, dtype=torch.float32) / torch.tensor(head_dim ** 0.5, dtype=torch.float32))
+
+
+def token_attention(q, k, v, bias, mask, inf, gate=None, scale=None):
+    """Fused fp32 attention of the diffusion token transformer (and the
+    Pairformer's single track): ``sigmoid(gate) * softmax(q k^T * scale + bias
+    + inf * (mask - 1)) v`` per head, the core of pair_bias.py:28-36.
+
+    ``q``, ``k``, ``v`` (and ``gate``): fp32 [B, N, H, d] views with a common
+    stride layout and contiguous head dims (e.g. slices of one joint
+    projection).  ``bias``: fp32 [Bb, H, N, N] with any strides, where ``Bb``
+    divides ``B`` -- sample ``b`` reads bias ``b // (B // Bb)``, which is the
+    reference's ``repeat_interleave(multiplicity, 0)`` without the copy.
+    ``mask``: [B, N] key mask or None.  Returns fp32 [B, N, H, d].
+    """
+    _require_inference(q, k, v, gate, bias, mask)
+    _require_cuda(q, k, v, gate, bias, mask)
+    tensors = [q, k, v] + ([gate] if gate is not None else [])
+    if any(t.dtype != torch.float32 for t in tensors + [bias]):
+        raise RuntimeError("token attention operands must be fp32")
+    if any(t.dim() != 4 or t.shape != q.shape or t.stride() != q.stride() for t in tensors):
+        raise RuntimeError("q, k, v and gate must be [B, N, H, d] views with the same strides")
+    batch, n, heads, d = q.shape
+    if q.stride(3) != 1:
+        raise RuntimeError("q/k/v head dims must be contiguous")
+    if bias.dim() != 4 or tuple(bias.shape[1:]) != (heads, n, n) or bias.shape[0] < 1 or batch % bias.shape[0]:
+        raise RuntimeError(f"bias must be [B', {heads}, {n}, {n}] with B' dividing {batch}, got {tuple(bias.shape)}")
+    mask_sb = 0
+    if mask is not None:
+        if tuple(mask.shape) != (batch, n):
+            raise RuntimeError("mask must be [B, N]")
+        mask = mask.float()
+        if mask.stride(1) != 1:
+            mask = mask.contiguous()
+        mask_sb = mask.stride(0)
+    if scale is None:
+        scale = attention_scale(d)
+    out = torch.empty(batch, n, heads, d, device=q.device, dtype=torch.float32)
+    call("bl_token_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), ptr(gate), q.stride(0), q.stride(1),
+         q.stride(2), bias.data_ptr(), bias.stride(0), bias.stride(1), bias.stride(2), bias.stride(3),
+         batch // bias.shape[0], ptr(mask), mask_sb, float(scale), float(inf), batch, heads, n, d, out.data_ptr(),
+         stream_of(q))
+    return out

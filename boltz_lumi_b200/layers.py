@@ -6,7 +6,6 @@ forwards are the kernel-backed functions of :mod:`boltz_lumi_b200.forwards`;
 they are inference-only and raise rather than fall back to eager code.
 """
 
-import math
 
 import torch
 import torch.nn.functional as F
@@ -132,8 +131,21 @@ class ConditionedTransitionBlock(nn.Module):
         return forwards.conditioned_transition_forward(self, a, s)
 
 
+class _HeadsFirst(nn.Module):
+    """``proj_z`` of a bias-consuming AttentionPairBias: [B, N, N, H] -> [B, H, N, N]
+    as a view (upstream's ``Rearrange("b ... h -> b h ...")``)."""
+
+    def forward(self, z):
+        return z.permute(0, 3, 1, 2)
+
+
 class AttentionPairBias(nn.Module):
-    """fp32 single-track attention with pair bias (upstream attentionv2)."""
+    """fp32 single-track attention with pair bias (upstream attentionv2).
+
+    With ``compute_pair_bias`` the bias is LayerNorm(z) . W_z (the Pairformer
+    block); without it ``z`` is the bias itself, [B, N, N, H] (the diffusion
+    token transformer's layer slice of the prepared token bias).
+    """
 
     def __init__(self, c_s, c_z=None, num_heads=None, inf=1e6, compute_pair_bias=True):
         super().__init__()
@@ -145,19 +157,9 @@ class AttentionPairBias(nn.Module):
         self.proj_g = nn.Linear(c_s, c_s, bias=False)
         if compute_pair_bias:
             self.proj_z = nn.Sequential(nn.LayerNorm(c_z), nn.Linear(c_z, num_heads, bias=False))
+        else:
+            self.proj_z = _HeadsFirst()
         self.proj_o = nn.Linear(c_s, c_s, bias=False)
-
-    def _joint_weights(self):
-        params = (self.proj_q.weight, self.proj_q.bias, self.proj_k.weight, self.proj_v.weight, self.proj_g.weight)
-
-        def build():
-            w = torch.cat([self.proj_q.weight, self.proj_k.weight, self.proj_v.weight, self.proj_g.weight], 0)
-            bias = torch.zeros(w.shape[0], device=w.device, dtype=w.dtype)
-            if self.proj_q.bias is not None:
-                bias[: self.c_s] = self.proj_q.bias
-            return dict(w=w.contiguous(), b=bias)
-
-        return forwards._cached(self, "_bl_joint_qkvg", params, build)
 
     def pair_bias(self, z):
         """LayerNorm(z) . W_z in one pass, head-major [b, heads, N, N] (fp32)."""
@@ -172,29 +174,15 @@ class AttentionPairBias(nn.Module):
                       float(ln.eps), w_z.data_ptr(), self.num_heads, bias[i].data_ptr(), stream)
         return bias
 
-    def forward(self, s, z, mask, k_in):
+    def forward(self, s, z, mask, k_in, multiplicity=1):
         _inference_only(self)
-        bias = self.pair_bias(z) if self.compute_pair_bias else z
-        return self.attend(s, bias, mask, k_in)
+        if not self.compute_pair_bias:
+            return forwards.token_attention_forward(self, s, z, mask, k_in, multiplicity)
+        return self.attend(s, self.pair_bias(z), mask, k_in)
 
     def attend(self, s, bias, mask, k_in):
-        """The attention given the pair bias [b, heads, N, N] (fp32)."""
-        b = s.shape[0]
-        if k_in is s:  # one GEMM for q | k | v | g (the block passes the same normed s)
-            joint = self._joint_weights()
-            q, k, v, g = F.linear(s, joint["w"], joint["b"]).split(self.c_s, dim=-1)
-        else:
-            q = F.linear(s, self.proj_q.weight, self.proj_q.bias)
-            k, v = F.linear(k_in, self.proj_k.weight), F.linear(k_in, self.proj_v.weight)
-            g = F.linear(s, self.proj_g.weight)
-        q = q.reshape(b, -1, self.num_heads, self.head_dim)
-        k = k.reshape(b, -1, self.num_heads, self.head_dim)
-        v = v.reshape(b, -1, self.num_heads, self.head_dim)
-        g = torch.sigmoid(g)
-        attn = torch.einsum("bihd,bjhd->bhij", q, k) / math.sqrt(self.head_dim) + bias
-        attn = attn + (1 - mask[:, None, None].float()) * -self.inf
-        o = torch.einsum("bhij,bjhd->bihd", attn.softmax(dim=-1), v).reshape(b, -1, self.c_s)
-        return F.linear(g * o, self.proj_o.weight)
+        """The attention given the pair bias [b', heads, N, N] (fp32, b' dividing b)."""
+        return forwards.attend_with_bias(self, s, bias, mask, k_in)
 
 
 class _FP32Transition(Transition):

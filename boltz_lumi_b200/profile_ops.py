@@ -2,7 +2,10 @@
 
     python -m boltz_lumi_b200.profile_ops --op att_start --n 512 --iters 3
 
-Ops: tri_mul_out, tri_mul_in, att_start, att_end, transition, block.  Inputs
+Ops: tri_mul_out, tri_mul_in, att_start, att_end, transition, block, and the
+diffusion token transformer's attention: token_attention (the whole
+AttentionPairBias forward, c_s 768, 16 heads, a layer of a prepared 24-layer
+token bias, --mult samples) and token_core (bl_token_attention alone).  Inputs
 and weights are the benchmark's synthetic ones (seeded); z is updated in
 place like in the Pairformer block.  Prints the mean device time per call.
 """
@@ -11,7 +14,7 @@ import argparse
 
 import torch
 
-from . import forwards, layers
+from . import forwards, kernels, layers
 
 
 def seeded_block(seed=1234):
@@ -24,12 +27,31 @@ def seeded_block(seed=1234):
     return module.eval()
 
 
+def _token_ops(n, mult, layers_=24, heads=16, c_s=768):
+    torch.manual_seed(3)
+    module = layers.AttentionPairBias(c_s, num_heads=heads, compute_pair_bias=False).cuda().eval()
+    g = torch.Generator().manual_seed(9)
+    s = torch.randn(mult, n, c_s, generator=g).cuda()
+    raw = torch.randn(1, n, n, layers_ * heads, generator=g).cuda()
+    bias = forwards.prepare_token_bias(raw).view(1, n, n, layers_, heads)[:, :, :, 0]
+    del raw
+    mask = torch.ones(mult, n, device="cuda")
+    d = c_s // heads
+    q, k, v, gate = (torch.randn(mult, n, heads, d, generator=g).cuda() for _ in range(4))
+    return {
+        "token_attention": lambda: module(s, bias, mask, s, multiplicity=mult),
+        "token_core": lambda: kernels.token_attention(q, k, v, bias.permute(0, 3, 1, 2), mask, 1e6, gate=gate),
+    }
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--op", default="block",
-                        choices=["tri_mul_out", "tri_mul_in", "att_start", "att_end", "transition", "block"])
+                        choices=["tri_mul_out", "tri_mul_in", "att_start", "att_end", "transition", "block",
+                                 "token_attention", "token_core"])
     parser.add_argument("--n", type=int, default=512)
     parser.add_argument("--iters", type=int, default=3)
+    parser.add_argument("--mult", type=int, default=1, help="diffusion samples (token ops)")
     args = parser.parse_args()
     block = seeded_block().cuda()
     g = torch.Generator().manual_seed(7)
@@ -46,6 +68,8 @@ def main():
         "transition": lambda: forwards.transition_forward(block.transition_z, z, residual=z),
         "block": lambda: block(s, z, mask, pmask),
     }
+    if args.op.startswith("token"):
+        ops.update(_token_ops(n, args.mult))
     fn = ops[args.op]
     with torch.inference_mode():
         fn()

@@ -275,6 +275,27 @@ BL_API int bl_triangle_attention(const void *q, const void *k, const void *v, co
                                  void *out, int64_t out_ld, void *stream);
 
 /*
+ * Attention core of the diffusion token transformer, fp32 end to end:
+ *   out[b][i][h][:] = sigmoid(g[b][i][h][:]) * sum_j softmax_j(s) v[b][j][h][:],
+ *   s = (q[b][i][h] . k[b][j][h]) * scale + bias[b / bias_batch_div][h][i][j]
+ *       + inf * (mask[b][j] - 1)
+ * q, k, v and the gate logits g (NULL: no gate): fp32, element (b, i, h, e)
+ * at b*sb + i*si + h*sh + e (strides multiples of 4, q/k/v 16-byte aligned); bias: element (b', h, i, j) at
+ * b'*bias_sb + h*bias_sh + i*bias_sq + j*bias_sk, so a layer's slice of the
+ * prepared [B, L*H, N, N] token bias is passed without a copy and one bias
+ * row serves the bias_batch_div diffusion samples of its input; mask: fp32
+ * at b*mask_sb + j, or NULL for none; head_dim 24, 32, 48 or 64; out: fp32
+ * [batch][n][heads][head_dim] contiguous.  Replaces the einsum / bias / mask /
+ * softmax / einsum and the gate product of pair_bias.py:28-36 (prepared_forward).
+ */
+BL_API int bl_token_attention(const float *q, const float *k, const float *v, const float *g, int64_t sb,
+                              int64_t si, int64_t sh,
+                              const float *bias, int64_t bias_sb, int64_t bias_sh, int64_t bias_sq,
+                              int64_t bias_sk, int64_t bias_batch_div, const float *mask, int64_t mask_sb,
+                              float scale, float inf, int64_t batch, int64_t heads, int64_t n, int64_t head_dim,
+                              float *out, void *stream);
+
+/*
  * Pair transition (LayerNorm -> fc1|fc2 -> SwiGLU -> fc3, the bf16-autocast
  * contract) that allocates no device memory.  This entry point has no
  * counterpart in the reference; it exists for callers that may not allocate

@@ -148,3 +148,71 @@ def test_bench_reference_arm_rank_nonzero_exits_without_work(monkeypatch):
     monkeypatch.setenv("WORLD_SIZE", "2")
     ns = type("A", (), dict(steps=1, warmup=0, n=8, impl="reference"))()
     assert bench.run_reference(ns) == 0
+
+
+class _RecordingDiffusion(nn.Module):
+    """AtomDiffusion stand-in: sample() records the conditioning it receives."""
+
+    def __init__(self):
+        super().__init__()
+        self.score_model = nn.Module()
+        self.score_model.token_transformer = nn.Module()
+        self.score_model.token_transformer.attention = layers.AttentionPairBias(64, num_heads=4,
+                                                                                compute_pair_bias=False)
+        self.seen = []
+
+    def sample(self, atom_mask=None, diffusion_conditioning=None, multiplicity=1):
+        self.seen.append(diffusion_conditioning["token_trans_bias"])
+        return diffusion_conditioning["token_trans_bias"]
+
+
+def _token_model():
+    model = nn.Module()
+    model.structure_module = _RecordingDiffusion()
+    model.trunk_attention = layers.AttentionPairBias(64, c_z=128, num_heads=4)  # not in the token transformer
+    return model
+
+
+def test_install_rebinds_token_transformer_and_sample():
+    model = _token_model()
+    assert adapters.install(model, require_device=False) == 1
+    structure = model.structure_module
+    assert "forward" in structure.score_model.token_transformer.attention.__dict__
+    assert "forward" not in model.trunk_attention.__dict__
+    assert "sample" in structure.__dict__
+    adapters.uninstall(model)
+    assert "forward" not in structure.score_model.token_transformer.attention.__dict__
+    assert "sample" not in structure.__dict__
+
+
+def test_sample_wrapper_packs_token_bias_dense():
+    """Under inference the bias reaches sample() fp32 with head-major storage and
+    unchanged values (the reference's diffusion.py:16-18); with grad enabled
+    the original conditioning passes through untouched."""
+    model = _token_model().eval()
+    adapters.install(model, require_device=False)
+    raw = torch.randn(1, 6, 6, 8).to(torch.bfloat16)
+    cond = {"token_trans_bias": raw, "c": torch.zeros(1)}
+    with torch.inference_mode():
+        out = model.structure_module.sample(atom_mask=None, diffusion_conditioning=cond, multiplicity=2)
+    assert out.dtype == torch.float32 and torch.equal(out, raw.float())
+    assert out.permute(0, 3, 1, 2).is_contiguous()  # layer / head slices are dense [N, N] planes
+    assert cond["token_trans_bias"] is raw  # the caller's dict is not modified
+    out = model.structure_module.sample(atom_mask=None, diffusion_conditioning=cond)
+    assert out is raw
+
+
+def test_prepared_bias_layer_slices():
+    raw = torch.randn(2, 5, 5, 3 * 4)
+    prepared = forwards.prepare_token_bias(raw)
+    assert torch.equal(prepared, raw)
+    layer = prepared.view(2, 5, 5, 3, 4)[:, :, :, 1].permute(0, 3, 1, 2)
+    assert layer.stride()[-2:] == (5, 1)
+
+
+def test_token_attention_forward_rejects_bad_multiplicity():
+    module = layers.AttentionPairBias(64, num_heads=4, compute_pair_bias=False).eval()
+    s = torch.randn(3, 5, 64)
+    z = torch.randn(2, 5, 5, 4)
+    with torch.inference_mode(), pytest.raises(RuntimeError, match="multiplicity"):
+        forwards.token_attention_forward(module, s, z, torch.ones(3, 5), s, multiplicity=1)
