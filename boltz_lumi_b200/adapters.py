@@ -9,11 +9,12 @@ cover (for example the template module's narrower pair width) -- exactly as
 the reference does; they never fall back to a CPU path.
 """
 
+import contextlib
 from types import MethodType
 
 import torch
 
-from . import forwards
+from . import atom_conditioning, forwards
 
 _TRIANGLE_ATTENTION = {"TriangleAttention", "TriangleAttentionEndingNode"}
 _TRIANGLE_MULTIPLICATION = {"TriangleMultiplicationIncoming", "TriangleMultiplicationOutgoing"}
@@ -85,16 +86,17 @@ def _token_attention(self, s, z, mask, k_in, multiplicity=1):
     if (not _inference(self, s, z, mask, k_in) or self.compute_pair_bias or torch.is_autocast_enabled("cuda")):
         return cls.forward(self, s, z, mask, k_in, multiplicity)
     bias = self.proj_z(z)
-    if (not forwards.token_attention_supported(self, s, k_in, bias)
-            or bias.shape[0] * multiplicity not in (s.shape[0], 1)
-            or (mask is not None and tuple(mask.shape) != tuple(s.shape[:2]))):
+    if (not forwards.token_attention_supported(self, s, k_in, bias, mask)
+            or bias.shape[0] * multiplicity not in (s.shape[0], 1)):
         return cls.forward(self, s, z, mask, k_in, multiplicity)
     return forwards.attend_with_bias(self, s, bias, mask, k_in)
 
 
 def _sample(self, *args, **kwargs):
     """``AtomDiffusion.sample`` with the token-transformer bias packed dense
-    once per prediction (the reference's optimized_sample, diffusion.py:13-18)."""
+    once per prediction and, for one input and one sample, the atom
+    conditioning projections computed once for all steps (the reference's
+    optimized_sample, diffusion.py:13-23)."""
     sample = type(self).sample
     conditioning = kwargs.get("diffusion_conditioning")
     if torch.is_grad_enabled() or self.training or not conditioning or "token_trans_bias" not in conditioning:
@@ -102,7 +104,13 @@ def _sample(self, *args, **kwargs):
     conditioning = dict(conditioning)
     conditioning["token_trans_bias"] = forwards.prepare_token_bias(conditioning["token_trans_bias"])
     kwargs["diffusion_conditioning"] = conditioning
-    return sample(self, *args, **kwargs)
+    context = contextlib.nullcontext()
+    single = "c" in conditioning and conditioning["c"].shape[0] == 1
+    if kwargs.get("multiplicity", 1) == 1 and single and hasattr(getattr(self, "score_model", None),
+                                                                   "atom_attention_encoder"):
+        context = atom_conditioning.atom_conditioning_cache(self.score_model)
+    with context:
+        return sample(self, *args, **kwargs)
 
 
 def install(model, require_device=True):

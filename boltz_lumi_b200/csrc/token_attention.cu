@@ -10,18 +10,25 @@
 // diffusion samples of an input without repeating it.
 //
 // fp32 rules out the bf16 tensor cores, so this is a CUDA-core flash kernel:
-// one CTA = 64 queries of one (batch, head), 128 threads; each thread owns 4
-// queries x 8 keys of every 64-key tile (S accumulated with 16-byte shared
-// loads, 10 FMA per load) and 4 queries x head_dim/8 output dims.  K / V
-// tiles are double-buffered with cp.async; P goes through shared memory for
-// the P.V product; online softmax in fp32 with the MUFU exponent.
+// one CTA = 64 queries of one (batch, head), 128 threads, two CTAs per SM.
+// Thread (tq, tk) = (t / 8, t % 8) owns queries 4 tq .. 4 tq + 3 and keys
+// tk + 8 j (j < 8) of every 64-key tile for S, and output dims
+// tk * D / 8 .. of its 4 queries for O.  Per key tile:
+//   * K, V, the 64 x 64 bias block and the 64 mask values of the NEXT tile
+//     are in flight (cp.async, double-buffered) while this one is computed;
+//   * S accumulates on the packed fp32x2 pipe (even / odd head dims in the two
+//     halves, summed once per tile): 64 fma.rn.f32x2 per 12 16-byte loads;
+//   * the online softmax needs one max-reduction over the row's 8 lanes;
+//     row sums stay per lane until the end;
+//   * P overwrites the bias block it was computed from (each element by the
+//     thread that read it), and O += P V on the fp32x2 pipe.
 #include "common.cuh"
 
 namespace bl {
 namespace {
 
 constexpr int kBQ = 64, kBK = 64, kThreads = 128;
-constexpr int kMaxD = 64;
+constexpr int kPld = kBK + 4;  // bias / P row (floats); 16-byte aligned rows
 
 struct TokArgs {
   const float *q, *k, *v, *g;  // g (gate logits) may be null
@@ -29,27 +36,54 @@ struct TokArgs {
   const float *bias;
   int64_t bias_sb, bias_sh, bias_sq, bias_sk;
   int bias_div;
+  int bias_vec;       // bias rows dense and 16-byte aligned: staged in 16-byte chunks
   const float *mask;  // [B][N] at mask + b * mask_sb + k, or null
   int64_t mask_sb;
   float scale, inf;
-  int heads, n, d;
+  int heads, n;
   float *out;  // [B][N][H][d] contiguous
 };
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, int bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
 }
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void *src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(valid ? 4 : 0) : "memory");
+}
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void lds_v2b64(uint32_t addr, uint64_t &a, uint64_t &b) {
+  asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(addr));
+}
+__device__ __forceinline__ uint64_t lds_b64(uint32_t addr) {
+  uint64_t v;
+  asm volatile("ld.shared.b64 %0, [%1];" : "=l"(v) : "r"(addr));
+  return v;
+}
+// acc.{lo,hi} += a.{lo,hi} * b.{lo,hi}
+__device__ __forceinline__ void ffma2(uint64_t &acc, uint64_t a, uint64_t b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+__device__ __forceinline__ uint64_t dup2(float x) {
+  uint64_t v;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(v) : "f"(x));
+  return v;
+}
+__device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float(uint32_t(v)); }
+__device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float(uint32_t(v >> 32)); }
 
 template <int D>
-__global__ void __launch_bounds__(kThreads) token_attention_kernel(const TokArgs a) {
-  constexpr int kLd = D + 4;        // padded row (floats): conflict-free 16-byte row reads
-  constexpr int kDpt = D / 8;       // output dims per thread
+__global__ void __launch_bounds__(kThreads, 2) token_attention_kernel(const TokArgs a) {
+  constexpr int kLd = D + 4;   // padded row (floats): conflict-free 16-byte row reads
+  constexpr int kDpt = D / 8;  // output dims per thread
+  constexpr bool kPairs = kDpt % 2 == 0;
   extern __shared__ float4 smem4[];
   float *qs = reinterpret_cast<float *>(smem4);  // [64][kLd]
   float *ks = qs + kBQ * kLd;                    // [2][64][kLd]
   float *vs = ks + 2 * kBK * kLd;                // [2][64][kLd]
-  float *ps = vs + 2 * kBK * kLd;                // [64][kBK + 4]
-  constexpr int kPld = kBK + 4;
+  float *bs = vs + 2 * kBK * kLd;                // [2][64][kPld]: bias block, then P
+  float *ms = bs + 2 * kBQ * kPld;               // [2][64]: mask values
 
   const int t = threadIdx.x, tq = t >> 3, tk = t & 7;
   const int q0 = blockIdx.x * kBQ, h = blockIdx.y, b = blockIdx.z;
@@ -58,27 +92,46 @@ __global__ void __launch_bounds__(kThreads) token_attention_kernel(const TokArgs
   const float *bias = a.bias + int64_t(b / a.bias_div) * a.bias_sb + h * a.bias_sh;
   const float *mask = a.mask ? a.mask + b * a.mask_sb : nullptr;
 
-  // Q tile (rows past n are zero) and the first K / V tile.
+  // Q tile (rows past n are zero).
   constexpr int kChunks = D / 4;  // 16-byte chunks per row
   for (int i = t; i < kBQ * kChunks; i += kThreads) {
     const int r = i / kChunks, c = i % kChunks;
     const bool ok = q0 + r < n;
-    cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(qs + r * kLd + 4 * c)),
-               qb + (ok ? int64_t(q0 + r) * a.si + 4 * c : 0), ok);
+    cp_async16(smem_u32(qs + r * kLd + 4 * c), qb + (ok ? int64_t(q0 + r) * a.si + 4 * c : 0), ok ? 16 : 0);
   }
-  auto load_kv = [&](int tile, int buf) {
+  auto load_tile = [&](int tile, int buf) {
     const int k0 = tile * kBK;
     for (int i = t; i < kBK * kChunks; i += kThreads) {
       const int r = i / kChunks, c = i % kChunks;
       const bool ok = k0 + r < n;
       const int64_t off = ok ? int64_t(k0 + r) * a.si + 4 * c : 0;
-      cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(ks + (buf * kBK + r) * kLd + 4 * c)), kb + off, ok);
-      cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(vs + (buf * kBK + r) * kLd + 4 * c)), vb + off, ok);
+      cp_async16(smem_u32(ks + (buf * kBK + r) * kLd + 4 * c), kb + off, ok ? 16 : 0);
+      cp_async16(smem_u32(vs + (buf * kBK + r) * kLd + 4 * c), vb + off, ok ? 16 : 0);
     }
+    float *bt = bs + buf * kBQ * kPld;
+    if (a.bias_vec) {
+#pragma unroll 4
+      for (int i = t; i < kBQ * (kBK / 4); i += kThreads) {
+        const int r = i >> 4, c = 4 * (i & 15);
+        const int qi = q0 + r, kj = k0 + c;
+        const int left = n - kj;
+        const int bytes = qi < n ? (left >= 4 ? 16 : left > 0 ? 4 * left : 0) : 0;
+        cp_async16(smem_u32(bt + r * kPld + c), bias + (bytes ? int64_t(qi) * a.bias_sq + kj : 0), bytes);
+      }
+    } else {
+#pragma unroll 4
+      for (int i = t; i < kBQ * kBK; i += kThreads) {
+        const int r = i >> 6, c = i & 63;
+        const bool ok = q0 + r < n && k0 + c < n;
+        cp_async4(smem_u32(bt + r * kPld + c),
+                  bias + (ok ? int64_t(q0 + r) * a.bias_sq + int64_t(k0 + c) * a.bias_sk : 0), ok);
+      }
+    }
+    if (mask && t < kBK) cp_async4(smem_u32(ms + buf * kBK + t), mask + (k0 + t < n ? k0 + t : 0), k0 + t < n);
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
   const int n_tiles = (n + kBK - 1) / kBK;
-  load_kv(0, 0);
+  load_tile(0, 0);
 
   float m[4], l[4], o[4][kDpt];
 #pragma unroll
@@ -88,55 +141,55 @@ __global__ void __launch_bounds__(kThreads) token_attention_kernel(const TokArgs
     for (int e = 0; e < kDpt; ++e) o[i][e] = 0.f;
   }
   constexpr float kLog2e = 1.4426950408889634f;
+  const uint32_t q_base = smem_u32(qs + 4 * tq * kLd);
 
   for (int tile = 0; tile < n_tiles; ++tile) {
     const int buf = tile & 1, k0 = tile * kBK;
     if (tile + 1 < n_tiles) {
-      load_kv(tile + 1, buf ^ 1);  // the buffer was released by the barrier that ended tile - 1
+      load_tile(tile + 1, buf ^ 1);  // the buffers were released by the barrier that ended tile - 1
       asm volatile("cp.async.wait_group 1;" ::: "memory");
     } else {
       asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
     __syncthreads();
 
-    // S = Q K^T for 4 queries (4 tq + i) x 8 keys (tk + 8 j).
-    float s[4][8];
+    // S = Q K^T for queries 4 tq + i and keys tk + 8 j; even / odd dims in the two halves.
+    uint64_t acc[4][8];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) s[i][j] = 0.f;
-    const float *kt = ks + buf * kBK * kLd;
-#pragma unroll 2
+      for (int j = 0; j < 8; ++j) acc[i][j] = 0;
+    const uint32_t k_base = smem_u32(ks + (buf * kBK + tk) * kLd);
+#pragma unroll 3
     for (int e = 0; e < D; e += 4) {
-      float4 qv[4], kv[8];
+      uint64_t qa[4], qz[4], ka[8], kz[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4 *>(qs + (4 * tq + i) * kLd + e);
+      for (int i = 0; i < 4; ++i) lds_v2b64(q_base + (i * kLd + e) * 4, qa[i], qz[i]);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) kv[j] = *reinterpret_cast<const float4 *>(kt + (tk + 8 * j) * kLd + e);
+      for (int j = 0; j < 8; ++j) lds_v2b64(k_base + (8 * j * kLd + e) * 4, ka[j], kz[j]);
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          s[i][j] += qv[i].x * kv[j].x + qv[i].y * kv[j].y + qv[i].z * kv[j].z + qv[i].w * kv[j].w;
+        for (int j = 0; j < 8; ++j) {
+          ffma2(acc[i][j], qa[i], ka[j]);
+          ffma2(acc[i][j], qz[i], kz[j]);
+        }
     }
-    // Scale, bias, mask; then the online softmax over the 8 lanes of each query row.
+    // Logits (log2 domain), the row max over the 8 lanes, P into the bias block.
     float mk[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const int key = k0 + tk + 8 * j;
-      mk[j] = key < n ? (mask ? a.inf * (mask[key] - 1.f) : 0.f) : -INFINITY;
+      const int key = tk + 8 * j;
+      mk[j] = k0 + key < n ? (mask ? a.inf * (ms[buf * kBK + key] - 1.f) : 0.f) : -INFINITY;
     }
+    float *bt = bs + buf * kBQ * kPld + 4 * tq * kPld + tk;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int qi = q0 + 4 * tq + i;
-      const float *brow = bias + int64_t(qi < n ? qi : 0) * a.bias_sq;
-      float mx = -INFINITY;
+      float sc[8], mx = -INFINITY;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int key = k0 + tk + 8 * j;
-        const float bv = key < n ? __ldg(brow + int64_t(key) * a.bias_sk) : 0.f;
-        s[i][j] = s[i][j] * a.scale + bv + mk[j];
-        mx = fmaxf(mx, s[i][j]);
+        sc[j] = ((lo_f(acc[i][j]) + hi_f(acc[i][j])) * a.scale + bt[i * kPld + 8 * j]) + mk[j];
+        mx = fmaxf(mx, sc[j]);
       }
 #pragma unroll
       for (int off = 1; off < 8; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
@@ -145,42 +198,63 @@ __global__ void __launch_bounds__(kThreads) token_attention_kernel(const TokArgs
       float sum = 0.f;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float p = exp2f((s[i][j] - m_new) * kLog2e);  // padding keys: exp2(-inf) = 0
+        // s - max first (exact for logits on the same binade grid, e.g. two
+        // masked keys near -inf), then the base change; padding keys: exp2(-inf) = 0.
+        const float p = exp2f((sc[j] - m_new) * kLog2e);
         sum += p;
-        ps[(4 * tq + i) * kPld + tk + 8 * j] = p;
+        bt[i * kPld + 8 * j] = p;
       }
-#pragma unroll
-      for (int off = 1; off < 8; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-      l[i] = l[i] * alpha + sum;
+      l[i] = fmaf(l[i], alpha, sum);  // this lane's share of the row sum
       m[i] = m_new;
 #pragma unroll
       for (int e = 0; e < kDpt; ++e) o[i][e] *= alpha;
     }
     __syncwarp();  // a query row's P is written and read by the same 8 lanes
     // O += P V: 4 queries x kDpt contiguous dims (tk * kDpt ...).
-    const float *vt = vs + buf * kBK * kLd + tk * kDpt;
-#pragma unroll 4
+    const float *pt = bs + buf * kBQ * kPld + 4 * tq * kPld;
+    const uint32_t v_base = smem_u32(vs + buf * kBK * kLd + tk * kDpt);
+#pragma unroll 2
     for (int kk = 0; kk < kBK; kk += 4) {
       float4 pv[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) pv[i] = *reinterpret_cast<const float4 *>(ps + (4 * tq + i) * kPld + kk);
+      for (int i = 0; i < 4; ++i) pv[i] = *reinterpret_cast<const float4 *>(pt + i * kPld + kk);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        float vv[kDpt];
+        if constexpr (kPairs) {
+          uint64_t vv[kDpt / 2];
 #pragma unroll
-        for (int e = 0; e < kDpt; ++e) vv[e] = vt[(kk + u) * kLd + e];
+          for (int e = 0; e < kDpt / 2; ++e) vv[e] = lds_b64(v_base + ((kk + u) * kLd + 2 * e) * 4);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float p = u == 0 ? pv[i].x : u == 1 ? pv[i].y : u == 2 ? pv[i].z : pv[i].w;
+          for (int i = 0; i < 4; ++i) {
+            const float p = u == 0 ? pv[i].x : u == 1 ? pv[i].y : u == 2 ? pv[i].z : pv[i].w;
+            const uint64_t pp = dup2(p);
 #pragma unroll
-          for (int e = 0; e < kDpt; ++e) o[i][e] += p * vv[e];
+            for (int e = 0; e < kDpt / 2; ++e) {
+              uint64_t acc2 = (uint64_t(__float_as_uint(o[i][2 * e + 1])) << 32) | __float_as_uint(o[i][2 * e]);
+              ffma2(acc2, pp, vv[e]);
+              o[i][2 * e] = lo_f(acc2), o[i][2 * e + 1] = hi_f(acc2);
+            }
+          }
+        } else {
+          const float *vr = vs + buf * kBK * kLd + (kk + u) * kLd + tk * kDpt;
+          float vv[kDpt];
+#pragma unroll
+          for (int e = 0; e < kDpt; ++e) vv[e] = vr[e];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float p = u == 0 ? pv[i].x : u == 1 ? pv[i].y : u == 2 ? pv[i].z : pv[i].w;
+#pragma unroll
+            for (int e = 0; e < kDpt; ++e) o[i][e] = fmaf(p, vv[e], o[i][e]);
+          }
         }
       }
     }
-    __syncthreads();  // K / V buffer `buf` and P are free for the next tile
+    __syncthreads();  // K / V / bias buffer `buf` is free for the tile after next
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int off = 1; off < 8; off <<= 1) l[i] += __shfl_xor_sync(0xffffffffu, l[i], off);
     const int qi = q0 + 4 * tq + i;
     if (qi >= n) continue;
     const float inv = 1.f / l[i];
@@ -196,7 +270,7 @@ __global__ void __launch_bounds__(kThreads) token_attention_kernel(const TokArgs
 
 template <int D> int launch_token(const TokArgs &a, int batch, cudaStream_t stream) {
   constexpr int kLd = D + 4;
-  const int smem = (kBQ * kLd + 4 * kBK * kLd + kBQ * (kBK + 4)) * 4;
+  const int smem = (kBQ * kLd + 4 * kBK * kLd + 2 * kBQ * kPld + 2 * kBK) * 4;
   BL_CUDA(ensure_smem_limit(reinterpret_cast<const void *>(token_attention_kernel<D>), smem));
   dim3 grid((a.n + kBQ - 1) / kBQ, a.heads, batch);
   token_attention_kernel<D><<<grid, kThreads, smem, stream>>>(a);
@@ -229,9 +303,11 @@ extern "C" int bl_token_attention(const float *q, const float *k, const float *v
   a.q = q, a.k = k, a.v = v, a.g = g, a.sb = sb, a.si = si, a.sh = sh;
   a.bias = bias, a.bias_sb = bias_sb, a.bias_sh = bias_sh, a.bias_sq = bias_sq, a.bias_sk = bias_sk;
   a.bias_div = int(bias_batch_div);
+  a.bias_vec = bias_sk == 1 && bias_sq % 4 == 0 && bias_sh % 4 == 0 && (bias_batch_div >= batch || bias_sb % 4 == 0) &&
+               aligned_to(bias, 16);
   a.mask = mask, a.mask_sb = mask_sb;
   a.scale = scale, a.inf = inf;
-  a.heads = int(heads), a.n = int(n), a.d = int(head_dim);
+  a.heads = int(heads), a.n = int(n);
   a.out = out;
   cudaStream_t s = as_stream(stream);
   if (head_dim == 24) return launch_token<24>(a, int(batch), s);

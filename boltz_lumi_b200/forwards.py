@@ -19,7 +19,7 @@ how the Pairformer block applies ``z = z + op(z)`` without a separate pass.
 import torch
 import torch.nn.functional as F
 
-from . import _lib, kernels
+from . import _lib, atom_conditioning, kernels
 from ._lib import call, stream_of
 
 _BF16 = torch.bfloat16
@@ -291,11 +291,14 @@ def adaln_forward(self, a, s):
     """Upstream ``AdaLN.forward(a, s)`` (the reference's diffusion.py:52-57), fp32."""
     if a.dtype != torch.float32 or s.dtype != torch.float32:
         raise RuntimeError("AdaLN kernels are fp32")
-    with torch.autocast("cuda", enabled=False):
+
+    def conditioning():  # depends on s only: reused across steps inside atom_conditioning_cache
         sn = kernels.layer_norm(s, self.s_norm.weight, getattr(self.s_norm, "bias", None), self.s_norm.eps,
                                 out_dtype=torch.float32)
-        scale = F.linear(sn, self.s_scale.weight, self.s_scale.bias)
-        shift = F.linear(sn, self.s_bias.weight, self.s_bias.bias)
+        return F.linear(sn, self.s_scale.weight, self.s_scale.bias), F.linear(sn, self.s_bias.weight, self.s_bias.bias)
+
+    with torch.autocast("cuda", enabled=False):
+        scale, shift = atom_conditioning.lookup(self, "adaln", s, conditioning)
         return kernels.adaln_modulate(a, scale, shift, self.a_norm.eps)
 
 
@@ -306,7 +309,8 @@ def conditioned_transition_forward(self, a, s):
         projected = F.linear(a, self.swish_gate[0].weight, self.swish_gate[0].bias)
         third = F.linear(a, self.a_to_b.weight, self.a_to_b.bias)
         b = kernels.epilogue(projected.contiguous(), third.contiguous(), None, kernels.GATED_SWIGLU)
-        gate = F.linear(s, self.output_projection[0].weight, self.output_projection[0].bias)
+        gate = atom_conditioning.lookup(
+            self, "gate", s, lambda: F.linear(s, self.output_projection[0].weight, self.output_projection[0].bias))
         return kernels.epilogue(gate.contiguous(), F.linear(b, self.b_to_a.weight, self.b_to_a.bias).contiguous(),
                                 None, kernels.GATE)
 
@@ -343,13 +347,14 @@ def _qkvg_weights(module):
     return _cached(module, "_bl_joint_qkvg", params, build)
 
 
-def token_attention_supported(module, s, k_in, bias):
+def token_attention_supported(module, s, k_in, bias, mask=None):
     """Shapes and dtypes the fused fp32 token attention covers."""
     heads, d = module.num_heads, module.head_dim
     return (d in _TOKEN_HEAD_DIMS and heads * d == module.c_s and s.dim() == 3 and s.dtype == torch.float32
-            and k_in.dtype == torch.float32 and k_in.shape == s.shape and s.shape[-1] == module.c_s
+            and s.is_cuda and k_in.dtype == torch.float32 and k_in.shape == s.shape and s.shape[-1] == module.c_s
             and bias.dim() == 4 and tuple(bias.shape[1:]) == (heads, s.shape[1], s.shape[1])
-            and bias.shape[0] >= 1 and s.shape[0] % bias.shape[0] == 0
+            and bias.shape[0] >= 1 and s.shape[0] % bias.shape[0] == 0 and bias.device == s.device
+            and (mask is None or tuple(mask.shape) == tuple(s.shape[:2]))
             and all(p.bias is None for p in (module.proj_k, module.proj_v, module.proj_g)))
 
 
@@ -361,19 +366,37 @@ def attend_with_bias(self, s, bias, mask, k_in):
     ``b`` reads bias ``b // (B / B')``).  When ``k_in is s`` the four input
     projections run as one GEMM over stacked weights.
     """
+    if not token_attention_supported(self, s, k_in, bias, mask):
+        raise RuntimeError(f"token attention covers fp32 CUDA s [B, N, H*d] with d in {_TOKEN_HEAD_DIMS}, "
+                           f"bias [B', H, N, N] and mask [B, N]; got s {tuple(s.shape)}, bias {tuple(bias.shape)}")
     b, n = s.shape[0], s.shape[1]
     heads, d, c = self.num_heads, self.head_dim, self.c_s
-    with torch.autocast("cuda", enabled=False):
-        if k_in is s:
-            w, w_bias = _qkvg_weights(self)
-            q, k, v, g = F.linear(s, w, w_bias).view(b, n, 4, heads, d).unbind(2)
-        else:  # four contiguous [B, N, c_s] projections share one stride layout
-            q = F.linear(s, self.proj_q.weight, self.proj_q.bias).view(b, n, heads, d)
-            k = F.linear(k_in, self.proj_k.weight).view(b, n, heads, d)
-            v = F.linear(k_in, self.proj_v.weight).view(b, n, heads, d)
-            g = F.linear(s, self.proj_g.weight).view(b, n, heads, d)
-        out = kernels.token_attention(q, k, v, bias.float(), mask, self.inf, gate=g)
-    return self.proj_o(out.view(b, n, c))
+    if torch.is_autocast_enabled("cuda"):  # the reference's math is fp32 throughout
+        with torch.autocast("cuda", enabled=False):
+            return attend_with_bias(self, s, bias, mask, k_in)
+    if bias.dtype != torch.float32:
+        bias = bias.float()
+    if mask is not None and (mask.dtype != torch.float32 or mask.stride(-1) != 1):
+        mask = mask.float().contiguous()
+    if b == 0 or n == 0:
+        return self.proj_o(s.new_zeros(b, n, c))
+    out = torch.empty(b, n, c, device=s.device, dtype=torch.float32)
+    stream = stream_of(s)
+    if k_in is s:
+        # One GEMM for q | k | v | g; the kernel reads the four column blocks in place.
+        w, w_bias = _qkvg_weights(self)
+        proj = F.linear(s, w, w_bias)
+        base = proj.data_ptr()
+        kernels.launch_token_attention(base, base + 4 * c, base + 8 * c, base + 12 * c, (n * 4 * c, 4 * c, d), bias,
+                                       mask, self.inf, b, heads, n, d, out, stream)
+    else:  # four contiguous [B, N, c_s] projections share one stride layout
+        q = F.linear(s, self.proj_q.weight, self.proj_q.bias)
+        k = F.linear(k_in, self.proj_k.weight)
+        v = F.linear(k_in, self.proj_v.weight)
+        g = F.linear(s, self.proj_g.weight)
+        kernels.launch_token_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), (n * c, c, d), bias,
+                                       mask, self.inf, b, heads, n, d, out, stream)
+    return self.proj_o(out)
 
 
 def token_attention_forward(self, s, z, mask, k_in, multiplicity=1):

@@ -7,6 +7,8 @@ CUDA stream of the input's device.  Errors raise ``RuntimeError``; there is
 no fallback path.
 """
 
+import functools
+
 import torch
 
 from . import _lib
@@ -225,10 +227,22 @@ def bmm(a, b_t, bias=None, out=None):
     return out
 
 
+@functools.lru_cache(maxsize=None)
 def attention_scale(head_dim):
     """fp32(1 / fp32(sqrt(head_dim))): the factor torch's CUDA division by the
     Python scalar ``head_dim ** 0.5`` applies (pair_bias.py:31)."""
     return float(torch.tensor(1.0, dtype=torch.float32) / torch.tensor(head_dim ** 0.5, dtype=torch.float32))
+
+
+def launch_token_attention(q_ptr, k_ptr, v_ptr, g_ptr, strides, bias, mask, inf, batch, heads, n, d, out, stream):
+    """bl_token_attention on raw operand pointers sharing ``strides`` (batch,
+    token, head) -- no validation; callers have checked shapes and dtypes."""
+    mask_ptr, mask_sb = (None, 0) if mask is None else (mask.data_ptr(), mask.stride(0))
+    bs = bias.stride()
+    call("bl_token_attention", q_ptr, k_ptr, v_ptr, g_ptr, strides[0], strides[1], strides[2], bias.data_ptr(),
+         bs[0], bs[1], bs[2], bs[3], batch // bias.shape[0], mask_ptr, mask_sb, attention_scale(d), float(inf),
+         batch, heads, n, d, out.data_ptr(), stream)
+    return out
 
 
 def token_attention(q, k, v, bias, mask, inf, gate=None, scale=None):
@@ -266,6 +280,8 @@ def token_attention(q, k, v, bias, mask, inf, gate=None, scale=None):
     if scale is None:
         scale = attention_scale(d)
     out = torch.empty(batch, n, heads, d, device=q.device, dtype=torch.float32)
+    if n == 0 or batch == 0:
+        return out
     call("bl_token_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), ptr(gate), q.stride(0), q.stride(1),
          q.stride(2), bias.data_ptr(), bias.stride(0), bias.stride(1), bias.stride(2), bias.stride(3),
          batch // bias.shape[0], ptr(mask), mask_sb, float(scale), float(inf), batch, heads, n, d, out.data_ptr(),

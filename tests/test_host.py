@@ -216,3 +216,32 @@ def test_token_attention_forward_rejects_bad_multiplicity():
     z = torch.randn(2, 5, 5, 4)
     with torch.inference_mode(), pytest.raises(RuntimeError, match="multiplicity"):
         forwards.token_attention_forward(module, s, z, torch.ones(3, 5), s, multiplicity=1)
+
+
+def test_atom_conditioning_context_installs_and_restores():
+    from boltz_lumi_b200 import atom_conditioning
+
+    def stack():
+        t = nn.Module()
+        t.diffusion_transformer = nn.Module()
+        layer = nn.Module()
+        layer.adaln = layers.AdaLN(16, 16)
+        layer.output_projection_linear = nn.Linear(16, 16)
+        layer.transition = layers.ConditionedTransitionBlock(16, 16)
+        t.diffusion_transformer.layers = nn.ModuleList([layer])
+        return t, layer
+
+    score = nn.Module()
+    score.atom_attention_encoder = nn.Module()
+    score.atom_attention_decoder = nn.Module()
+    score.atom_attention_encoder.atom_encoder, enc = stack()
+    score.atom_attention_decoder.atom_decoder, dec = stack()
+    linear = enc.output_projection_linear
+    with atom_conditioning.atom_conditioning_cache(score):
+        assert "forward" in linear.__dict__ and "forward" in enc.adaln.s_scale.__dict__
+        assert atom_conditioning.CACHE_ATTR in dec.transition.__dict__
+        x = torch.randn(2, 16)
+        with torch.no_grad():
+            assert torch.equal(linear(x), nn.Linear.forward(linear, x))  # CPU input: computed, not cached
+    assert "forward" not in linear.__dict__ and "forward" not in enc.adaln.s_scale.__dict__
+    assert atom_conditioning.CACHE_ATTR not in dec.transition.__dict__
