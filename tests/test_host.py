@@ -245,3 +245,43 @@ def test_atom_conditioning_context_installs_and_restores():
             assert torch.equal(linear(x), nn.Linear.forward(linear, x))  # CPU input: computed, not cached
     assert "forward" not in linear.__dict__ and "forward" not in enc.adaln.s_scale.__dict__
     assert atom_conditioning.CACHE_ATTR not in dec.transition.__dict__
+
+
+def test_benchmark_field_errors_and_summary():
+    from boltz_lumi_b200 import benchmark
+
+    coords = torch.zeros(1, 5, 3, dtype=torch.float64)
+    moved = coords.clone()
+    moved[0, 0, 0] = 0.2  # one atom 0.2 A away: RMSD = sqrt(0.04 / 5)
+    rec = benchmark.field_error("coords", moved, coords)
+    assert abs(rec["rmsd"] - (0.04 / 5) ** 0.5) < 1e-12 and rec["within_bound"]
+    far = benchmark.field_error("coords", coords + 1.0, coords)
+    assert far["rmsd"] > 0.1 and not far["within_bound"]
+    pl = benchmark.field_error("plddt", torch.tensor([0.5, 0.7]), torch.tensor([0.5, 0.705]))
+    assert pl["metric"] == "max_abs" and pl["within_bound"] and pl["differing_values"] == 1
+    other = benchmark.field_error("ptm", torch.tensor([0.3]), torch.tensor([0.2]))
+    assert "within_bound" not in other
+    report = {"model_calls": [
+        dict(recipe="upstream", first=True, model_s=9.0, stages_s={"pairformer_module": 5.0}),
+        dict(recipe="upstream", first=False, model_s=4.0, stages_s={"pairformer_module": 2.0}),
+        dict(recipe="optimized", first=True, model_s=3.0, stages_s={}),
+        dict(recipe="optimized", first=False, model_s=1.0, stages_s={"pairformer_module": 0.5}),
+    ], "errors": [rec, pl, other]}
+    benchmark.summarize(report)
+    assert report["upstream_warm_mean_s"] == 4.0 and report["optimized_warm_mean_s"] == 1.0
+    assert report["saved_s"] == 3.0 and report["speedup"] == 4.0 and report["status"] == "complete"
+    assert report["optimized_warm_stages_s"] == {"pairformer_module": 0.5}
+    report["errors"].append(far)
+    assert benchmark.summarize(report)["status"] == "outside_tolerance"
+
+
+def test_benchmark_cli_needs_upstream_boltz():
+    from boltz_lumi_b200 import benchmark
+
+    try:
+        import boltz  # noqa: F401
+        pytest.skip("upstream boltz is installed")
+    except ImportError:
+        pass
+    with pytest.raises(SystemExit, match="boltz"):
+        benchmark.main(["predict", "input.yaml"])

@@ -85,6 +85,20 @@ def test_pair_transition(n):
             assert_close(actual.float(), expected, atol=BF16_ATOL)
 
 
+@pytest.mark.parametrize("dim,hidden", [(64, 256), (256, 1024), (128, 256)])
+def test_pair_transition_other_widths(dim, hidden):
+    """Widths other than the trunk's 128 -> 512 -> 128 (the template module's
+    pair stack runs c_z = 64 with hidden 256) take the unfused-width path:
+    LayerNorm, fc1|fc2 GEMM, SwiGLU, fc3 GEMM on the same kernels."""
+    mod, ref = build(layers.Transition, oracle.Transition, dim, hidden, std=0.05)
+    x = torch.randn(1, 37, 37, dim, generator=torch.Generator().manual_seed(dim + hidden))
+    expected = ref(x)
+    with torch.inference_mode():
+        actual = mod(x.cuda())
+    assert actual.shape == (1, 37, 37, dim)
+    assert_close(actual.float(), expected, atol=BF16_ATOL)
+
+
 @pytest.mark.parametrize("rows", [1, 129, 5000])
 def test_pair_transition_residual_in_place(rows):
     """z += Transition(z) with z both the input and the residual (the block's
