@@ -14,7 +14,7 @@ from types import MethodType
 
 import torch
 
-from . import atom_conditioning, forwards
+from . import atom_conditioning, forwards, graphs
 
 _TRIANGLE_ATTENTION = {"TriangleAttention", "TriangleAttentionEndingNode"}
 _TRIANGLE_MULTIPLICATION = {"TriangleMultiplicationIncoming", "TriangleMultiplicationOutgoing"}
@@ -109,11 +109,29 @@ def _sample(self, *args, **kwargs):
     if kwargs.get("multiplicity", 1) == 1 and single and hasattr(getattr(self, "score_model", None),
                                                                    "atom_attention_encoder"):
         context = atom_conditioning.atom_conditioning_cache(self.score_model)
-    with context:
+    with context, _graphed_score_model(self):
         return sample(self, *args, **kwargs)
 
 
-def install(model, require_device=True):
+@contextlib.contextmanager
+def _graphed_score_model(structure):
+    """With ``install(model, cuda_graphs=True)``: the score model's forward
+    replays a CUDA graph from the third diffusion step on, for this sampling
+    call only (features and conditioning change between predictions)."""
+    score_model = getattr(structure, "score_model", None)
+    if not getattr(structure, "_b200_cuda_graphs", False) or score_model is None or "forward" in score_model.__dict__:
+        yield
+        return
+    step = graphs.GraphedStep(score_model.forward)
+    score_model.forward = step
+    try:
+        yield
+    finally:
+        del score_model.forward
+        step.reset()
+
+
+def install(model, require_device=True, cuda_graphs=False):
     """Rebind the hot-path forwards of ``model`` in place; idempotent.
 
     Returns the number of modules rebound.  Like the reference, modules are
@@ -123,7 +141,10 @@ def install(model, require_device=True):
     ``structure_module.score_model`` and the AttentionPairBias modules under
     ``structure_module.score_model.token_transformer``; and, like the
     reference (adapters.py:46), wraps ``structure_module.sample`` so the token
-    bias is packed once per prediction.
+    bias is packed once per prediction.  ``cuda_graphs=True`` additionally
+    replays the score model of each sampling call from a CUDA graph
+    (:mod:`boltz_lumi_b200.graphs`); it needs a capture-safe score model and is
+    off by default.
     """
     if getattr(model, "_b200_optimized", False):
         return 0
@@ -150,6 +171,7 @@ def install(model, require_device=True):
     structure = getattr(model, "structure_module", None)
     if structure is not None and callable(getattr(type(structure), "sample", None)):
         structure.sample = MethodType(_sample, structure)
+        structure._b200_cuda_graphs = bool(cuda_graphs)
     model._b200_optimized = True
     return count
 
@@ -164,4 +186,5 @@ def uninstall(model):
     structure = getattr(model, "structure_module", None)
     if structure is not None and getattr(structure.__dict__.get("sample"), "__func__", None) is _sample:
         del structure.sample
+        structure.__dict__.pop("_b200_cuda_graphs", None)
     model._b200_optimized = False

@@ -285,3 +285,21 @@ def test_benchmark_cli_needs_upstream_boltz():
         pass
     with pytest.raises(SystemExit, match="boltz"):
         benchmark.main(["predict", "input.yaml"])
+
+
+def test_graph_step_argument_plumbing():
+    """GraphedStep's signature and leaf order (CPU: no capture here)."""
+    from boltz_lumi_b200 import graphs
+
+    a, b, c = torch.zeros(1), torch.ones(2, 3)[:, :2], torch.full((3,), 2.0)
+    obj = ((a, [b]), {"z": b, "a": c, "n": 3, "f": len})
+    leaves = []
+    key = graphs._flatten(obj, leaves)
+    rebuilt = graphs._rebuild(obj, leaves, iter(range(len(leaves))))
+    assert rebuilt[0][0] is a and rebuilt[0][1][0] is b and rebuilt[1]["a"] is c and rebuilt[1]["z"] is b
+    assert rebuilt[1]["n"] == 3 and rebuilt[1]["f"] is len
+    other = []
+    assert graphs._flatten(((a, [b.contiguous()]), {"z": b, "a": c, "n": 3, "f": len}), other) != key  # strides
+    assert graphs._flatten(((a, [b]), {"z": b, "a": c, "n": 4, "f": len}), []) != key  # a Python value
+    same = []
+    assert graphs._flatten(((a.clone(), [b]), {"z": b, "a": c, "n": 3, "f": len}), same) == key
