@@ -265,6 +265,11 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
 __device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&a)[16], uint32_t (&b)[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" : BL_R16(a), BL_R16(b)::"memory");
 }
+__device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&a)[32]) {
+  uint32_t(&a0)[16] = *reinterpret_cast<uint32_t(*)[16]>(&a[0]);
+  uint32_t(&a1)[16] = *reinterpret_cast<uint32_t(*)[16]>(&a[16]);
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : BL_R16(a0), BL_R16(a1)::"memory");
+}
 __device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&a)[32], uint32_t (&b)[32]) {
   uint32_t(&a0)[16] = *reinterpret_cast<uint32_t(*)[16]>(&a[0]);
   uint32_t(&a1)[16] = *reinterpret_cast<uint32_t(*)[16]>(&a[16]);

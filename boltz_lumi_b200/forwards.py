@@ -81,6 +81,44 @@ def _linear_out(a, w, rows, k, stream, bias=None, a2=None, k1=None, gate=False, 
          None if out is None else out.data_ptr(), 0 if out is None else out.shape[-1], stream)
 
 
+def _split_weight(module, name, weights, biases=None):
+    """bf16 split planes [3, N, K] of the row-concatenated fp32 ``weights``
+    (and their joint fp32 bias, zeros where a part has none), cached on the
+    module until a source parameter changes."""
+    biases = list(biases) if biases is not None else [None] * len(weights)
+    params = tuple(weights) + tuple(b for b in biases if b is not None)
+
+    def build():
+        w = torch.cat([x.float() for x in weights], 0).contiguous()
+        bias = None
+        if any(b is not None for b in biases):
+            bias = torch.cat([b.float() if b is not None else torch.zeros(x.shape[0], device=w.device)
+                              for x, b in zip(weights, biases)]).contiguous()
+        return kernels.split3(w), bias
+
+    return _cached(module, name, params, build)
+
+
+def _linear32(module, name, x, weights, biases=None, x3=None):
+    """fp32 ``x @ [W_1; W_2; ...]^T + bias`` (upstream's fp32 nn.Linear calls,
+    autocast off) on the tensor cores via the three-way bf16 split
+    (bl_linear_split3); shapes it does not cover stay on cuBLAS fp32."""
+    n = sum(w.shape[0] for w in weights)
+    if not kernels.linear_f32_supported(x, n):
+        w = torch.cat(list(weights), 0) if len(weights) > 1 else weights[0]
+        bias = None
+        if biases is not None and any(b is not None for b in biases):
+            bias = torch.cat([b if b is not None else w.new_zeros(p.shape[0]) for p, b in zip(weights, biases)])
+        return F.linear(x, w, bias)
+    w3, bias = _split_weight(module, name, weights, biases)
+    return kernels.linear_f32(x, w3, bias, x3=x3)
+
+
+def _split_input(x, n_min=4):
+    """split3(x) when x can feed bl_linear_split3, else None."""
+    return kernels.split3(x) if kernels.linear_f32_supported(x, n_min) else None
+
+
 # ---------------------------------------------------------------------------
 # Triangle attention (starting / ending node)
 # ---------------------------------------------------------------------------
@@ -295,7 +333,9 @@ def adaln_forward(self, a, s):
     def conditioning():  # depends on s only: reused across steps inside atom_conditioning_cache
         sn = kernels.layer_norm(s, self.s_norm.weight, getattr(self.s_norm, "bias", None), self.s_norm.eps,
                                 out_dtype=torch.float32)
-        return F.linear(sn, self.s_scale.weight, self.s_scale.bias), F.linear(sn, self.s_bias.weight, self.s_bias.bias)
+        sn3 = _split_input(sn)
+        return (_linear32(self, "_bl_w3_scale", sn, [self.s_scale.weight], [self.s_scale.bias], x3=sn3),
+                _linear32(self, "_bl_w3_shift", sn, [self.s_bias.weight], [self.s_bias.bias], x3=sn3))
 
     with torch.autocast("cuda", enabled=False):
         scale, shift = atom_conditioning.lookup(self, "adaln", s, conditioning)
@@ -306,13 +346,14 @@ def conditioned_transition_forward(self, a, s):
     """Upstream ``ConditionedTransitionBlock.forward(a, s)`` (diffusion.py:60-68), fp32."""
     with torch.autocast("cuda", enabled=False):
         a = adaln_forward(self.adaln, a, s)
-        projected = F.linear(a, self.swish_gate[0].weight, self.swish_gate[0].bias)
-        third = F.linear(a, self.a_to_b.weight, self.a_to_b.bias)
+        a3 = _split_input(a)
+        projected = _linear32(self, "_bl_w3_swish", a, [self.swish_gate[0].weight], [self.swish_gate[0].bias], x3=a3)
+        third = _linear32(self, "_bl_w3_atob", a, [self.a_to_b.weight], [self.a_to_b.bias], x3=a3)
         b = kernels.epilogue(projected.contiguous(), third.contiguous(), None, kernels.GATED_SWIGLU)
-        gate = atom_conditioning.lookup(
-            self, "gate", s, lambda: F.linear(s, self.output_projection[0].weight, self.output_projection[0].bias))
-        return kernels.epilogue(gate.contiguous(), F.linear(b, self.b_to_a.weight, self.b_to_a.bias).contiguous(),
-                                None, kernels.GATE)
+        op = self.output_projection[0]
+        gate = atom_conditioning.lookup(self, "gate", s, lambda: _linear32(self, "_bl_w3_gate", s, [op.weight], [op.bias]))
+        out = _linear32(self, "_bl_w3_btoa", b, [self.b_to_a.weight], [self.b_to_a.bias])
+        return kernels.epilogue(gate.contiguous(), out.contiguous(), None, kernels.GATE)
 
 
 # ---------------------------------------------------------------------------
@@ -329,22 +370,6 @@ def prepare_token_bias(value):
     the attention kernel (the reference's prepare_token_bias, pair_bias.py:6-12).
     """
     return value.permute(0, 3, 1, 2).contiguous().float().permute(0, 2, 3, 1)
-
-
-def _qkvg_weights(module):
-    """proj_q | proj_k | proj_v | proj_g stacked into one [4 c_s, c_s] weight
-    (proj_q's bias, zeros for the others), rebuilt when a source changes."""
-    params = (module.proj_q.weight, module.proj_q.bias, module.proj_k.weight, module.proj_v.weight,
-              module.proj_g.weight)
-
-    def build():
-        w = torch.cat([module.proj_q.weight, module.proj_k.weight, module.proj_v.weight, module.proj_g.weight], 0)
-        bias = torch.zeros(w.shape[0], device=w.device, dtype=w.dtype)
-        if module.proj_q.bias is not None:
-            bias[: module.c_s] = module.proj_q.bias
-        return w.contiguous(), bias
-
-    return _cached(module, "_bl_joint_qkvg", params, build)
 
 
 def token_attention_supported(module, s, k_in, bias, mask=None):
@@ -384,19 +409,21 @@ def attend_with_bias(self, s, bias, mask, k_in):
     stream = stream_of(s)
     if k_in is s:
         # One GEMM for q | k | v | g; the kernel reads the four column blocks in place.
-        w, w_bias = _qkvg_weights(self)
-        proj = F.linear(s, w, w_bias)
+        proj = _linear32(self, "_bl_w3_qkvg", s,
+                         [self.proj_q.weight, self.proj_k.weight, self.proj_v.weight, self.proj_g.weight],
+                         [self.proj_q.bias, None, None, None])
         base = proj.data_ptr()
         kernels.launch_token_attention(base, base + 4 * c, base + 8 * c, base + 12 * c, (n * 4 * c, 4 * c, d), bias,
                                        mask, self.inf, b, heads, n, d, out, stream)
     else:  # four contiguous [B, N, c_s] projections share one stride layout
-        q = F.linear(s, self.proj_q.weight, self.proj_q.bias)
-        k = F.linear(k_in, self.proj_k.weight)
-        v = F.linear(k_in, self.proj_v.weight)
-        g = F.linear(s, self.proj_g.weight)
+        s3, k3 = _split_input(s), _split_input(k_in)
+        q = _linear32(self, "_bl_w3_q", s, [self.proj_q.weight], [self.proj_q.bias], x3=s3)
+        k = _linear32(self, "_bl_w3_k", k_in, [self.proj_k.weight], x3=k3)
+        v = _linear32(self, "_bl_w3_v", k_in, [self.proj_v.weight], x3=k3)
+        g = _linear32(self, "_bl_w3_g", s, [self.proj_g.weight], x3=s3)
         kernels.launch_token_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), (n * c, c, d), bias,
                                        mask, self.inf, b, heads, n, d, out, stream)
-    return self.proj_o(out)
+    return _linear32(self, "_bl_w3_o", out, [self.proj_o.weight], [self.proj_o.bias])
 
 
 def token_attention_forward(self, s, z, mask, k_in, multiplicity=1):

@@ -287,3 +287,42 @@ def token_attention(q, k, v, bias, mask, inf, gate=None, scale=None):
          batch // bias.shape[0], ptr(mask), mask_sb, float(scale), float(inf), batch, heads, n, d, out.data_ptr(),
          stream_of(q))
     return out
+
+
+def split3(x):
+    """fp32 ``x`` [..., K] -> bf16 planes [3, rows, K] with x = x1 + x2 + x3
+    (bl_split3_bf16); the operand form of :func:`linear_f32`."""
+    _require_cuda(x)
+    if x.dtype != torch.float32:
+        raise RuntimeError("split3 expects fp32")
+    cols = x.shape[-1]
+    x2 = x.reshape(-1, cols)
+    if x2.stride(-1) != 1 or x2.data_ptr() % 16 or x2.stride(0) % 4:
+        x2 = x2.contiguous()
+    out = torch.empty(3, x2.shape[0], cols, device=x.device, dtype=torch.bfloat16)
+    call("bl_split3_bf16", x2.data_ptr(), x2.shape[0], cols, x2.stride(0), out.data_ptr(), stream_of(x))
+    return out
+
+
+def linear_f32_supported(x, n):
+    return x.is_cuda and x.dtype == torch.float32 and x.shape[-1] % 8 == 0 and n % 4 == 0
+
+
+def linear_f32(x, w3, bias=None, x3=None):
+    """fp32 ``x @ W^T + bias`` on the tensor cores with fp32-GEMM accuracy
+    (bl_linear_split3).  ``w3`` = ``split3(W)`` (bf16 [3, N, K]); ``x3`` may
+    pass ``split3(x)`` when one input feeds several linears."""
+    _require_inference(x)
+    _require_cuda(x, w3, bias)
+    k = x.shape[-1]
+    n = w3.shape[1]
+    if w3.shape != (3, n, k) or w3.dtype != torch.bfloat16:
+        raise RuntimeError(f"w3 must be bf16 [3, N, {k}]")
+    if bias is not None and (bias.dtype != torch.float32 or bias.numel() != n or not bias.is_contiguous()):
+        raise RuntimeError("bias must be contiguous fp32 with N elements")
+    if x3 is None:
+        x3 = split3(x)
+    m = x3.shape[1]
+    y = torch.empty(*x.shape[:-1], n, device=x.device, dtype=torch.float32)
+    call("bl_linear_split3", x3.data_ptr(), m, k, w3.data_ptr(), n, ptr(bias), y.data_ptr(), n, stream_of(x))
+    return y

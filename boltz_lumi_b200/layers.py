@@ -192,10 +192,9 @@ class _FP32Transition(Transition):
         _inference_only(self)
         xn = kernels.layer_norm(x.contiguous(), self.norm.weight, self.norm.bias, self.norm.eps,
                                 out_dtype=torch.float32)
-        w12 = forwards._cached(self, "_bl_fc12", (self.fc1.weight, self.fc2.weight),
-                               lambda: torch.cat([self.fc1.weight, self.fc2.weight], 0).contiguous())
-        a, b = F.linear(xn, w12).split(self.fc1.weight.shape[0], dim=-1)
-        return F.linear(F.silu(a) * b, self.fc3.weight)
+        h = forwards._linear32(self, "_bl_w3_fc12", xn, [self.fc1.weight, self.fc2.weight])
+        a, b = h.split(self.fc1.weight.shape[0], dim=-1)
+        return forwards._linear32(self, "_bl_w3_fc3", F.silu(a) * b, [self.fc3.weight])
 
 
 class PairformerLayer(nn.Module):

@@ -296,6 +296,24 @@ BL_API int bl_token_attention(const float *q, const float *k, const float *v, co
                               float *out, void *stream);
 
 /*
+ * fp32-accurate linear layers on the bf16 tensor cores (three-way split).
+ * bl_split3_bf16: out = bf16 planes [3][rows][cols] with x = x1 + x2 + x3
+ *   (x1 = bf16(x), x2 = bf16(x - x1), x3 = bf16(x - x1 - x2); |x - sum| <=
+ *   2^-27 |x|); x fp32 rows of ldx elements; cols and ldx multiples of 4.
+ * bl_linear_split3: y[i][j] = sum_k x[i][k] w[j][k] + bias[j] from the split
+ *   planes x3 [3][m][k] and w3 [3][n][k] (bl_split3_bf16 of x and of the fp32
+ *   weight), keeping every cross product down to 2^-24 relative (error
+ *   within 2^-17 of the largest output); y fp32 rows of ldy; k % 8 == 0,
+ *   n % 4 == 0, ldy % 4 == 0, pointers 16-byte aligned; bias may be NULL.
+ * Replaces the fp32 linears the reference leaves to the BLAS: the diffusion
+ * AdaLN / ConditionedTransitionBlock projections (diffusion.py:55-68) and the
+ * AttentionPairBias projections (pair_bias.py:22-28, 36).
+ */
+BL_API int bl_split3_bf16(const float *x, int64_t rows, int64_t cols, int64_t ldx, void *out, void *stream);
+BL_API int bl_linear_split3(const void *x3, int64_t m, int64_t k, const void *w3, int64_t n, const float *bias,
+                            float *y, int64_t ldy, void *stream);
+
+/*
  * Pair transition (LayerNorm -> fc1|fc2 -> SwiGLU -> fc3, the bf16-autocast
  * contract) that allocates no device memory.  This entry point has no
  * counterpart in the reference; it exists for callers that may not allocate

@@ -1,0 +1,58 @@
+"""fp32-accurate tensor-core linear (bl_split3_bf16 + bl_linear_split3) on B200.
+
+The three-way bf16 split must reconstruct fp32 to 2^-27 relative, and the
+six-product GEMM must match a float64 reference to 2^-17 of the largest
+output (a few times an fp32 SGEMM's error: the tensor core's fp32
+accumulation of the dominant product is slightly coarser), far inside the
+1e-4 bound of the fp32 diffusion ops.
+"""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from boltz_lumi_b200 import kernels
+
+
+def test_split3_reconstructs():
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(333, 96, generator=g) * torch.logspace(-6, 6, 96)
+    x3 = kernels.split3(x.cuda()).double().cpu()
+    assert x3.shape == (3, 333, 96)
+    rel = ((x3.sum(0) - x.double()).abs() / x.double().abs().clamp_min(1e-30)).max().item()
+    assert rel <= 2.0 ** -26
+    assert torch.equal(x3[0].float(), x.bfloat16().float())  # the first plane is bf16(x)
+
+
+@pytest.mark.parametrize("m,n,k,with_bias", [(117, 3072, 768, True), (40, 768, 768, False), (512, 1536, 384, True),
+                                             (1, 4, 8, True), (300, 100, 72, False), (2000, 768, 768, True),
+                                             (129, 260, 1536, True)])
+def test_linear_matches_fp64(m, n, k, with_bias):
+    g = torch.Generator().manual_seed(m + n + k)
+    x = torch.randn(m, k, generator=g)
+    w = torch.randn(n, k, generator=g) * k ** -0.5
+    bias = torch.randn(n, generator=g) if with_bias else None
+    ref = x.double() @ w.double().T + (bias.double() if with_bias else 0)
+    with torch.inference_mode():
+        y = kernels.linear_f32(x.cuda(), kernels.split3(w.cuda()), None if bias is None else bias.cuda())
+        y_cublas = torch.nn.functional.linear(x.cuda(), w.cuda(), None if bias is None else bias.cuda())
+    err = (y.double().cpu() - ref).abs().max().item()
+    err_cublas = (y_cublas.double().cpu() - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    assert y.shape == (m, n) and y.dtype == torch.float32
+    assert err <= 2.0 ** -17 * scale, (err, err_cublas, scale)
+
+
+def test_linear_batched_input_and_shared_split():
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(2, 50, 384, generator=g).cuda()
+    w1, w2 = (torch.randn(n, 384, generator=g).cuda() * 0.05 for n in (768, 384))
+    with torch.inference_mode():
+        x3 = kernels.split3(x)
+        y1 = kernels.linear_f32(x, kernels.split3(w1), x3=x3)
+        y2 = kernels.linear_f32(x, kernels.split3(w2), x3=x3)
+    assert y1.shape == (2, 50, 768) and y2.shape == (2, 50, 384)
+    for y, w in ((y1, w1), (y2, w2)):
+        ref = (x.double() @ w.double().T)
+        assert (y.double() - ref).abs().max().item() <= 1e-5
