@@ -101,6 +101,7 @@ class CallObserver:
 
 
 _observer = None
+_functions = {}  # name -> bound ctypes function
 
 
 def set_observer(observer):
@@ -112,14 +113,16 @@ def set_observer(observer):
 
 def call(name, *args):
     """Call ``name`` and raise ``RuntimeError`` with the library's message on failure."""
-    lib = load()
+    fn = _functions.get(name)
+    if fn is None:
+        fn = _functions[name] = getattr(load(), name)
     observer = _observer
     token = observer.before(name, args) if observer is not None else None
-    status = getattr(lib, name)(*args)
+    status = fn(*args)
     if observer is not None:
         observer.after(name, args, token)
     if status != 0:
-        message = lib.bl_last_error().decode(errors="replace")
+        message = load().bl_last_error().decode(errors="replace")
         raise RuntimeError(f"{name} failed with status {status}: {message}")
     return status
 

@@ -32,8 +32,10 @@ def _pad8(n):
 
 def _cached(module, name, params, build):
     """Derived weights, rebuilt when any source parameter changes identity,
-    version, device or dtype (the reference's cache key, multiplication.py:29-40)."""
-    key = tuple((id(p), p._version, p.device, p.dtype) for p in params if p is not None)
+    in-place version or storage (a move to another device or dtype makes new
+    storage): the invalidation events of the reference's cache key
+    (multiplication.py:29-40), checked with cheap attribute reads."""
+    key = tuple((id(p), p._version, p.data_ptr()) for p in params if p is not None)
     cached = getattr(module, name, None)
     if cached is None or cached[0] != key:
         with torch.no_grad():
@@ -103,20 +105,26 @@ def _linear32(module, name, x, weights, biases=None, x3=None):
     """fp32 ``x @ [W_1; W_2; ...]^T + bias`` (upstream's fp32 nn.Linear calls,
     autocast off) on the tensor cores via the three-way bf16 split
     (bl_linear_split3); shapes it does not cover stay on cuBLAS fp32."""
-    n = sum(w.shape[0] for w in weights)
-    if not kernels.linear_f32_supported(x, n):
-        w = torch.cat(list(weights), 0) if len(weights) > 1 else weights[0]
-        bias = None
-        if biases is not None and any(b is not None for b in biases):
-            bias = torch.cat([b if b is not None else w.new_zeros(p.shape[0]) for p, b in zip(weights, biases)])
-        return F.linear(x, w, bias)
-    w3, bias = _split_weight(module, name, weights, biases)
-    return kernels.linear_f32(x, w3, bias, x3=x3)
+    k = x.shape[-1]
+    if x.dtype == torch.float32 and x.is_cuda and k % 8 == 0:
+        w3, bias = _split_weight(module, name, weights, biases)
+        n = w3.shape[1]
+        if n % 4 == 0:
+            if x3 is None:
+                x3 = kernels.split3_fast(x)
+            y = torch.empty(*x.shape[:-1], n, device=x.device, dtype=torch.float32)
+            kernels.linear_split3_fast(x3, w3, bias, y)
+            return y
+    w = torch.cat(list(weights), 0) if len(weights) > 1 else weights[0]
+    bias = None
+    if biases is not None and any(b is not None for b in biases):
+        bias = torch.cat([b if b is not None else w.new_zeros(p.shape[0]) for p, b in zip(weights, biases)])
+    return F.linear(x, w, bias)
 
 
-def _split_input(x, n_min=4):
+def _split_input(x):
     """split3(x) when x can feed bl_linear_split3, else None."""
-    return kernels.split3(x) if kernels.linear_f32_supported(x, n_min) else None
+    return kernels.split3_fast(x) if x.dtype == torch.float32 and x.is_cuda and x.shape[-1] % 8 == 0 else None
 
 
 # ---------------------------------------------------------------------------
