@@ -41,7 +41,10 @@ constexpr int kStagingBytes = 4096;  // [32 rows][32 fp32], 128-byte swizzled
 struct LinArgs {
   int m, n, k;
   int tiles_m, tiles_n;
+  int splits, kb_per_split;  // cluster kernel: K blocks [rank * kb_per_split, ...) per CTA
   const float *bias;
+  float *y;
+  int64_t ldy;
   unsigned int *status;
 };
 
@@ -228,6 +231,215 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Problems with few output tiles (skinny m): one cluster of S CTAs per tile,
+// CTA rank r accumulating K blocks [r * kbs, (r + 1) * kbs).  Partials meet in
+// shared memory: after a cluster barrier CTA r sums rows [r * 128 / S, ...)
+// over the S partials in rank order through distributed shared memory
+// (deterministic), adds the bias and writes Y.  Every thread reaches both
+// cluster barriers on every path (a failed bounded wait only skips work).
+// ---------------------------------------------------------------------------
+template <int BN> struct ClusterShape {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = 3 * (kABytes + kBBytes);
+  static constexpr int kStages = BN <= 32 ? 3 : 2;
+  static constexpr int kRingBytes = kStages * kStageBytes;
+  static constexpr int kPartLd = BN + 4;  // floats per partial row
+  static constexpr int kPartBytes = kBM * kPartLd * 4;
+  static constexpr int kBarrierOffset = kRingBytes + kPartBytes;
+  static constexpr int kSmemBytes = kBarrierOffset + 256 + 1024;
+  static constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float4 ld_peer_f4(uint32_t local_addr, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(remote)
+               : "memory");
+  return v;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    linear_split3_cluster_kernel(const __grid_constant__ CUtensorMap tma_x, const __grid_constant__ CUtensorMap tma_w,
+                                 const LinArgs args) {
+  using S = ClusterShape<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float *part = reinterpret_cast<float *>(smem + S::kRingBytes);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + S::kBarrierOffset);
+  uint64_t *empty = full + S::kStages;
+  uint64_t *acc_full = empty + S::kStages;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int splits = args.splits;
+  const int rank = int(cluster_rank());
+  const int tile = int(blockIdx.x) / splits;
+  const int m0 = (tile / args.tiles_n) * kBM, n0 = (tile % args.tiles_n) * BN;
+  const int k_blocks = (args.k + kBK - 1) / kBK;
+  const int kb0 = rank * args.kb_per_split, kb1 = min(k_blocks, kb0 + args.kb_per_split);
+
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < S::kStages; ++st) {
+      tc::mbar_init(&full[st], 1);
+      tc::mbar_init(&empty[st], 1);
+    }
+    tc::mbar_init(acc_full, 1);
+    tc::fence_mbar_init();
+    tc::prefetch_tmap(&tma_x);
+    tc::prefetch_tmap(&tma_w);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, S::kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!tc::mbar_wait(&empty[stage], phase ^ 1u, args.status, 0x611)) break;
+        uint8_t *sa = smem + stage * S::kStageBytes;
+        uint8_t *sb = sa + 3 * S::kABytes;
+        tc::mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+#pragma unroll
+        for (int p = 0; p < 3; ++p) {
+          tc::tma_load_3d(sa + p * S::kABytes, &tma_x, &full[stage], kb * kBK, m0, p);
+          tc::tma_load_3d(sb + p * S::kBBytes, &tma_w, &full[stage], kb * kBK, n0, p);
+        }
+        if (++stage == S::kStages) stage = 0, phase ^= 1u;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_bf16(kBM, BN, false, false);
+      const uint32_t d_hi = tmem_base, d_lo = tmem_base + BN;
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1 && ok; ++kb) {
+        if (!(ok = tc::mbar_wait(&full[stage], phase, args.status, 0x612))) break;
+        tc::tc_fence_after();
+        const uint32_t sa = tc::smem_u32(smem + stage * S::kStageBytes);
+        const uint32_t sb = sa + 3 * S::kABytes;
+#pragma unroll
+        for (int p = 0; p < 6; ++p) {
+          const uint32_t pa = sa + pair_a(p) * S::kABytes, pb = sb + pair_b(p) * S::kBBytes;
+          const uint32_t d = p == 5 ? d_hi : d_lo;
+          const bool first = kb == kb0 && (p == 0 || p == 5);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            tc::umma_f16_ss(d, tc::desc_sw128(pa + kk * 32, 16), tc::desc_sw128(pb + kk * 32, 16), idesc,
+                            !(first && kk == 0));
+        }
+        tc::umma_commit(&empty[stage]);
+        if (++stage == S::kStages) stage = 0, phase ^= 1u;
+      }
+      if (ok && kb0 < kb1) tc::umma_commit(acc_full);
+    }
+  } else {
+    // This CTA's partial (hi + lo) into shared memory, row = TMEM lane; a
+    // rank with no K blocks (k_blocks not a multiple of the split) adds zeros.
+    const int quarter = warp & 3;
+    if (kb0 >= kb1) {
+      float *dst = part + (quarter * 32 + lane) * S::kPartLd;
+      for (int j = 0; j < BN; j += 4) *reinterpret_cast<float4 *>(dst + j) = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else if (tc::mbar_wait(acc_full, 0, args.status, 0x613)) {
+      tc::tc_fence_after();
+      const uint32_t tbase = tc::tmem_addr(tmem_base, quarter * 32, 0);
+      float *dst = part + (quarter * 32 + lane) * S::kPartLd;
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t r[32], rl[32];
+        tc::tmem_ld_32x32b_x32(tbase + cc * 32, r);
+        tc::tmem_ld_32x32b_x32(tbase + BN + cc * 32, rl);
+        tc::tmem_ld_wait_regs(r, rl);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          *reinterpret_cast<float4 *>(dst + cc * 32 + j) =
+              make_float4(__uint_as_float(r[j]) + __uint_as_float(rl[j]),
+                          __uint_as_float(r[j + 1]) + __uint_as_float(rl[j + 1]),
+                          __uint_as_float(r[j + 2]) + __uint_as_float(rl[j + 2]),
+                          __uint_as_float(r[j + 3]) + __uint_as_float(rl[j + 3]));
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();  // every partial of the cluster is in shared memory
+  {
+    const int rows = kBM / splits, r0 = rank * rows;
+    constexpr int kCols4 = BN / 4;
+    const uint32_t part_addr = tc::smem_u32(part);
+    for (int it = threadIdx.x; it < rows * kCols4; it += kThreads) {
+      const int r = r0 + it / kCols4, c = 4 * (it % kCols4);
+      const uint32_t off = part_addr + uint32_t((r * S::kPartLd + c) * 4);
+      float4 v = ld_peer_f4(off, 0);
+      for (int p = 1; p < splits; ++p) {
+        const float4 w = ld_peer_f4(off, uint32_t(p));
+        v.x += w.x, v.y += w.y, v.z += w.z, v.w += w.w;
+      }
+      const int col = n0 + c, row = m0 + r;
+      if (row < args.m && col < args.n) {
+        if (args.bias) v.x += args.bias[col], v.y += args.bias[col + 1], v.z += args.bias[col + 2], v.w += args.bias[col + 3];
+        *reinterpret_cast<float4 *>(args.y + int64_t(row) * args.ldy + col) = v;
+      }
+    }
+  }
+  __syncwarp();
+  cluster_sync_all();  // peers finished reading this CTA's partial
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem_base, S::kTmemCols);
+  }
+}
+
+template <int BN>
+int launch_linear_cluster(const CUtensorMap &tx, const CUtensorMap &tw, LinArgs args, int splits,
+                          cudaStream_t stream) {
+  using S = ClusterShape<BN>;
+  auto kernel = linear_split3_cluster_kernel<BN>;
+  BL_CUDA(ensure_smem_limit(reinterpret_cast<const void *>(kernel), S::kSmemBytes));
+  const int k_blocks = (args.k + kBK - 1) / kBK;
+  args.tiles_n = (args.n + BN - 1) / BN;
+  args.kb_per_split = (k_blocks + splits - 1) / splits;
+  args.splits = splits;
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(unsigned(args.tiles_m * args.tiles_n * splits));
+  config.blockDim = dim3(kThreads);
+  config.dynamicSmemBytes = S::kSmemBytes;
+  config.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(splits);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  config.attrs = attr;
+  config.numAttrs = 1;
+  BL_CUDA(cudaLaunchKernelEx(&config, kernel, tx, tw, args));
+  BL_LAUNCH_CHECK();
+  return BL_OK;
+}
+
 template <int BN>
 int launch_linear(const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorMap &ty, LinArgs args,
                   cudaStream_t stream) {
@@ -300,7 +512,24 @@ extern "C" int bl_linear_split3(const void *x3, int64_t m, int64_t k, const void
   BL_REQUIRE(aligned_to(x3, 16) && aligned_to(w3, 16) && aligned_to(y, 16),
              "bl_linear_split3: pointers must be 16-byte aligned");
   BL_REQUIRE(m < (1ll << 31) && n < (1ll << 31) && k < (1ll << 31), "bl_linear_split3: shape too large");
-  const int bn = m > 2 * kBM ? 128 : (m > kBM ? 64 : 32);
+  // Every CTA streams its tile's A and B rows through the whole K range, so
+  // the critical path is (waves of work units) x (bytes one unit loads).
+  // Pick the N tile and, for problems with few tiles, a cluster split over K
+  // (one wave, BN <= 64) that minimise it.
+  int bn = 128, splits = 1;
+  {
+    const int64_t k_blocks = (k + kBK - 1) / kBK, tiles_m = (m + kBM - 1) / kBM, sms = num_sms();
+    int64_t best = -1;
+    for (int b : {32, 64, 128}) {
+      const int64_t tiles = tiles_m * ((n + b - 1) / b);
+      for (int sp = 1; sp <= 8; sp *= 2) {
+        if (sp > 1 && (b > 64 || tiles * sp > sms || sp > k_blocks)) break;
+        const int64_t waves = (tiles * sp + sms - 1) / sms;
+        const int64_t cost = waves * ((k_blocks + sp - 1) / sp) * (3 * (kBM + b) * kBK * 2);
+        if (best < 0 || cost < best) best = cost, bn = b, splits = sp;
+      }
+    }
+  }
   CUtensorMap tx, tw, ty;
   {
     uint64_t dims[3] = {uint64_t(k), uint64_t(m), 3};
@@ -330,9 +559,15 @@ extern "C" int bl_linear_split3(const void *x3, int64_t m, int64_t k, const void
   args.m = int(m), args.n = int(n), args.k = int(k);
   args.tiles_m = int((m + kBM - 1) / kBM);
   args.bias = bias;
+  args.y = y, args.ldy = ldy;
+  args.splits = 1, args.kb_per_split = 0;
   args.status = device_status_ptr();
   BL_REQUIRE(args.status, "bl_linear_split3: device status word unavailable");
   cudaStream_t s = as_stream(stream);
+  if (splits > 1) {
+    if (bn == 64) return launch_linear_cluster<64>(tx, tw, args, splits, s);
+    return launch_linear_cluster<32>(tx, tw, args, splits, s);
+  }
   if (bn == 128) return launch_linear<128>(tx, tw, ty, args, s);
   if (bn == 64) return launch_linear<64>(tx, tw, ty, args, s);
   return launch_linear<32>(tx, tw, ty, args, s);

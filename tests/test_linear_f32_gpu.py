@@ -27,7 +27,8 @@ def test_split3_reconstructs():
 
 @pytest.mark.parametrize("m,n,k,with_bias", [(117, 3072, 768, True), (40, 768, 768, False), (512, 1536, 384, True),
                                              (1, 4, 8, True), (300, 100, 72, False), (2000, 768, 768, True),
-                                             (129, 260, 1536, True)])
+                                             (129, 260, 1536, True), (117, 768, 768, True), (100, 100, 1096, True),
+                                             (8, 768, 136, False), (300, 768, 768, True), (256, 3072, 768, False)])
 def test_linear_matches_fp64(m, n, k, with_bias):
     g = torch.Generator().manual_seed(m + n + k)
     x = torch.randn(m, k, generator=g)
@@ -56,3 +57,19 @@ def test_linear_batched_input_and_shared_split():
     for y, w in ((y1, w1), (y2, w2)):
         ref = (x.double() @ w.double().T)
         assert (y.double() - ref).abs().max().item() <= 1e-5
+
+
+@pytest.mark.parametrize("m,n,k", [(117, 768, 768), (100, 100, 1096), (64, 1536, 768), (300, 768, 768)])
+def test_skinny_cluster_split_is_deterministic(m, n, k):
+    """m <= 128 with few N tiles splits K over a thread-block cluster and
+    reduces the partials in rank order through distributed shared memory:
+    repeated calls must agree bitwise."""
+    g = torch.Generator().manual_seed(m + k)
+    x = torch.randn(m, k, generator=g).cuda()
+    w3 = kernels.split3((torch.randn(n, k, generator=g) * k ** -0.5).cuda())
+    bias = torch.randn(n, generator=g).cuda()
+    with torch.inference_mode():
+        ys = [kernels.linear_f32(x, w3, bias) for _ in range(3)]
+    assert all(torch.equal(ys[0], y) for y in ys[1:])
+    ref = x.double() @ w3.double().sum(0).T + bias.double()
+    assert (ys[0].double() - ref).abs().max().item() <= 2.0 ** -17 * ref.abs().max().item()
