@@ -5,7 +5,8 @@
 Ops: tri_mul_out, tri_mul_in, att_start, att_end, transition, block, and the
 diffusion token transformer's attention: token_attention (the whole
 AttentionPairBias forward, c_s 768, 16 heads, a layer of a prepared 24-layer
-token bias, --mult samples) and token_core (bl_token_attention alone).  Inputs
+token bias, --mult samples) and token_core (bl_token_attention alone); and
+linear (the fp32 tensor-core linear bl_linear_split3 at --m x --n x --k).  Inputs
 and weights are the benchmark's synthetic ones (seeded); z is updated in
 place like in the Pairformer block.  Prints the mean device time per call.
 """
@@ -48,10 +49,13 @@ def main():
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--op", default="block",
                         choices=["tri_mul_out", "tri_mul_in", "att_start", "att_end", "transition", "block",
-                                 "token_attention", "token_core"])
+                                 "token_attention", "token_core", "linear"])
     parser.add_argument("--n", type=int, default=512)
     parser.add_argument("--iters", type=int, default=3)
     parser.add_argument("--mult", type=int, default=1, help="diffusion samples (token ops)")
+    parser.add_argument("--m", type=int, default=117, help="rows (linear)")
+    parser.add_argument("--k", type=int, default=768, help="input features (linear)")
+    parser.add_argument("--n-out", type=int, default=768, help="output features (linear)")
     args = parser.parse_args()
     block = seeded_block().cuda()
     g = torch.Generator().manual_seed(7)
@@ -70,6 +74,11 @@ def main():
     }
     if args.op.startswith("token"):
         ops.update(_token_ops(n, args.mult))
+    if args.op == "linear":
+        x = torch.randn(args.m, args.k, generator=g).cuda()
+        w3 = kernels.split3((torch.randn(args.n_out, args.k, generator=g) * args.k ** -0.5).cuda())
+        x3 = kernels.split3(x)
+        ops["linear"] = lambda: kernels.linear_f32(x, w3, x3=x3)
     fn = ops[args.op]
     with torch.inference_mode():
         fn()
@@ -80,7 +89,8 @@ def main():
             fn()
         end.record()
         torch.cuda.synchronize()
-    print(f"{args.op} n={n}: {start.elapsed_time(end) / args.iters:.4f} ms per call")
+    shape = f"m={args.m} n={args.n_out} k={args.k}" if args.op == "linear" else f"n={n}"
+    print(f"{args.op} {shape}: {start.elapsed_time(end) / args.iters:.4f} ms per call")
 
 
 if __name__ == "__main__":
