@@ -107,4 +107,25 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Packed fp32 pairs (sm_100 fma.rn.f32x2): the pair lives in one 64-bit register.
+__device__ __forceinline__ void lds_v2b64(uint32_t addr, uint64_t &a, uint64_t &b) {
+  asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(addr));
+}
+__device__ __forceinline__ uint64_t lds_b64(uint32_t addr) {
+  uint64_t v;
+  asm volatile("ld.shared.b64 %0, [%1];" : "=l"(v) : "r"(addr));
+  return v;
+}
+// acc.{lo,hi} += a.{lo,hi} * b.{lo,hi}
+__device__ __forceinline__ void ffma2(uint64_t &acc, uint64_t a, uint64_t b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+__device__ __forceinline__ uint64_t dup2(float x) {
+  uint64_t v;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(v) : "f"(x));
+  return v;
+}
+__device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float(uint32_t(v)); }
+__device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float(uint32_t(v >> 32)); }
+
 }  // namespace bl

@@ -11,8 +11,8 @@
 // One thread per pair row.  A CTA stages 128 rows (64 KB of fp32) in shared
 // memory with coalesced 16-byte loads, then each thread computes its row's
 // statistics and the heads dot products from shared memory with no
-// cross-lane reductions: 2048 FMA per row against weights read as
-// same-address (broadcast) shared loads.
+// cross-lane reductions: 2048 FMA per row (1024 packed fp32x2 FMA) against
+// weights read as same-address (broadcast) shared loads.
 #include "common.cuh"
 
 namespace bl {
@@ -30,6 +30,7 @@ __global__ void __launch_bounds__(kRowsPerCta) pair_bias_kernel(const float *z, 
   float *tile = reinterpret_cast<float *>(smem4);           // [128][kRowStride]
   float *ws = tile + kRowsPerCta * kRowStride;              // [kC][kHeads]: w transposed, zero past `heads`
   float *lnw = ws + kC * kHeads, *lnb = lnw + kC;
+  const uint32_t ws_addr = static_cast<uint32_t>(__cvta_generic_to_shared(ws));
   const int t = threadIdx.x;
   for (int i = t; i < kC * kHeads; i += kRowsPerCta) {
     const int c = i / kHeads, h = i % kHeads;
@@ -73,9 +74,11 @@ __global__ void __launch_bounds__(kRowsPerCta) pair_bias_kernel(const float *z, 
       q4[0] += d0 * d0, q4[1] += d1 * d1, q4[2] += d2 * d2, q4[3] += d3 * d3;
     }
     const float rstd = rsqrtf(((q4[0] + q4[1]) + (q4[2] + q4[3])) * (1.f / kC) + eps);
-    float acc[kHeads];
+    // Heads in packed pairs (fma.rn.f32x2): each pair accumulates in the same
+    // order as two scalar FMA chains.
+    uint64_t acc2[kHeads / 2];
 #pragma unroll
-    for (int h = 0; h < kHeads; ++h) acc[h] = 0.f;
+    for (int h = 0; h < kHeads / 2; ++h) acc2[h] = 0;
 #pragma unroll 2
     for (int c = 0; c < kC; c += 4) {
       const float4 v = *reinterpret_cast<const float4 *>(row + c);  // 16-byte reads: no bank conflicts
@@ -84,19 +87,21 @@ __global__ void __launch_bounds__(kRowsPerCta) pair_bias_kernel(const float *z, 
                           (v.z - mean) * rstd * gw.z + gb.z, (v.w - mean) * rstd * gw.w + gb.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float4 *wc = reinterpret_cast<const float4 *>(ws + (c + e) * kHeads);  // same address in every lane
+        const uint64_t yy = dup2(y[e]);
+        const uint32_t wc = ws_addr + uint32_t((c + e) * kHeads * 4);  // same address in every lane
 #pragma unroll
         for (int q = 0; q < kHeads / 4; ++q) {
-          const float4 wv = wc[q];
-          acc[4 * q] += y[e] * wv.x, acc[4 * q + 1] += y[e] * wv.y;
-          acc[4 * q + 2] += y[e] * wv.z, acc[4 * q + 3] += y[e] * wv.w;
+          uint64_t w01, w23;
+          lds_v2b64(wc + 16 * q, w01, w23);
+          ffma2(acc2[2 * q], yy, w01);
+          ffma2(acc2[2 * q + 1], yy, w23);
         }
       }
     }
     if (t < valid) {
 #pragma unroll
       for (int h = 0; h < kHeads; ++h)
-        if (h < heads) out[int64_t(h) * rows + r0 + t] = acc[h];
+        if (h < heads) out[int64_t(h) * rows + r0 + t] = (h & 1) ? hi_f(acc2[h / 2]) : lo_f(acc2[h / 2]);
     }
   }
 }

@@ -53,26 +53,6 @@ __device__ __forceinline__ void cp_async4(uint32_t dst, const void *src, bool va
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
-__device__ __forceinline__ void lds_v2b64(uint32_t addr, uint64_t &a, uint64_t &b) {
-  asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(addr));
-}
-__device__ __forceinline__ uint64_t lds_b64(uint32_t addr) {
-  uint64_t v;
-  asm volatile("ld.shared.b64 %0, [%1];" : "=l"(v) : "r"(addr));
-  return v;
-}
-// acc.{lo,hi} += a.{lo,hi} * b.{lo,hi}
-__device__ __forceinline__ void ffma2(uint64_t &acc, uint64_t a, uint64_t b) {
-  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
-}
-__device__ __forceinline__ uint64_t dup2(float x) {
-  uint64_t v;
-  asm("mov.b64 %0, {%1, %1};" : "=l"(v) : "f"(x));
-  return v;
-}
-__device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float(uint32_t(v)); }
-__device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float(uint32_t(v >> 32)); }
-
 template <int D>
 __global__ void __launch_bounds__(kThreads, 2) token_attention_kernel(const TokArgs a) {
   constexpr int kLd = D + 4;   // padded row (floats): conflict-free 16-byte row reads
