@@ -439,6 +439,22 @@ def run_b200(args):
         "peak_source": f"{peak_source} ({'bf16_tflops_sustained' if top['kind'] == 'flops' else 'hbm_gbs'})",
     })
 
+    roofline_sfu = None
+    if top_label.startswith("bl_triangle_attention"):
+        # The attention core's other bound (report both): one ex2
+        # per score on the MUFU pipe, 16 per clock per SM.  The peak is derived
+        # from that rate, the SM count and the sampled SM clock (there is no
+        # measured SFU figure).
+        exps = top["amount"] / (4 * 32)  # 4 N^3 H d FLOP with d = 32 -> N^3 H scores
+        clock_mhz = (clock_info or {}).get("sm_mhz") or 1965.0
+        sms = torch.cuda.get_device_properties(device).multi_processor_count
+        sfu_peak = 16 * sms * clock_mhz * 1e6
+        sfu_achieved = exps / (avg_ms * 1e-3)
+        roofline_sfu = {"bound": "sfu", "unit": "ex2/s", "achieved": float(f"{sfu_achieved:.4g}"),
+                        "peak": float(f"{sfu_peak:.4g}"), "frac": round(sfu_achieved / sfu_peak, 4),
+                        "kernel": top_label, "exps_per_launch": exps,
+                        "peak_source": f"derived: 16 ex2/clk/SM x {sms} SMs x {clock_mhz:.0f} MHz (sampled)"}
+
     line = {
         "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": round(ms_per_step, 4), "higher_is_better": False,
@@ -450,6 +466,7 @@ def run_b200(args):
         "gpu_launches": launches_timed,
         "launches_per_step": launches_per_step,
         "roofline": roofline,
+        **({"roofline_sfu": roofline_sfu} if roofline_sfu else {}),
         "clocks": clock_info,
         "kernels_ms_per_step": {k: round(v["ms"], 4) for k, v in sorted(per_label.items(), key=lambda kv: -kv[1]["ms"])},
     }
