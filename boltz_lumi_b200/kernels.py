@@ -325,10 +325,6 @@ def linear_split3_fast(x3, w3, bias, y):
     return y
 
 
-def linear_f32_supported(x, n):
-    return x.is_cuda and x.dtype == torch.float32 and x.shape[-1] % 8 == 0 and n % 4 == 0
-
-
 def linear_f32(x, w3, bias=None, x3=None):
     """fp32 ``x @ W^T + bias`` on the tensor cores (error within 2^-17 of the largest output)
     (bl_linear_split3).  ``w3`` = ``split3(W)`` (bf16 [3, N, K]); ``x3`` may
