@@ -20,6 +20,12 @@ if torch.cuda.is_available():
 
 BF16_ATOL = 2e-2
 FP32_ATOL = 1e-4
+# Above |y| = 2.56 one bf16 ulp of the output itself exceeds 2e-2, and an
+# fp32 accumulation-order difference can flip the output's final rounding:
+# large-N cases allow max(2e-2, one bf16 ulp) per element and bound the
+# relative L2 error.
+BF16_ULP = 2.0 ** -7
+BF16_REL_L2 = 1e-2
 
 
 def build(product_cls, oracle_cls, *args, seed=732991, std=0.08):
@@ -56,6 +62,50 @@ def test_triangle_attention(ending, n, kind):
         actual = mod(x.cuda(), mask.cuda(), chunk_size=32)
     assert actual.dtype == torch.bfloat16
     assert_close(actual.float(), expected, atol=BF16_ATOL)
+
+
+@pytest.mark.parametrize("ending", [False, True])
+@pytest.mark.parametrize("n,kind,rows", [(312, "ones", None), (312, "partial", None), (576, "ones", None),
+                                         (576, "partial", None), (1134, "partial", None), (2511, "partial", 48)])
+def test_triangle_attention_reference_sizes(ending, n, kind, rows):
+    """The reference's own attention case list (test_operator_additions.py:60-67: N = 312, 576,
+    1134, 2511, x * 0.3, the last three tokens masked).  At these sizes the oracle runs on the
+    GPU as the checker (same torch restatement, fp32); at N = 2511 it computes the first
+    `rows` outer rows (rows attend independently) and the kernel output is compared there.
+    Bound: max(2e-2, one bf16 ulp of the expected value) per element, relative L2 <= 1e-2."""
+    cls = (layers.TriangleAttentionEndingNode, oracle.TriangleAttentionEndingNode) if ending else \
+        (layers.TriangleAttention, oracle.TriangleAttention)
+    mod, ref = build(*cls, 128, 32, 4)
+    ref = ref.cuda()
+    g = torch.Generator().manual_seed(n)
+    x = (torch.randn(1, n, n, 128, generator=g) * 0.3).cuda()
+    mask = pair_mask(n, kind).cuda()
+    with torch.inference_mode():
+        expected = ref(x, mask, chunk_size=32, rows=rows)
+        actual = mod(x, mask, chunk_size=32)
+    if rows is not None:
+        actual = actual[:, :, :rows] if ending else actual[:, :rows]
+    assert actual.shape == expected.shape
+    assert_close(actual.float(), expected, atol=BF16_ATOL, rtol=BF16_ULP, rel_l2=BF16_REL_L2)
+
+
+@pytest.mark.parametrize("incoming", [False, True])
+@pytest.mark.parametrize("n", [312, 576])
+@pytest.mark.parametrize("kind", ["zero", "ones", "partial", "fractional"])
+def test_triangle_multiplication_reference_sizes(incoming, n, kind):
+    """The reference's multiplication cases at N = 312 and 576 (test_operator_additions.py:68,
+    x * 0.3, the last two tokens masked), oracle on the GPU as the checker.  Bound: max(2e-2,
+    one bf16 ulp of the expected value) per element, relative L2 <= 1e-2."""
+    cls = (layers.TriangleMultiplicationIncoming, oracle.TriangleMultiplicationIncoming) if incoming else \
+        (layers.TriangleMultiplicationOutgoing, oracle.TriangleMultiplicationOutgoing)
+    mod, ref = build(*cls, 128)
+    ref = ref.cuda()
+    x = (torch.randn(1, n, n, 128, generator=torch.Generator().manual_seed(n + 1)) * 0.3).cuda()
+    mask = pair_mask(n, kind, masked_tokens=2).cuda()
+    with torch.inference_mode():
+        expected = ref(x, mask)
+        actual = mod(x, mask)
+    assert_close(actual.float(), expected, atol=BF16_ATOL, rtol=BF16_ULP, rel_l2=BF16_REL_L2)
 
 
 @pytest.mark.parametrize("incoming", [False, True])
