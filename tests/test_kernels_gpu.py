@@ -194,8 +194,10 @@ def test_adaln_modulate(rows, cols):
 # Ordered bias softmax (tests/test_triangle_softmax.py case list)
 # ---------------------------------------------------------------------------
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-@pytest.mark.parametrize("n", [117, 129, 257, 312, 513])
+@pytest.mark.parametrize("n", [117, 129, 257, 312, 513, 576, 1023, 1024, 1134, 1734, 2511])
 def test_ordered_softmax(dtype, n):
+    if n > 1024 and dtype != torch.bfloat16:
+        pytest.skip("the reference runs fp32 scores up to 1024 only (test_triangle_softmax.py:29-30)")
     g = gen(46)
     scores = (torch.randn(1, 3, 4, n, n, generator=g) * 5).to(dtype)
     bias = (torch.randn(1, 1, 4, n, n, generator=g) * 2).to(dtype)

@@ -135,6 +135,20 @@ def test_pair_transition(n):
             assert_close(actual.float(), expected, atol=BF16_ATOL)
 
 
+@pytest.mark.parametrize("n", [17, 117, 312, 576])
+def test_pair_transition_reference_cases(n):
+    """The reference's transition cases (test_pair_transition.py:52-66): x [2, n, 128],
+    weights N(0, 0.05), dense and strided (x[:, ::2]) inputs."""
+    mod, ref = build(layers.Transition, oracle.Transition, 128, 512, std=0.05, seed=81)
+    x = torch.randn(2, n, 128, generator=torch.Generator().manual_seed(81 + n))
+    with torch.inference_mode():
+        for value in (x, x[:, ::2]):
+            expected = ref(value)
+            actual = mod(value.cuda())
+            assert expected.abs().max() > 0
+            assert_close(actual.float(), expected, atol=BF16_ATOL)
+
+
 @pytest.mark.parametrize("dim,hidden", [(64, 256), (256, 1024), (128, 256)])
 def test_pair_transition_other_widths(dim, hidden):
     """Widths other than the trunk's 128 -> 512 -> 128 (the template module's
