@@ -2,7 +2,8 @@
 
     python -m boltz_lumi_b200.profile_ops --op att_start --n 512 --iters 3
 
-Ops: tri_mul_out, tri_mul_in, att_start, att_end, transition, block, and the
+Ops: tri_mul_out, tri_mul_in, att_start, att_end, transition, block, c2
+(att_start + att_end), c3 (tri_mul_out + tri_mul_in + transition), and the
 diffusion token transformer's attention: token_attention (the whole
 AttentionPairBias forward, c_s 768, 16 heads, a layer of a prepared 24-layer
 token bias, --mult samples) and token_core (bl_token_attention alone); and
@@ -49,10 +50,12 @@ def main():
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--op", default="block",
                         choices=["tri_mul_out", "tri_mul_in", "att_start", "att_end", "transition", "block",
-                                 "token_attention", "token_core", "linear"])
+                                 "token_attention", "token_core", "linear", "c2", "c3"])
     parser.add_argument("--n", type=int, default=512)
     parser.add_argument("--iters", type=int, default=3)
     parser.add_argument("--mult", type=int, default=1, help="diffusion samples (token ops)")
+    parser.add_argument("--masked-tail", type=float, default=0.0,
+                        help="fraction of tokens masked at the end (rows and columns of the pair mask)")
     parser.add_argument("--m", type=int, default=117, help="rows (linear)")
     parser.add_argument("--k", type=int, default=768, help="input features (linear)")
     parser.add_argument("--n-out", type=int, default=768, help="output features (linear)")
@@ -64,6 +67,11 @@ def main():
     s = torch.randn(1, n, 384, generator=g).cuda()
     mask = torch.ones(1, n, device="cuda")
     pmask = torch.ones(1, n, n, device="cuda")
+    tail = int(round(args.masked_tail * n))
+    if tail:
+        mask[:, n - tail:] = 0
+        pmask[:, n - tail:, :] = 0
+        pmask[:, :, n - tail:] = 0
     ops = {
         "tri_mul_out": lambda: forwards.triangle_multiplication_forward(block.tri_mul_out, z, pmask, residual=z),
         "tri_mul_in": lambda: forwards.triangle_multiplication_forward(block.tri_mul_in, z, pmask, residual=z),
@@ -72,6 +80,10 @@ def main():
         "transition": lambda: forwards.transition_forward(block.transition_z, z, residual=z),
         "block": lambda: block(s, z, mask, pmask),
     }
+    # SURVEY measurement configs: C2 = both triangle attentions, C3 = both
+    # triangle multiplications and the pair transition.
+    ops["c2"] = lambda: (ops["att_start"](), ops["att_end"]())
+    ops["c3"] = lambda: (ops["tri_mul_out"](), ops["tri_mul_in"](), ops["transition"]())
     if args.op.startswith("token"):
         ops.update(_token_ops(n, args.mult))
     if args.op == "linear":
