@@ -128,4 +128,32 @@ __device__ __forceinline__ uint64_t dup2(float x) {
 __device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float(uint32_t(v)); }
 __device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float(uint32_t(v >> 32)); }
 
+// Four fp32 values as three bf16 planes (x = x1 + x2 + x3, x1 = bf16(x),
+// x2 = bf16(x - x1), x3 = bf16(x - x1 - x2); both subtractions exact): the
+// operand form of bl_linear_split3.  Element e (a multiple of 4) of each
+// plane; planes are `plane` elements apart.
+__device__ __forceinline__ void store_split3_4(__nv_bfloat16 *planes, int64_t plane, int64_t e, float v0, float v1,
+                                               float v2, float v3) {
+  const float v[4] = {v0, v1, v2, v3};
+  float p1[4], p2[4], p3[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    p1[i] = bf16r(v[i]);
+    const float r1 = v[i] - p1[i];
+    p2[i] = bf16r(r1);
+    p3[i] = r1 - p2[i];
+  }
+  *reinterpret_cast<uint2 *>(planes + e) = make_uint2(pack_bf16x2(p1[0], p1[1]), pack_bf16x2(p1[2], p1[3]));
+  *reinterpret_cast<uint2 *>(planes + plane + e) = make_uint2(pack_bf16x2(p2[0], p2[1]), pack_bf16x2(p2[2], p2[3]));
+  *reinterpret_cast<uint2 *>(planes + 2 * plane + e) =
+      make_uint2(pack_bf16x2(p3[0], p3[1]), pack_bf16x2(p3[2], p3[3]));
+}
+
+__device__ __forceinline__ void store_split3_1(__nv_bfloat16 *planes, int64_t plane, int64_t e, float v) {
+  const float p1 = bf16r(v), r1 = v - p1, p2 = bf16r(r1);
+  planes[e] = __float2bfloat16_rn(p1);
+  planes[plane + e] = __float2bfloat16_rn(p2);
+  planes[2 * plane + e] = __float2bfloat16_rn(r1 - p2);
+}
+
 }  // namespace bl

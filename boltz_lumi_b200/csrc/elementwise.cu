@@ -224,6 +224,31 @@ template <int KIND> __device__ __forceinline__ float epilogue_value(float a, flo
   }
 }
 
+// The epilogue result as three bf16 planes (the fp32 linears' operand form);
+// cols % 4 == 0, 16-byte aligned operands.
+template <int KIND>
+__global__ void diffusion_epilogue_split3_kernel(const float *a, const float *b, const float *c,
+                                                 __nv_bfloat16 *out, int64_t rows, int64_t cols) {
+  const int64_t width = cols / 4, total = rows * width, plane = rows * cols;
+  for (int64_t t = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; t < total;
+       t += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t row = t / width, col = t % width;
+    float4 av, bv, cv = make_float4(0.f, 0.f, 0.f, 0.f);
+    if constexpr (KIND == BL_EPI_GATED_SWIGLU) {
+      const float4 *a4 = reinterpret_cast<const float4 *>(a) + row * 2 * width;
+      av = a4[col];
+      bv = a4[width + col];
+      cv = reinterpret_cast<const float4 *>(b)[t];
+    } else {
+      av = reinterpret_cast<const float4 *>(a)[t];
+      bv = reinterpret_cast<const float4 *>(b)[t];
+      if constexpr (KIND == BL_EPI_MODULATION) cv = reinterpret_cast<const float4 *>(c)[t];
+    }
+    store_split3_4(out, plane, 4 * t, epilogue_value<KIND>(av.x, bv.x, cv.x), epilogue_value<KIND>(av.y, bv.y, cv.y),
+                   epilogue_value<KIND>(av.z, bv.z, cv.z), epilogue_value<KIND>(av.w, bv.w, cv.w));
+  }
+}
+
 template <int KIND, bool VEC>
 __global__ void diffusion_epilogue_kernel(const float *a, const float *b, const float *c, float *out,
                                           int64_t rows, int64_t cols) {
@@ -267,8 +292,8 @@ __global__ void diffusion_epilogue_kernel(const float *a, const float *b, const 
 // Fused AdaLN modulation: out = sigmoid(scale) * LN(a) + shift (no affine LN).
 // One warp per row; the row stays in registers when cols <= 32 * 4 * MAXV.
 // ---------------------------------------------------------------------------
-template <int MAXV>
-__global__ void adaln_modulate_kernel(const float *a, const float *scale, const float *shift, float *out,
+template <int MAXV, bool SPLIT>
+__global__ void adaln_modulate_kernel(const float *a, const float *scale, const float *shift, void *out_,
                                       int64_t rows, int cols, float eps) {
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
@@ -297,7 +322,7 @@ __global__ void adaln_modulate_kernel(const float *a, const float *scale, const 
     const float rstd = rsqrtf(warp_sum(sq) / float(cols) + eps);
     const float4 *s4 = reinterpret_cast<const float4 *>(scale + row * cols);
     const float4 *b4 = reinterpret_cast<const float4 *>(shift + row * cols);
-    float4 *o4 = reinterpret_cast<float4 *>(out + row * cols);
+    float4 *o4 = reinterpret_cast<float4 *>(static_cast<float *>(out_) + row * cols);
 #pragma unroll
     for (int j = 0; j < MAXV; ++j) {
       int idx = lane + 32 * j;
@@ -307,7 +332,10 @@ __global__ void adaln_modulate_kernel(const float *a, const float *scale, const 
         r.y = epilogue_value<BL_EPI_MODULATION>((v[j].y - mean) * rstd, sc.y, sh.y);
         r.z = epilogue_value<BL_EPI_MODULATION>((v[j].z - mean) * rstd, sc.z, sh.z);
         r.w = epilogue_value<BL_EPI_MODULATION>((v[j].w - mean) * rstd, sc.w, sh.w);
-        o4[idx] = r;
+        if constexpr (SPLIT)
+          store_split3_4(static_cast<__nv_bfloat16 *>(out_), rows * cols, row * cols + 4 * idx, r.x, r.y, r.z, r.w);
+        else
+          o4[idx] = r;
       }
     }
   }
@@ -513,11 +541,55 @@ int bl_adaln_modulate(const float *a, const float *scale, const float *shift, fl
   auto s = as_stream(stream);
   int blocks = grid_for(rows, 8);
   if (cols <= 512)
-    adaln_modulate_kernel<4><<<blocks, 256, 0, s>>>(a, scale, shift, out, rows, int(cols), eps);
+    adaln_modulate_kernel<4, false><<<blocks, 256, 0, s>>>(a, scale, shift, out, rows, int(cols), eps);
   else if (cols <= 1024)
-    adaln_modulate_kernel<8><<<blocks, 256, 0, s>>>(a, scale, shift, out, rows, int(cols), eps);
+    adaln_modulate_kernel<8, false><<<blocks, 256, 0, s>>>(a, scale, shift, out, rows, int(cols), eps);
   else
-    adaln_modulate_kernel<16><<<blocks, 256, 0, s>>>(a, scale, shift, out, rows, int(cols), eps);
+    adaln_modulate_kernel<16, false><<<blocks, 256, 0, s>>>(a, scale, shift, out, rows, int(cols), eps);
+  BL_LAUNCH_CHECK();
+  return BL_OK;
+}
+
+int bl_adaln_modulate_split3(const float *a, const float *scale, const float *shift, void *out3, int64_t rows,
+                             int64_t cols, float eps, void *stream) {
+  BL_REQUIRE(rows >= 0 && cols > 0, "bl_adaln_modulate_split3: bad shape");
+  if (rows == 0) return BL_OK;
+  BL_REQUIRE(a && scale && shift && out3, "bl_adaln_modulate_split3: null pointer");
+  BL_REQUIRE(cols % 4 == 0 && cols <= 32 * 4 * 16, "bl_adaln_modulate_split3: cols must be a multiple of 4, <= 2048");
+  BL_REQUIRE(aligned_to(a, 16) && aligned_to(scale, 16) && aligned_to(shift, 16) && aligned_to(out3, 8),
+             "bl_adaln_modulate_split3: misaligned pointer");
+  BL_REQUIRE(eps > 0.f, "bl_adaln_modulate_split3: eps must be positive");
+  auto s = as_stream(stream);
+  int blocks = grid_for(rows, 8);
+  if (cols <= 512)
+    adaln_modulate_kernel<4, true><<<blocks, 256, 0, s>>>(a, scale, shift, out3, rows, int(cols), eps);
+  else if (cols <= 1024)
+    adaln_modulate_kernel<8, true><<<blocks, 256, 0, s>>>(a, scale, shift, out3, rows, int(cols), eps);
+  else
+    adaln_modulate_kernel<16, true><<<blocks, 256, 0, s>>>(a, scale, shift, out3, rows, int(cols), eps);
+  BL_LAUNCH_CHECK();
+  return BL_OK;
+}
+
+int bl_diffusion_epilogue_split3(const float *a, const float *b, const float *c, void *out3, int64_t rows,
+                                 int64_t cols, int kind, void *stream) {
+  BL_REQUIRE(kind == BL_EPI_MODULATION || kind == BL_EPI_GATE || kind == BL_EPI_GATED_SWIGLU,
+             "bl_diffusion_epilogue_split3: unknown kind %d", kind);
+  BL_REQUIRE(rows >= 0 && cols >= 0, "bl_diffusion_epilogue_split3: negative shape");
+  if (rows == 0 || cols == 0) return BL_OK;
+  BL_REQUIRE(a && b && out3 && (kind != BL_EPI_MODULATION || c), "bl_diffusion_epilogue_split3: null pointer");
+  BL_REQUIRE(cols % 4 == 0 && aligned_to(a, 16) && aligned_to(b, 16) && aligned_to(out3, 8) &&
+                 (kind != BL_EPI_MODULATION || aligned_to(c, 16)),
+             "bl_diffusion_epilogue_split3: cols % 4 == 0 and 16-byte aligned operands");
+  auto s = as_stream(stream);
+  int blocks = grid_for(rows * (cols / 4), 256);
+  auto *o = static_cast<__nv_bfloat16 *>(out3);
+  if (kind == BL_EPI_MODULATION)
+    diffusion_epilogue_split3_kernel<BL_EPI_MODULATION><<<blocks, 256, 0, s>>>(a, b, c, o, rows, cols);
+  else if (kind == BL_EPI_GATE)
+    diffusion_epilogue_split3_kernel<BL_EPI_GATE><<<blocks, 256, 0, s>>>(a, b, c, o, rows, cols);
+  else
+    diffusion_epilogue_split3_kernel<BL_EPI_GATED_SWIGLU><<<blocks, 256, 0, s>>>(a, b, c, o, rows, cols);
   BL_LAUNCH_CHECK();
   return BL_OK;
 }

@@ -70,6 +70,49 @@ __global__ void layernorm_rows_vec_kernel(const Tin *x, const float *w, const fl
   }
 }
 
+// fp32 rows -> LayerNorm -> three bf16 planes (the fp32 linears' operand form).
+template <int V>
+__global__ void layernorm_split3_kernel(const float *x, const float *w, const float *b, __nv_bfloat16 *out,
+                                        int64_t rows, float eps) {
+  constexpr int C = 128 * V;
+  const int lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  const int64_t plane = rows * C;
+  for (int64_t row = blockIdx.x * int64_t(warps) + (threadIdx.x >> 5); row < rows;
+       row += int64_t(gridDim.x) * warps) {
+    float v[V][4];
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      Vec4<float>::load(x + row * C + j * 128 + lane * 4, v[j]);
+      sum += (v[j][0] + v[j][1]) + (v[j][2] + v[j][3]);
+    }
+    const float mean = warp_sum(sum) * (1.f / C);
+    float sq = 0.f;
+#pragma unroll
+    for (int j = 0; j < V; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float d = v[j][e] - mean;
+        sq += d * d;
+      }
+    const float rstd = rsqrtf(warp_sum(sq) * (1.f / C) + eps);
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      float r[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        int c = j * 128 + lane * 4 + e;
+        float y = (v[j][e] - mean) * rstd;
+        if (w) y = y * w[c];
+        if (b) y = y + b[c];
+        r[e] = y;
+      }
+      store_split3_4(out, plane, row * C + j * 128 + lane * 4, r[0], r[1], r[2], r[3]);
+    }
+  }
+}
+
 // Any width, any alignment: two passes over global memory.
 template <typename Tin, typename Tout>
 __global__ void layernorm_rows_generic_kernel(const Tin *x, const float *w, const float *b, Tout *out,
@@ -216,4 +259,35 @@ extern "C" int bl_layernorm(const void *x, int x_dtype, int64_t rows, int64_t co
                             static_cast<float *>(out), s);
   return launch_layernorm(static_cast<const __nv_bfloat16 *>(x), rows, cols, channel_first, weight, bias, eps,
                           static_cast<__nv_bfloat16 *>(out), s);
+}
+
+extern "C" int bl_layernorm_split3(const float *x, int64_t rows, int64_t cols, const float *weight,
+                                   const float *bias, float eps, void *out3, void *stream) {
+  BL_REQUIRE(rows >= 0 && cols > 0, "bl_layernorm_split3: bad shape");
+  BL_REQUIRE(eps > 0.f, "bl_layernorm_split3: eps must be positive");
+  if (rows == 0) return BL_OK;
+  BL_REQUIRE(x && out3, "bl_layernorm_split3: null pointer");
+  BL_REQUIRE(cols % 128 == 0 && cols <= 1024 && aligned_to(x, 16) && aligned_to(out3, 8),
+             "bl_layernorm_split3: cols must be a multiple of 128 (<= 1024), x 16-byte aligned");
+  auto s = as_stream(stream);
+  int64_t blocks = (rows + 7) / 8, cap = int64_t(num_sms()) * 16;
+  if (blocks > cap) blocks = cap;
+  auto *o = static_cast<__nv_bfloat16 *>(out3);
+  switch (cols / 128) {
+#define BL_LN3_CASE(V) \
+  case V:              \
+    layernorm_split3_kernel<V><<<int(blocks), 256, 0, s>>>(x, weight, bias, o, rows, eps); \
+    break;
+    BL_LN3_CASE(1)
+    BL_LN3_CASE(2)
+    BL_LN3_CASE(3)
+    BL_LN3_CASE(4)
+    BL_LN3_CASE(5)
+    BL_LN3_CASE(6)
+    BL_LN3_CASE(7)
+    BL_LN3_CASE(8)
+#undef BL_LN3_CASE
+  }
+  BL_LAUNCH_CHECK();
+  return BL_OK;
 }

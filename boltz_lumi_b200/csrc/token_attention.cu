@@ -41,7 +41,9 @@ struct TokArgs {
   int64_t mask_sb;
   float scale, inf;
   int heads, n;
-  float *out;  // [B][N][H][d] contiguous
+  float *out;  // [B][N][H][d] contiguous, or null when out3 is set
+  __nv_bfloat16 *out3;  // [3][B * N][H * d] bf16 planes of the output, or null
+  int batch;
 };
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, int bytes) {
@@ -238,12 +240,17 @@ __global__ void __launch_bounds__(kThreads, 2) token_attention_kernel(const TokA
     const int qi = q0 + 4 * tq + i;
     if (qi >= n) continue;
     const float inv = 1.f / l[i];
-    float *dst = a.out + ((int64_t(b) * n + qi) * a.heads + h) * D + tk * kDpt;
+    const int64_t at = ((int64_t(b) * n + qi) * a.heads + h) * D + tk * kDpt;
+    float *dst = a.out + at;
     const float *gr = a.g ? a.g + b * a.sb + h * a.sh + int64_t(qi) * a.si + tk * kDpt : nullptr;
 #pragma unroll
     for (int e = 0; e < kDpt; ++e) {
       const float y = o[i][e] * inv;
-      dst[e] = gr ? y * (1.f / (1.f + expf(-gr[e]))) : y;
+      const float out_v = gr ? y * (1.f / (1.f + expf(-gr[e]))) : y;
+      if (a.out3)
+        store_split3_1(a.out3, int64_t(a.batch) * n * a.heads * D, at + e, out_v);
+      else
+        dst[e] = out_v;
     }
   }
 }
@@ -268,12 +275,12 @@ extern "C" int bl_token_attention(const float *q, const float *k, const float *v
                                   const float *bias, int64_t bias_sb, int64_t bias_sh, int64_t bias_sq,
                                   int64_t bias_sk, int64_t bias_batch_div, const float *mask, int64_t mask_sb,
                                   float scale, float inf, int64_t batch, int64_t heads, int64_t n, int64_t head_dim,
-                                  float *out, void *stream) {
+                                  float *out, void *out3, void *stream) {
   BL_REQUIRE(batch >= 0 && heads > 0 && n >= 0, "bl_token_attention: bad shape");
   if (batch == 0 || n == 0) return BL_OK;
   BL_REQUIRE(head_dim == 24 || head_dim == 32 || head_dim == 48 || head_dim == 64,
              "bl_token_attention: head_dim 24, 32, 48 or 64");
-  BL_REQUIRE(q && k && v && bias && out && bias_batch_div >= 1, "bl_token_attention: null pointer");
+  BL_REQUIRE(q && k && v && bias && (out || out3) && bias_batch_div >= 1, "bl_token_attention: null pointer");
   BL_REQUIRE(aligned_to(q, 16) && aligned_to(k, 16) && aligned_to(v, 16) && aligned_to(g, 4) && si % 4 == 0 &&
                  sh % 4 == 0 &&
                  sb % 4 == 0,
@@ -288,7 +295,7 @@ extern "C" int bl_token_attention(const float *q, const float *k, const float *v
   a.mask = mask, a.mask_sb = mask_sb;
   a.scale = scale, a.inf = inf;
   a.heads = int(heads), a.n = int(n);
-  a.out = out;
+  a.out = out, a.out3 = static_cast<__nv_bfloat16 *>(out3), a.batch = int(batch);
   cudaStream_t s = as_stream(stream);
   if (head_dim == 24) return launch_token<24>(a, int(batch), s);
   if (head_dim == 32) return launch_token<32>(a, int(batch), s);

@@ -122,6 +122,20 @@ def _linear32(module, name, x, weights, biases=None, x3=None):
     return F.linear(x, w, bias)
 
 
+def _linear32_planes(module, name, x3, lead, weights, biases=None):
+    """:func:`_linear32` on an input already in split form (x3 = bf16 [3, rows, K],
+    written by a fused producer); the output is fp32 [*lead, N]."""
+    w3, bias = _split_weight(module, name, weights, biases)
+    n = w3.shape[1]
+    if n % 4 == 0:
+        y = torch.empty(*lead, n, device=x3.device, dtype=torch.float32)
+        kernels.linear_split3_fast(x3, w3, bias, y)
+        return y
+    x = x3.float().sum(0).view(*lead, x3.shape[-1])  # exact to 2^-27 relative
+    w = torch.cat(list(weights), 0) if len(weights) > 1 else weights[0]
+    return F.linear(x, w, bias)
+
+
 def _split_input(x):
     """split3(x) when x can feed bl_linear_split3, else None."""
     return kernels.split3_fast(x) if x.dtype == torch.float32 and x.is_cuda and x.shape[-1] % 8 == 0 else None
@@ -338,29 +352,58 @@ def adaln_forward(self, a, s):
     if a.dtype != torch.float32 or s.dtype != torch.float32:
         raise RuntimeError("AdaLN kernels are fp32")
 
-    def conditioning():  # depends on s only: reused across steps inside atom_conditioning_cache
+    with torch.autocast("cuda", enabled=False):
+        scale, shift = _adaln_conditioning(self, s)
+        return kernels.adaln_modulate(a, scale, shift, self.a_norm.eps)
+
+
+def _adaln_conditioning(self, s):
+    """AdaLN's (s_scale(s_norm(s)), s_bias(s_norm(s))); depends on s only, so
+    reused across steps inside atom_conditioning_cache."""
+
+    def conditioning():
+        cols = s.shape[-1]
+        if cols % 128 == 0 and cols <= 1024:
+            # LayerNorm straight into the linears' split operand form.
+            sn3 = kernels.layer_norm_split3(s, self.s_norm.weight, getattr(self.s_norm, "bias", None),
+                                            self.s_norm.eps)
+            lead = s.shape[:-1]
+            return (_linear32_planes(self, "_bl_w3_scale", sn3, lead, [self.s_scale.weight], [self.s_scale.bias]),
+                    _linear32_planes(self, "_bl_w3_shift", sn3, lead, [self.s_bias.weight], [self.s_bias.bias]))
         sn = kernels.layer_norm(s, self.s_norm.weight, getattr(self.s_norm, "bias", None), self.s_norm.eps,
                                 out_dtype=torch.float32)
         sn3 = _split_input(sn)
         return (_linear32(self, "_bl_w3_scale", sn, [self.s_scale.weight], [self.s_scale.bias], x3=sn3),
                 _linear32(self, "_bl_w3_shift", sn, [self.s_bias.weight], [self.s_bias.bias], x3=sn3))
 
-    with torch.autocast("cuda", enabled=False):
-        scale, shift = atom_conditioning.lookup(self, "adaln", s, conditioning)
-        return kernels.adaln_modulate(a, scale, shift, self.a_norm.eps)
+    return atom_conditioning.lookup(self, "adaln", s, conditioning)
 
 
 def conditioned_transition_forward(self, a, s):
     """Upstream ``ConditionedTransitionBlock.forward(a, s)`` (diffusion.py:60-68), fp32."""
     with torch.autocast("cuda", enabled=False):
-        a = adaln_forward(self.adaln, a, s)
-        a3 = _split_input(a)
-        projected = _linear32(self, "_bl_w3_swish", a, [self.swish_gate[0].weight], [self.swish_gate[0].bias], x3=a3)
-        third = _linear32(self, "_bl_w3_atob", a, [self.a_to_b.weight], [self.a_to_b.bias], x3=a3)
-        b = kernels.epilogue(projected.contiguous(), third.contiguous(), None, kernels.GATED_SWIGLU)
+        dim, lead = a.shape[-1], a.shape[:-1]
+        inner = self.a_to_b.weight.shape[0]
         op = self.output_projection[0]
         gate = atom_conditioning.lookup(self, "gate", s, lambda: _linear32(self, "_bl_w3_gate", s, [op.weight], [op.bias]))
-        out = _linear32(self, "_bl_w3_btoa", b, [self.b_to_a.weight], [self.b_to_a.bias])
+        if dim % 8 == 0 and dim <= 2048 and inner % 8 == 0 and a.dtype == torch.float32:
+            # a' = AdaLN(a, s) and b = SwiGLU(...) leave their kernels as the
+            # split operands of the linears that consume them.
+            scale, shift = _adaln_conditioning(self.adaln, s)
+            a3 = kernels.adaln_modulate_split3(a, scale, shift, self.adaln.a_norm.eps)
+            projected = _linear32_planes(self, "_bl_w3_swish", a3, lead, [self.swish_gate[0].weight],
+                                         [self.swish_gate[0].bias])
+            third = _linear32_planes(self, "_bl_w3_atob", a3, lead, [self.a_to_b.weight], [self.a_to_b.bias])
+            b3 = kernels.epilogue_split3(projected, third, None, kernels.GATED_SWIGLU)
+            out = _linear32_planes(self, "_bl_w3_btoa", b3, lead, [self.b_to_a.weight], [self.b_to_a.bias])
+        else:
+            a = adaln_forward(self.adaln, a, s)
+            a3 = _split_input(a)
+            projected = _linear32(self, "_bl_w3_swish", a, [self.swish_gate[0].weight], [self.swish_gate[0].bias],
+                                  x3=a3)
+            third = _linear32(self, "_bl_w3_atob", a, [self.a_to_b.weight], [self.a_to_b.bias], x3=a3)
+            b = kernels.epilogue(projected.contiguous(), third.contiguous(), None, kernels.GATED_SWIGLU)
+            out = _linear32(self, "_bl_w3_btoa", b, [self.b_to_a.weight], [self.b_to_a.bias])
         return kernels.epilogue(gate.contiguous(), out.contiguous(), None, kernels.GATE)
 
 
@@ -413,7 +456,7 @@ def attend_with_bias(self, s, bias, mask, k_in):
         mask = mask.float().contiguous()
     if b == 0 or n == 0:
         return self.proj_o(s.new_zeros(b, n, c))
-    out = torch.empty(b, n, c, device=s.device, dtype=torch.float32)
+    out3 = torch.empty(3, b * n, c, device=s.device, dtype=torch.bfloat16)  # the output, as proj_o's operand
     stream = stream_of(s)
     if k_in is s:
         # One GEMM for q | k | v | g; the kernel reads the four column blocks in place.
@@ -422,7 +465,7 @@ def attend_with_bias(self, s, bias, mask, k_in):
                          [self.proj_q.bias, None, None, None])
         base = proj.data_ptr()
         kernels.launch_token_attention(base, base + 4 * c, base + 8 * c, base + 12 * c, (n * 4 * c, 4 * c, d), bias,
-                                       mask, self.inf, b, heads, n, d, out, stream)
+                                       mask, self.inf, b, heads, n, d, None, stream, out3=out3)
     else:  # four contiguous [B, N, c_s] projections share one stride layout
         s3, k3 = _split_input(s), _split_input(k_in)
         q = _linear32(self, "_bl_w3_q", s, [self.proj_q.weight], [self.proj_q.bias], x3=s3)
@@ -430,8 +473,8 @@ def attend_with_bias(self, s, bias, mask, k_in):
         v = _linear32(self, "_bl_w3_v", k_in, [self.proj_v.weight], x3=k3)
         g = _linear32(self, "_bl_w3_g", s, [self.proj_g.weight], x3=s3)
         kernels.launch_token_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), (n * c, c, d), bias,
-                                       mask, self.inf, b, heads, n, d, out, stream)
-    return _linear32(self, "_bl_w3_o", out, [self.proj_o.weight], [self.proj_o.bias])
+                                       mask, self.inf, b, heads, n, d, None, stream, out3=out3)
+    return _linear32_planes(self, "_bl_w3_o", out3, (b, n), [self.proj_o.weight], [self.proj_o.bias])
 
 
 def token_attention_forward(self, s, z, mask, k_in, multiplicity=1):

@@ -234,14 +234,17 @@ def attention_scale(head_dim):
     return float(torch.tensor(1.0, dtype=torch.float32) / torch.tensor(head_dim ** 0.5, dtype=torch.float32))
 
 
-def launch_token_attention(q_ptr, k_ptr, v_ptr, g_ptr, strides, bias, mask, inf, batch, heads, n, d, out, stream):
+def launch_token_attention(q_ptr, k_ptr, v_ptr, g_ptr, strides, bias, mask, inf, batch, heads, n, d, out, stream,
+                           out3=None):
     """bl_token_attention on raw operand pointers sharing ``strides`` (batch,
-    token, head) -- no validation; callers have checked shapes and dtypes."""
+    token, head) -- no validation; callers have checked shapes and dtypes.
+    With ``out3`` (bf16 [3, batch * n, heads * d]) the result is written as the
+    split planes instead of into ``out``."""
     mask_ptr, mask_sb = (None, 0) if mask is None else (mask.data_ptr(), mask.stride(0))
     bs = bias.stride()
     call("bl_token_attention", q_ptr, k_ptr, v_ptr, g_ptr, strides[0], strides[1], strides[2], bias.data_ptr(),
          bs[0], bs[1], bs[2], bs[3], batch // bias.shape[0], mask_ptr, mask_sb, attention_scale(d), float(inf),
-         batch, heads, n, d, out.data_ptr(), stream)
+         batch, heads, n, d, ptr(out), ptr(out3), stream)
     return out
 
 
@@ -285,7 +288,7 @@ def token_attention(q, k, v, bias, mask, inf, gate=None, scale=None):
     call("bl_token_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), ptr(gate), q.stride(0), q.stride(1),
          q.stride(2), bias.data_ptr(), bias.stride(0), bias.stride(1), bias.stride(2), bias.stride(3),
          batch // bias.shape[0], ptr(mask), mask_sb, float(scale), float(inf), batch, heads, n, d, out.data_ptr(),
-         stream_of(q))
+         None, stream_of(q))
     return out
 
 
@@ -342,3 +345,36 @@ def linear_f32(x, w3, bias=None, x3=None):
     m = x3.shape[1]
     y = torch.empty(*x.shape[:-1], n, device=x.device, dtype=torch.float32)
     return linear_split3_fast(x3, w3, bias, y)
+
+
+def layer_norm_split3(x, weight, bias, eps):
+    """LayerNorm of fp32 rows written as split planes [3, rows, C] (bl_layernorm_split3);
+    C % 128 == 0 and <= 1024."""
+    cols = x.shape[-1]
+    x = x.contiguous()
+    rows = x.numel() // cols
+    out = torch.empty(3, rows, cols, device=x.device, dtype=torch.bfloat16)
+    call("bl_layernorm_split3", x.data_ptr(), rows, cols, ptr(weight), ptr(bias), float(eps), out.data_ptr(),
+         torch.cuda.current_stream().cuda_stream)
+    return out
+
+
+def adaln_modulate_split3(a, scale, shift, eps):
+    """:func:`adaln_modulate` written as split planes [3, rows, C]."""
+    a, scale, shift = a.contiguous(), scale.contiguous(), shift.contiguous()
+    cols = a.shape[-1]
+    rows = a.numel() // cols
+    out = torch.empty(3, rows, cols, device=a.device, dtype=torch.bfloat16)
+    call("bl_adaln_modulate_split3", a.data_ptr(), scale.data_ptr(), shift.data_ptr(), out.data_ptr(), rows, cols,
+         float(eps), torch.cuda.current_stream().cuda_stream)
+    return out
+
+
+def epilogue_split3(a, b, c, kind):
+    """:func:`epilogue` written as split planes [3, rows, C] (C = output width)."""
+    cols = a.shape[-1] // 2 if kind == GATED_SWIGLU else a.shape[-1]
+    rows = a.numel() // a.shape[-1]
+    out = torch.empty(3, rows, cols, device=a.device, dtype=torch.bfloat16)
+    call("bl_diffusion_epilogue_split3", a.data_ptr(), b.data_ptr(), ptr(c), out.data_ptr(), rows, cols, kind,
+         torch.cuda.current_stream().cuda_stream)
+    return out

@@ -287,13 +287,16 @@ BL_API int bl_triangle_attention(const void *q, const void *k, const void *v, co
  * at b*mask_sb + j, or NULL for none; head_dim 24, 32, 48 or 64; out: fp32
  * [batch][n][heads][head_dim] contiguous.  Replaces the einsum / bias / mask /
  * softmax / einsum and the gate product of pair_bias.py:28-36 (prepared_forward).
+ * With out3 != NULL the result is written instead as three bf16 planes
+ * [3][batch * n][heads * head_dim] (the operand form of bl_linear_split3,
+ * for proj_o) and out may be NULL.
  */
 BL_API int bl_token_attention(const float *q, const float *k, const float *v, const float *g, int64_t sb,
                               int64_t si, int64_t sh,
                               const float *bias, int64_t bias_sb, int64_t bias_sh, int64_t bias_sq,
                               int64_t bias_sk, int64_t bias_batch_div, const float *mask, int64_t mask_sb,
                               float scale, float inf, int64_t batch, int64_t heads, int64_t n, int64_t head_dim,
-                              float *out, void *stream);
+                              float *out, void *out3, void *stream);
 
 /*
  * fp32-accurate linear layers on the bf16 tensor cores (three-way split).
@@ -312,6 +315,24 @@ BL_API int bl_token_attention(const float *q, const float *k, const float *v, co
 BL_API int bl_split3_bf16(const float *x, int64_t rows, int64_t cols, int64_t ldx, void *out, void *stream);
 BL_API int bl_linear_split3(const void *x3, int64_t m, int64_t k, const void *w3, int64_t n, const float *bias,
                             float *y, int64_t ldy, void *stream);
+
+/*
+ * Producers of fp32-linear operands that write the three bf16 planes
+ * [3][rows][cols] (as bl_split3_bf16 would) instead of fp32, saving the
+ * separate split pass:
+ *   bl_layernorm_split3:          LayerNorm of fp32 rows (cols % 128 == 0, <= 1024),
+ *                                 the s_norm of AdaLN (diffusion.py:55-57);
+ *   bl_adaln_modulate_split3:     bl_adaln_modulate's result (the conditioned
+ *                                 transition's a', diffusion.py:63-65);
+ *   bl_diffusion_epilogue_split3: bl_diffusion_epilogue's result (cols % 4 == 0;
+ *                                 GATED_SWIGLU's b feeds b_to_a, diffusion.py:66-68).
+ */
+BL_API int bl_layernorm_split3(const float *x, int64_t rows, int64_t cols, const float *weight, const float *bias,
+                               float eps, void *out3, void *stream);
+BL_API int bl_adaln_modulate_split3(const float *a, const float *scale, const float *shift, void *out3, int64_t rows,
+                                    int64_t cols, float eps, void *stream);
+BL_API int bl_diffusion_epilogue_split3(const float *a, const float *b, const float *c, void *out3, int64_t rows,
+                                        int64_t cols, int kind, void *stream);
 
 /*
  * Pair transition (LayerNorm -> fc1|fc2 -> SwiGLU -> fc3, the bf16-autocast

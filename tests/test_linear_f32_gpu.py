@@ -73,3 +73,40 @@ def test_skinny_cluster_split_is_deterministic(m, n, k):
     assert all(torch.equal(ys[0], y) for y in ys[1:])
     ref = x.double() @ w3.double().sum(0).T + bias.double()
     assert (ys[0].double() - ref).abs().max().item() <= 2.0 ** -17 * ref.abs().max().item()
+
+
+@pytest.mark.parametrize("rows,cols", [(117, 768), (5, 128), (300, 384)])
+def test_fused_split_producers_match_split3(rows, cols):
+    """The producers that write split planes directly (LayerNorm, AdaLN
+    modulation, diffusion epilogue, token attention) must give exactly
+    split3 of their fp32 results."""
+    g = torch.Generator().manual_seed(rows + cols)
+    x = torch.randn(rows, cols, generator=g).cuda()
+    w, b = (torch.randn(cols, generator=g).cuda() for _ in range(2))
+    sc, sh = (torch.randn(rows, cols, generator=g).cuda() for _ in range(2))
+    with torch.inference_mode():
+        ln = kernels.layer_norm(x, w, b, 1e-5, out_dtype=torch.float32)
+        assert torch.equal(kernels.layer_norm_split3(x, w, b, 1e-5), kernels.split3(ln))
+        mod = kernels.adaln_modulate(x, sc, sh, 1e-5)
+        assert torch.equal(kernels.adaln_modulate_split3(x, sc, sh, 1e-5), kernels.split3(mod))
+        a2 = torch.randn(rows, 2 * cols, generator=g).cuda()
+        for kind, args in ((kernels.GATED_SWIGLU, (a2, x, None)), (kernels.GATE, (x, sc, None)),
+                           (kernels.MODULATION, (x, sc, sh))):
+            ref = kernels.epilogue(*args, kind)
+            assert torch.equal(kernels.epilogue_split3(*args, kind), kernels.split3(ref)), kind
+
+
+def test_token_attention_split_output():
+    g = torch.Generator().manual_seed(3)
+    b, n, h, d = 2, 70, 16, 48
+    q, k, v, gate = (torch.randn(b, n, h, d, generator=g).cuda() for _ in range(4))
+    bias = torch.randn(b, h, n, n, generator=g).cuda()
+    mask = torch.ones(b, n).cuda()
+    with torch.inference_mode():
+        out = kernels.token_attention(q, k, v, bias, mask, 1e6, gate=gate)
+        out3 = torch.empty(3, b * n, h * d, device="cuda", dtype=torch.bfloat16)
+        kernels.launch_token_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), gate.data_ptr(),
+                                       q.stride()[:3], bias, mask, 1e6, b, h, n, d, None,
+                                       torch.cuda.current_stream().cuda_stream, out3=out3)
+    torch.cuda.synchronize()
+    assert torch.equal(out3, kernels.split3(out.view(b * n, h * d)))
