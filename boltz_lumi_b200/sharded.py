@@ -40,6 +40,16 @@ __all__ = ["Comm", "SingleComm", "TorchComm", "ThreadComm", "rows_to_columns", "
 # ---------------------------------------------------------------------------
 # Collectives
 # ---------------------------------------------------------------------------
+class _Ready:
+    """A collective that has already completed."""
+
+    def __init__(self, value):
+        self.value = value
+
+    def wait(self):
+        return self.value
+
+
 class Comm:
     """The two collectives the sharded block needs."""
 
@@ -49,6 +59,11 @@ class Comm:
     def all_gather(self, t):
         """[world, *t.shape]: entry p is rank p's tensor."""
         raise NotImplementedError
+
+    def all_gather_async(self, t):
+        """Start an all_gather; ``.wait()`` returns its result and orders the
+        current stream after it (here: completed at once)."""
+        return _Ready(self.all_gather(t))
 
     def all_to_all(self, t):
         """t is [world, ...] with chunk p addressed to rank p; returns [world, ...]
@@ -79,6 +94,22 @@ class TorchComm(Comm):
         self.dist.all_to_all_single(out, t, group=self.group)
         return out
 
+    def all_gather_async(self, t):
+        """NCCL runs the gather on its own stream; compute queued on the
+        current stream before ``.wait()`` overlaps it."""
+        t = t.contiguous()
+        flat = t.view(-1)
+        out = torch.empty(self.world * flat.numel(), dtype=t.dtype, device=t.device)
+        work = self.dist.all_gather_into_tensor(out, flat, group=self.group, async_op=True)
+        shape = (self.world,) + tuple(t.shape)
+
+        class _Pending:
+            def wait(self):
+                work.wait()
+                return out.view(shape)
+
+        return _Pending()
+
 
 class SingleComm(Comm):
     """World of one (no process group needed)."""
@@ -94,7 +125,7 @@ class _ThreadHub:
     def __init__(self, world):
         self.world = world
         self.slots = [None] * world
-        self.barrier = threading.Barrier(world)
+        self.barrier = threading.Barrier(world, timeout=300)  # a rank that dies breaks it instead of hanging
 
 
 class ThreadComm(Comm):
@@ -175,13 +206,21 @@ def _trimul_slab(module, x, mask_rows, comm, swap):
          _f32(module.norm_in.bias).data_ptr(), float(module.norm_in.eps), w["w_in"].data_ptr(),
          mask_rows.data_ptr(), planes.data_ptr(), n_pad, xn.data_ptr(), stream)
     rows_op, cols_op = (planes[128:], planes[:128]) if swap else (planes[:128], planes[128:])
-    cols_all = comm.all_gather(cols_op.contiguous())  # [P, 128, n_loc, n_pad]
     prod = torch.empty(128, n_loc, n_pad, device=x.device, dtype=_BF16)
     plane = n_loc * n_pad
-    for p in range(comm.world):
-        # O_c[i in I_r, j in I_p] = sum_k rows_c[i, k] cols_c[p][j, k]
-        call("bl_batched_gemm", rows_op.data_ptr(), 0, n_pad, plane, cols_all[p].data_ptr(), 0, n_pad, plane,
-             prod.data_ptr() + p * n_loc * 2, n_pad, plane, 128, n_loc, n_loc, n, None, stream)
+    # The other ranks' column planes arrive in channel groups: the per-channel
+    # products of group g run while group g + 1 is still being gathered.
+    groups = 4 if comm.world > 1 else 1
+    cg = 128 // groups
+    pending = [comm.all_gather_async(cols_op[g * cg:(g + 1) * cg]) for g in range(groups)]
+    for g in range(groups):
+        cols_all = pending[g].wait()  # [P, cg, n_loc, n_pad]
+        off = g * cg * plane * 2
+        for p in range(comm.world):
+            # O_c[i in I_r, j in I_p] = sum_k rows_c[i, k] cols_c[p][j, k]
+            call("bl_batched_gemm", rows_op.data_ptr() + off, 0, n_pad, plane, cols_all[p].data_ptr(), 0, n_pad,
+                 plane, prod.data_ptr() + off + p * n_loc * 2, n_pad, plane, cg, n_loc, n_loc, n, None, stream)
+        del cols_all
     norm = module.norm_out
     call("bl_trimul_output", prod.data_ptr(), n, n_loc, n_pad, _f32(norm.weight).data_ptr(),
          _f32(norm.bias).data_ptr(), float(norm.eps), xn.data_ptr(), w["w_pg"].data_ptr(), x.data_ptr(), None,
