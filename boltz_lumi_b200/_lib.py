@@ -15,7 +15,7 @@ import torch
 LIBRARY_PATH = Path(__file__).resolve().parent / "libboltz_b200.so"
 
 BL_F32, BL_BF16 = 0, 1
-BL_EPI_MODULATION, BL_EPI_GATE, BL_EPI_GATED_SWIGLU = 0, 1, 3
+BL_EPI_MODULATION, BL_EPI_GATE, BL_EPI_GATED_SWIGLU, BL_EPI_SWIGLU = 0, 1, 3, 2
 
 _p = c_void_p
 _i64p = ctypes.POINTER(c_int64)

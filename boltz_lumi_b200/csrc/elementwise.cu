@@ -217,6 +217,9 @@ template <int KIND> __device__ __forceinline__ float epilogue_value(float a, flo
     return __fadd_rn(product, c);
   } else if constexpr (KIND == BL_EPI_GATE) {
     return __fmul_rn(sigmoidf_acc(a), b);
+  } else if constexpr (KIND == BL_EPI_SWIGLU) {
+    // a: first half (silu input), b: second half.
+    return __fmul_rn(a / (1.f + expf(-a)), b);
   } else {
     // a: first half (value), b: second half (gate input), c: a_to_b.
     float activation = b / (1.f + expf(-b));
@@ -234,11 +237,11 @@ __global__ void diffusion_epilogue_split3_kernel(const float *a, const float *b,
        t += int64_t(gridDim.x) * blockDim.x) {
     const int64_t row = t / width, col = t % width;
     float4 av, bv, cv = make_float4(0.f, 0.f, 0.f, 0.f);
-    if constexpr (KIND == BL_EPI_GATED_SWIGLU) {
+    if constexpr (KIND == BL_EPI_GATED_SWIGLU || KIND == BL_EPI_SWIGLU) {
       const float4 *a4 = reinterpret_cast<const float4 *>(a) + row * 2 * width;
       av = a4[col];
       bv = a4[width + col];
-      cv = reinterpret_cast<const float4 *>(b)[t];
+      if constexpr (KIND == BL_EPI_GATED_SWIGLU) cv = reinterpret_cast<const float4 *>(b)[t];
     } else {
       av = reinterpret_cast<const float4 *>(a)[t];
       bv = reinterpret_cast<const float4 *>(b)[t];
@@ -259,11 +262,11 @@ __global__ void diffusion_epilogue_kernel(const float *a, const float *b, const 
     int64_t row = t / width, col = t % width;
     if constexpr (VEC) {
       float4 av, bv, cv = make_float4(0.f, 0.f, 0.f, 0.f);
-      if constexpr (KIND == BL_EPI_GATED_SWIGLU) {
+      if constexpr (KIND == BL_EPI_GATED_SWIGLU || KIND == BL_EPI_SWIGLU) {
         const float4 *a4 = reinterpret_cast<const float4 *>(a) + row * 2 * width;
         av = a4[col];
         bv = a4[width + col];
-        cv = reinterpret_cast<const float4 *>(b)[t];
+        if constexpr (KIND == BL_EPI_GATED_SWIGLU) cv = reinterpret_cast<const float4 *>(b)[t];
       } else {
         av = reinterpret_cast<const float4 *>(a)[t];
         bv = reinterpret_cast<const float4 *>(b)[t];
@@ -274,10 +277,10 @@ __global__ void diffusion_epilogue_kernel(const float *a, const float *b, const 
       reinterpret_cast<float4 *>(out)[t] = r;
     } else {
       float av, bv, cv = 0.f;
-      if constexpr (KIND == BL_EPI_GATED_SWIGLU) {
+      if constexpr (KIND == BL_EPI_GATED_SWIGLU || KIND == BL_EPI_SWIGLU) {
         av = a[row * 2 * cols + col];
         bv = a[row * 2 * cols + cols + col];
-        cv = b[t];
+        if constexpr (KIND == BL_EPI_GATED_SWIGLU) cv = b[t];
       } else {
         av = a[t];
         bv = b[t];
@@ -501,11 +504,12 @@ int bl_gate_split(const void *p, const void *g, int64_t pair_stride, const float
 
 int bl_diffusion_epilogue(const float *a, const float *b, const float *c, float *out, int64_t rows,
                           int64_t cols, int kind, void *stream) {
-  BL_REQUIRE(kind == BL_EPI_MODULATION || kind == BL_EPI_GATE || kind == BL_EPI_GATED_SWIGLU,
+  BL_REQUIRE(kind == BL_EPI_MODULATION || kind == BL_EPI_GATE || kind == BL_EPI_GATED_SWIGLU ||
+                 kind == BL_EPI_SWIGLU,
              "bl_diffusion_epilogue: unknown kind %d", kind);
   BL_REQUIRE(rows >= 0 && cols >= 0, "bl_diffusion_epilogue: negative shape");
   if (rows == 0 || cols == 0) return BL_OK;
-  BL_REQUIRE(a && b && out, "bl_diffusion_epilogue: null pointer");
+  BL_REQUIRE(a && (b || kind == BL_EPI_SWIGLU) && out, "bl_diffusion_epilogue: null pointer");
   BL_REQUIRE(kind != BL_EPI_MODULATION || c, "bl_diffusion_epilogue: MODULATION needs c");
   bool vec = cols % 4 == 0 && aligned_to(a, 16) && aligned_to(b, 16) && aligned_to(out, 16) &&
              (kind != BL_EPI_MODULATION || aligned_to(c, 16));
@@ -523,6 +527,7 @@ int bl_diffusion_epilogue(const float *a, const float *b, const float *c, float 
     BL_EPI_CASE(BL_EPI_MODULATION)
     BL_EPI_CASE(BL_EPI_GATE)
     BL_EPI_CASE(BL_EPI_GATED_SWIGLU)
+    BL_EPI_CASE(BL_EPI_SWIGLU)
   }
 #undef BL_EPI_CASE
   BL_LAUNCH_CHECK();
@@ -573,11 +578,13 @@ int bl_adaln_modulate_split3(const float *a, const float *scale, const float *sh
 
 int bl_diffusion_epilogue_split3(const float *a, const float *b, const float *c, void *out3, int64_t rows,
                                  int64_t cols, int kind, void *stream) {
-  BL_REQUIRE(kind == BL_EPI_MODULATION || kind == BL_EPI_GATE || kind == BL_EPI_GATED_SWIGLU,
+  BL_REQUIRE(kind == BL_EPI_MODULATION || kind == BL_EPI_GATE || kind == BL_EPI_GATED_SWIGLU ||
+                 kind == BL_EPI_SWIGLU,
              "bl_diffusion_epilogue_split3: unknown kind %d", kind);
   BL_REQUIRE(rows >= 0 && cols >= 0, "bl_diffusion_epilogue_split3: negative shape");
   if (rows == 0 || cols == 0) return BL_OK;
-  BL_REQUIRE(a && b && out3 && (kind != BL_EPI_MODULATION || c), "bl_diffusion_epilogue_split3: null pointer");
+  BL_REQUIRE(a && (b || kind == BL_EPI_SWIGLU) && out3 && (kind != BL_EPI_MODULATION || c),
+             "bl_diffusion_epilogue_split3: null pointer");
   BL_REQUIRE(cols % 4 == 0 && aligned_to(a, 16) && aligned_to(b, 16) && aligned_to(out3, 8) &&
                  (kind != BL_EPI_MODULATION || aligned_to(c, 16)),
              "bl_diffusion_epilogue_split3: cols % 4 == 0 and 16-byte aligned operands");
@@ -588,6 +595,8 @@ int bl_diffusion_epilogue_split3(const float *a, const float *b, const float *c,
     diffusion_epilogue_split3_kernel<BL_EPI_MODULATION><<<blocks, 256, 0, s>>>(a, b, c, o, rows, cols);
   else if (kind == BL_EPI_GATE)
     diffusion_epilogue_split3_kernel<BL_EPI_GATE><<<blocks, 256, 0, s>>>(a, b, c, o, rows, cols);
+  else if (kind == BL_EPI_SWIGLU)
+    diffusion_epilogue_split3_kernel<BL_EPI_SWIGLU><<<blocks, 256, 0, s>>>(a, b, c, o, rows, cols);
   else
     diffusion_epilogue_split3_kernel<BL_EPI_GATED_SWIGLU><<<blocks, 256, 0, s>>>(a, b, c, o, rows, cols);
   BL_LAUNCH_CHECK();

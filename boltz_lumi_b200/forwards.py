@@ -434,13 +434,15 @@ def token_attention_supported(module, s, k_in, bias, mask=None):
             and all(p.bias is None for p in (module.proj_k, module.proj_v, module.proj_g)))
 
 
-def attend_with_bias(self, s, bias, mask, k_in):
+def attend_with_bias(self, s, bias, mask, k_in, s3=None):
     """Upstream attentionv2 ``AttentionPairBias`` after ``proj_z``: projections,
     fused fp32 attention with bias, key mask and sigmoid gate, then ``proj_o``.
 
     ``bias`` is fp32 [B', H, N, N] (any strides, B' dividing the batch: sample
     ``b`` reads bias ``b // (B / B')``).  When ``k_in is s`` the four input
-    projections run as one GEMM over stacked weights.
+    projections run as one GEMM over stacked weights; ``s3`` may pass s
+    already in split form (a fused producer wrote it), with ``s`` then only
+    giving the shape.
     """
     if not token_attention_supported(self, s, k_in, bias, mask):
         raise RuntimeError(f"token attention covers fp32 CUDA s [B, N, H*d] with d in {_TOKEN_HEAD_DIMS}, "
@@ -449,7 +451,7 @@ def attend_with_bias(self, s, bias, mask, k_in):
     heads, d, c = self.num_heads, self.head_dim, self.c_s
     if torch.is_autocast_enabled("cuda"):  # the reference's math is fp32 throughout
         with torch.autocast("cuda", enabled=False):
-            return attend_with_bias(self, s, bias, mask, k_in)
+            return attend_with_bias(self, s, bias, mask, k_in, s3=s3)
     if bias.dtype != torch.float32:
         bias = bias.float()
     if mask is not None and (mask.dtype != torch.float32 or mask.stride(-1) != 1):
@@ -460,9 +462,12 @@ def attend_with_bias(self, s, bias, mask, k_in):
     stream = stream_of(s)
     if k_in is s:
         # One GEMM for q | k | v | g; the kernel reads the four column blocks in place.
-        proj = _linear32(self, "_bl_w3_qkvg", s,
-                         [self.proj_q.weight, self.proj_k.weight, self.proj_v.weight, self.proj_g.weight],
-                         [self.proj_q.bias, None, None, None])
+        weights = [self.proj_q.weight, self.proj_k.weight, self.proj_v.weight, self.proj_g.weight]
+        biases = [self.proj_q.bias, None, None, None]
+        if s3 is not None:
+            proj = _linear32_planes(self, "_bl_w3_qkvg", s3, (b, n), weights, biases)
+        else:
+            proj = _linear32(self, "_bl_w3_qkvg", s, weights, biases)
         base = proj.data_ptr()
         kernels.launch_token_attention(base, base + 4 * c, base + 8 * c, base + 12 * c, (n * 4 * c, 4 * c, d), bias,
                                        mask, self.inf, b, heads, n, d, None, stream, out3=out3)

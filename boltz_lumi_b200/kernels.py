@@ -128,29 +128,31 @@ def silu_mul(a, b):
 
 
 MODULATION, GATE, GATED_SWIGLU = _lib.BL_EPI_MODULATION, _lib.BL_EPI_GATE, _lib.BL_EPI_GATED_SWIGLU
+SWIGLU = _lib.BL_EPI_SWIGLU  # silu(a[:, :C]) * a[:, C:] (an fp32 Transition's fc1 | fc2 product)
 
 
 def epilogue(a, b, c, kind):
     """fp32 diffusion epilogues (reference ``kernels/diffusion_hip.cu:80``)."""
     _require_inference(a, b, c)
     _require_cuda(a, b, c)
-    if kind not in (MODULATION, GATE, GATED_SWIGLU):
+    if kind not in (MODULATION, GATE, GATED_SWIGLU, SWIGLU):
         raise RuntimeError(f"unknown epilogue kind {kind}")
     for t in (a, b, c):
         if t is not None and (t.dtype != torch.float32 or not t.is_contiguous()):
             raise RuntimeError("epilogue expects contiguous fp32 tensors")
     shape = list(a.shape)
     cols = shape[-1]
-    if kind == GATED_SWIGLU:
+    if kind in (GATED_SWIGLU, SWIGLU):
         if cols % 2:
-            raise RuntimeError("GATED_SWIGLU needs an even last dimension")
+            raise RuntimeError("SwiGLU epilogues need an even last dimension")
         cols //= 2
         shape[-1] = cols
     out = torch.empty(shape, device=a.device, dtype=torch.float32)
-    if tuple(b.shape) != tuple(shape) or (kind == MODULATION and (c is None or tuple(c.shape) != tuple(shape))):
+    if (kind != SWIGLU and tuple(b.shape) != tuple(shape)) or \
+            (kind == MODULATION and (c is None or tuple(c.shape) != tuple(shape))):
         raise RuntimeError("epilogue operand shapes disagree")
     rows = out.numel() // max(cols, 1)
-    call("bl_diffusion_epilogue", a.data_ptr(), b.data_ptr(), ptr(c), out.data_ptr(), rows, cols, kind, stream_of(a))
+    call("bl_diffusion_epilogue", a.data_ptr(), ptr(b), ptr(c), out.data_ptr(), rows, cols, kind, stream_of(a))
     return out
 
 
@@ -372,9 +374,9 @@ def adaln_modulate_split3(a, scale, shift, eps):
 
 def epilogue_split3(a, b, c, kind):
     """:func:`epilogue` written as split planes [3, rows, C] (C = output width)."""
-    cols = a.shape[-1] // 2 if kind == GATED_SWIGLU else a.shape[-1]
+    cols = a.shape[-1] // 2 if kind in (GATED_SWIGLU, SWIGLU) else a.shape[-1]
     rows = a.numel() // a.shape[-1]
     out = torch.empty(3, rows, cols, device=a.device, dtype=torch.bfloat16)
-    call("bl_diffusion_epilogue_split3", a.data_ptr(), b.data_ptr(), ptr(c), out.data_ptr(), rows, cols, kind,
+    call("bl_diffusion_epilogue_split3", a.data_ptr(), ptr(b), ptr(c), out.data_ptr(), rows, cols, kind,
          torch.cuda.current_stream().cuda_stream)
     return out

@@ -190,10 +190,19 @@ class _FP32Transition(Transition):
 
     def forward(self, x, chunk_size=None):
         _inference_only(self)
+        cols, hidden = x.shape[-1], self.fc1.weight.shape[0]
+        if cols % 128 == 0 and cols <= 1024 and hidden % 8 == 0:
+            # LayerNorm and silu(fc1) * fc2 leave their kernels as the split
+            # operands of fc1 | fc2 and fc3.
+            lead = x.shape[:-1]
+            xn3 = kernels.layer_norm_split3(x, self.norm.weight, self.norm.bias, self.norm.eps)
+            h = forwards._linear32_planes(self, "_bl_w3_fc12", xn3, lead, [self.fc1.weight, self.fc2.weight])
+            h3 = kernels.epilogue_split3(h, None, None, kernels.SWIGLU)
+            return forwards._linear32_planes(self, "_bl_w3_fc3", h3, lead, [self.fc3.weight])
         xn = kernels.layer_norm(x.contiguous(), self.norm.weight, self.norm.bias, self.norm.eps,
                                 out_dtype=torch.float32)
         h = forwards._linear32(self, "_bl_w3_fc12", xn, [self.fc1.weight, self.fc2.weight])
-        a, b = h.split(self.fc1.weight.shape[0], dim=-1)
+        a, b = h.split(hidden, dim=-1)
         return forwards._linear32(self, "_bl_w3_fc3", F.silu(a) * b, [self.fc3.weight])
 
 
@@ -222,8 +231,15 @@ class PairformerLayer(nn.Module):
         forwards.triangle_attention_forward(self.tri_att_start, z, pair_mask, residual=z)
         forwards.triangle_attention_forward(self.tri_att_end, z, pair_mask, residual=z)
         forwards.transition_forward(self.transition_z, z, residual=z)
-        s_normed = kernels.layer_norm(s.contiguous(), self.pre_norm_s.weight, self.pre_norm_s.bias,
-                                      self.pre_norm_s.eps, out_dtype=torch.float32)
-        s = s + self.attention(s_normed, z, mask, s_normed)
+        s = s.contiguous()
+        att = self.attention
+        if s.shape[-1] % 128 == 0 and s.shape[-1] <= 1024:
+            # LN(s) goes straight into the q | k | v | g projection's split operand.
+            s3 = kernels.layer_norm_split3(s, self.pre_norm_s.weight, self.pre_norm_s.bias, self.pre_norm_s.eps)
+            s = s + forwards.attend_with_bias(att, s, att.pair_bias(z), mask, s, s3=s3)
+        else:
+            s_normed = kernels.layer_norm(s, self.pre_norm_s.weight, self.pre_norm_s.bias, self.pre_norm_s.eps,
+                                          out_dtype=torch.float32)
+            s = s + att(s_normed, z, mask, s_normed)
         s = s + self.transition_s(s)
         return s, z

@@ -41,6 +41,10 @@ enum { BL_F32 = 0, BL_BF16 = 1 };
 /* Diffusion epilogue kinds; values match the reference's operation codes
  * (diffusion.py:27 MODULATION, GATE, GATED_SWIGLU = 0, 1, 3). */
 enum { BL_EPI_MODULATION = 0, BL_EPI_GATE = 1, BL_EPI_GATED_SWIGLU = 3 };
+/* silu(a[:, :cols]) * a[:, cols:] (an fp32 Transition's fc1 | fc2 product,
+ * the Pairformer's transition_s); no counterpart code in the reference, which
+ * leaves 2 unused. */
+enum { BL_EPI_SWIGLU = 2 };
 
 /* Message for the last failed call on this thread ("" if none). */
 BL_API const char *bl_last_error(void);
@@ -106,6 +110,7 @@ BL_API int bl_silu_mul(const void *a, const void *b, void *out, int64_t n, void 
  *   MODULATION:   out = sigmoid(b) * a + c
  *   GATE:         out = sigmoid(a) * b
  *   GATED_SWIGLU: a is [rows, 2*cols]; out = silu(a[:, cols:]) * a[:, :cols] * b
+ *   SWIGLU:       a is [rows, 2*cols]; out = silu(a[:, :cols]) * a[:, cols:]   (b unused, may be NULL)
  * Replaces kernels/diffusion_hip.cu:80 `diffusion_epilogue` (diffusion.py:52-68).
  */
 BL_API int bl_diffusion_epilogue(const float *a, const float *b, const float *c, float *out,

@@ -110,3 +110,15 @@ def test_token_attention_split_output():
                                        torch.cuda.current_stream().cuda_stream, out3=out3)
     torch.cuda.synchronize()
     assert torch.equal(out3, kernels.split3(out.view(b * n, h * d)))
+
+
+def test_swiglu_epilogue():
+    """SWIGLU (the fp32 transition's silu(fc1) * fc2 on the joint fc1 | fc2
+    output) against torch, and its split form against split3."""
+    g = torch.Generator().manual_seed(12)
+    h = torch.randn(300, 2 * 1536, generator=g).cuda() * 4
+    with torch.inference_mode():
+        ref = torch.nn.functional.silu(h[:, :1536]) * h[:, 1536:]
+        out = kernels.epilogue(h, None, None, kernels.SWIGLU)
+        assert (out - ref).abs().max().item() <= 1e-6 * ref.abs().max().item()
+        assert torch.equal(kernels.epilogue_split3(h, None, None, kernels.SWIGLU), kernels.split3(out))
