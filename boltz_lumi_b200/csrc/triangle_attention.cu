@@ -191,39 +191,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     tc::tmem_alloc(tmem_slot, kTmemCols);
     tc::tmem_relinquish();
   }
-  __syncthreads();
-  // Start the Q load and fill the ring before the mask pass so the TMA
-  // latency overlaps it.
-  const int prefilled = n_tiles < kStages ? n_tiles : kStages;
-  if (tid == 0) {
-    tc::prefetch_tmap(&map_q);
-    tc::prefetch_tmap(&map_k);
-    tc::prefetch_tmap(&map_v);
-    tc::prefetch_tmap(&map_bias);
-    tc::mbar_arrive_expect_tx(q_full, kBQ * kD * 2);
-    tc::tma_load_3d(smem + kQOff, &map_q, q_full, h * kD, q0, outer);
-    for (int j = 0; j < prefilled; ++j) {
-      uint8_t *stage = smem + kStageOff + j * kStageBytes;
-      tc::mbar_arrive_expect_tx(&st_full[j], kStageBytes);
-      tc::tma_load_3d(stage, &map_k, &st_full[j], h * kD, j * kBK, outer);
-      tc::tma_load_3d(stage + kKBytes, &map_v, &st_full[j], h * kD, j * kBK, outer);
-      tc::tma_load_3d(stage + kKBytes + kVBytes, &map_bias, &st_full[j], j * kBK, q0, h);
-    }
-  }
-  // Mask bias of this outer row, 4 keys per thread (bf16; for mask in {0, 1}
-  // adding it rounds exactly like the fp32 value), and per-tile "any key
-  // masked" flags.
-  for (int k4 = tid * 4; k4 < n_tiles * kBK; k4 += kThreads * 4) {
-    float mb[4];
-    const float *mrow = args.mask + int64_t(outer) * args.ms_o;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int key = k4 + e;
-      mb[e] = key < n ? args.inf * (__ldg(mrow + int64_t(key) * args.ms_k) - 1.f) : 0.f;
-    }
-    *reinterpret_cast<uint2 *>(mask_bias + k4) = make_uint2(pack_bf16x2(mb[0], mb[1]), pack_bf16x2(mb[2], mb[3]));
-    if (mb[0] != 0.f || mb[1] != 0.f || mb[2] != 0.f || mb[3] != 0.f) atomicOr(&tile_masked[k4 / kBK], 1);
-  }
+  // The ones block is read by the MMA (async proxy).
   tc::fence_proxy_async_smem();
   tc::tc_fence_before();
   __syncthreads();
@@ -233,9 +201,15 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      for (int j = prefilled; j < n_tiles; ++j) {
+      tc::prefetch_tmap(&map_q);
+      tc::prefetch_tmap(&map_k);
+      tc::prefetch_tmap(&map_v);
+      tc::prefetch_tmap(&map_bias);
+      tc::mbar_arrive_expect_tx(q_full, kBQ * kD * 2);
+      tc::tma_load_3d(smem + kQOff, &map_q, q_full, h * kD, q0, outer);
+      for (int j = 0; j < n_tiles; ++j) {
         const int s = j % kStages;
-        if (!tc::mbar_wait(&st_empty[s], ((j / kStages) & 1) ^ 1u, args.status, 0x201)) break;
+        if (j >= kStages && !tc::mbar_wait(&st_empty[s], ((j / kStages) & 1) ^ 1u, args.status, 0x201)) break;
         uint8_t *stage = smem + kStageOff + s * kStageBytes;
         tc::mbar_arrive_expect_tx(&st_full[s], kStageBytes);
         tc::tma_load_3d(stage, &map_k, &st_full[s], h * kD, j * kBK, outer);
@@ -291,6 +265,27 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
     const uint32_t o_base = lane_base + kOCol + half * kOStride;
+    // The gate rows this thread's epilogue applies go to L2 now.
+    if (q0 + row < n) {
+      const int64_t pair = int64_t(outer) * args.so + int64_t(q0 + row) * args.si;
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(args.g + pair * args.ld + h * kD + half * 16));
+    }
+    // Mask bias of this outer row, 4 keys per thread (bf16; for mask in {0,
+    // 1} adding it rounds exactly like the fp32 value), and per-tile "any key
+    // masked" flags.  Only the softmax warps read them, so the TMA and MMA
+    // warps start without waiting for this pass.
+    const float *mrow = args.mask + int64_t(outer) * args.ms_o;
+    for (int k4 = (tid - 64) * 4; k4 < n_tiles * kBK; k4 += kSoftmaxWarps * 32 * 4) {
+      float mb[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = k4 + e;
+        mb[e] = key < n ? args.inf * (__ldg(mrow + int64_t(key) * args.ms_k) - 1.f) : 0.f;
+      }
+      *reinterpret_cast<uint2 *>(mask_bias + k4) = make_uint2(pack_bf16x2(mb[0], mb[1]), pack_bf16x2(mb[2], mb[3]));
+      if (mb[0] != 0.f || mb[1] != 0.f || mb[2] != 0.f || mb[3] != 0.f) atomicOr(&tile_masked[k4 / kBK], 1);
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxWarps * 32) : "memory");
     float m_ref = -INFINITY;  // reference maximum of this half-row's exponentials
     bool ok = true;
     for (int j = 0; j < n_tiles && ok; ++j) {
@@ -396,6 +391,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     // Epilogue: merge the two key halves, O / l, bf16, gate, store.  This
     // thread writes output channels 16 half .. 16 half + 15 of its row.
     row_max[half * kBQ + row] = m_ref;
+    // The gate (bf16(sigmoid(g)) from the projection) is loaded before the
+    // barrier and the wait for the last P.V, which cover its latency.
+    const int qi = q0 + row;
+    const int64_t pair = int64_t(outer) * args.so + int64_t(qi) * args.si;
+    uint4 gate[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
+    if (qi < n) {
+      const uint4 *g4 = reinterpret_cast<const uint4 *>(args.g + pair * args.ld + h * kD + half * 16);
+      gate[0] = g4[0];
+      gate[1] = g4[1];
+    }
     asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxWarps * 32) : "memory");
     const float m_other = row_max[(half ^ 1) * kBQ + row];
     if (ok && warp_wait(o_full, 0, args.status, 0x20A)) {
@@ -403,21 +408,18 @@ __global__ void __launch_bounds__(kThreads, 2)
       const float m0 = half == 0 ? m_ref : m_other, m1 = half == 0 ? m_other : m_ref;
       const float m = fmaxf(m0, m1);
       const float a0 = fast_exp2((m0 - m) * kLog2e), a1 = fast_exp2((m1 - m) * kLog2e);
-      uint32_t o0[16], o1[16], l0[16], l1[16];
+      uint32_t o0[16], o1[16], l0, l1;  // row sums: column 32 of each half's accumulator
       tc::tmem_ld_32x32b_x16(lane_base + kOCol + half * 16, o0);
       tc::tmem_ld_32x32b_x16(lane_base + kOCol + kOStride + half * 16, o1);
-      tc::tmem_ld_32x32b_x16(lane_base + kOCol + 32, l0);
-      tc::tmem_ld_32x32b_x16(lane_base + kOCol + kOStride + 32, l1);
+      tc::tmem_ld_32x32b_x1(lane_base + kOCol + 32, l0);
+      tc::tmem_ld_32x32b_x1(lane_base + kOCol + kOStride + 32, l1);
       tc::tmem_ld_wait();
-      const int qi = q0 + row;
       if (qi < n) {
-        const float inv = fast_rcp(__uint_as_float(l0[0]) * a0 + __uint_as_float(l1[0]) * a1);
-        const int64_t pair = int64_t(outer) * args.so + int64_t(qi) * args.si;
-        const uint4 *g4 = reinterpret_cast<const uint4 *>(args.g + pair * args.ld + h * kD + half * 16);
+        const float inv = fast_rcp(__uint_as_float(l0) * a0 + __uint_as_float(l1) * a1);
         uint4 *o4 = reinterpret_cast<uint4 *>(args.out + pair * args.out_ld + h * kD + half * 16);
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          const uint4 gv = g4[c];
+          const uint4 gv = gate[c];
           const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
           uint32_t w[4];
 #pragma unroll
