@@ -44,7 +44,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 def parse_args():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--n", type=int, default=N_TOKENS, help="tokens (default 512, the metric's config)")
@@ -234,21 +234,24 @@ def algorithmic_work(name, a):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons, sampled every 20 ms from before
+    the warm-up; ``stop(window)`` keeps the samples taken inside the timed
+    region (host monotonic times)."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device):
-        self.samples = []
+    def __init__(self, device, interval_ms=20):
+        self.samples = []  # (host monotonic seconds, fields)
         self.proc = None
+        self.first = threading.Event()
         try:
             uuid = str(torch.cuda.get_device_properties(device).uuid)
             ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", ident, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", str(interval_ms)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except (OSError, RuntimeError):
@@ -258,20 +261,28 @@ class ClockSampler:
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) == 7:
-                self.samples.append(parts)
+                self.samples.append((time.monotonic(), parts))
+                self.first.set()
 
-    def stop(self):
+    def wait_ready(self, timeout=10.0):
+        """Block until nvidia-smi has produced its first sample (it takes a moment to start)."""
+        if self.proc is not None:
+            self.first.wait(timeout)
+
+    def stop(self, window):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.25)
+        time.sleep(0.05)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
+        t0, t1 = window
+        inside = [parts for t, parts in self.samples if t0 <= t <= t1]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         sm, sm_max, reasons = [], [], set()
-        for parts in self.samples:
+        for parts in inside:
             try:
                 sm.append(float(parts[0]))
                 sm_max.append(float(parts[1]))
@@ -281,7 +292,8 @@ class ClockSampler:
                 if flag.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(sm_max) if sm_max else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "interval_ms": 20,
+                "timed_region_s": round(t1 - t0, 4)}
 
 
 def run_b200(args):
@@ -314,6 +326,8 @@ def run_b200(args):
         if dist is not None:
             dist.barrier()
 
+    clocks = ClockSampler(device)
+    clocks.wait_ready()
     with torch.inference_mode():
         for _ in range(max(args.warmup, 3)):
             step()
@@ -337,19 +351,20 @@ def run_b200(args):
 
         # Timed region: K chained blocks; the dominant kernel is event-timed in place.
         observer = _lib.CallObserver(timed=(top["name"],))
-        clocks = ClockSampler(device)
         barrier()
         torch.cuda.synchronize()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         _lib.set_observer(observer)
+        t0 = time.monotonic()
         start.record()
         for _ in range(args.steps):
             step()
         end.record()
         torch.cuda.synchronize()
+        t1 = time.monotonic()
         _lib.set_observer(None)
         barrier()
-        clock_info = clocks.stop()
+        clock_info = clocks.stop((t0, t1))
         elapsed_ms = start.elapsed_time(end)
         launches_timed = observer.calls
         top_times = [e0.elapsed_time(e1) for name, a, e0, e1 in observer.records
@@ -365,19 +380,22 @@ def run_b200(args):
         s_back = torch.empty_like(s_host).pin_memory()
         h2d = z_host.numel() * 4 + s_host.numel() * 4 + mask_h.numel() * 4 + pmask_h.numel() * 4
         d2h = z_back.numel() * 4 + s_back.numel() * 4
-        # Three streams, two device buffer sets: the host->device copy of step
-        # k + 1 and the device->host copy of step k - 1 run while step k computes
-        # (PCIe is full duplex); every step still moves all of its inputs in and
-        # all of z and s out.
+        # Three streams, three device buffer sets: the host->device copy of
+        # step k + 1 and the device->host copy of step k - 1 run while step k
+        # computes (PCIe is full duplex).  A buffer set is held from its input
+        # copy to the end of its output copy, so with three sets the two copy
+        # directions run back to back.  Every step still moves all of its
+        # inputs in and all of z and s out.
+        nbuf = 3
         mask_host, pmask_host = mask_h.pin_memory(), pmask_h.pin_memory()
         bufs = [{"z": torch.empty_like(z_h, device=device), "s": torch.empty_like(s_h, device=device),
                  "m": torch.empty_like(mask_h, device=device), "p": torch.empty_like(pmask_h, device=device)}
-                for _ in range(2)]
+                for _ in range(nbuf)]
         s_in, s_comp, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device), torch.cuda.Stream(device)
-        ev_in = [torch.cuda.Event() for _ in range(2)]
-        ev_comp = [torch.cuda.Event() for _ in range(2)]
-        ev_out = [torch.cuda.Event() for _ in range(2)]
-        outputs = [None, None]
+        ev_in = [torch.cuda.Event() for _ in range(nbuf)]
+        ev_comp = [torch.cuda.Event() for _ in range(nbuf)]
+        ev_out = [torch.cuda.Event() for _ in range(nbuf)]
+        outputs = [None] * nbuf
         barrier()
         torch.cuda.synchronize()
         e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -387,30 +405,30 @@ def run_b200(args):
         steps_e2e = args.e2e_steps
         for k in range(steps_e2e + 2):
             if k < steps_e2e:  # inputs of step k
-                b = bufs[k % 2]
-                if k >= 2:
-                    s_in.wait_event(ev_out[k % 2])  # step k - 2 has left this buffer set
+                b = bufs[k % nbuf]
+                if k >= nbuf:
+                    s_in.wait_event(ev_out[k % nbuf])  # step k - nbuf has left this buffer set
                 with torch.cuda.stream(s_in):
                     b["z"].copy_(z_host, non_blocking=True)
                     b["s"].copy_(s_host, non_blocking=True)
                     b["m"].copy_(mask_host, non_blocking=True)
                     b["p"].copy_(pmask_host, non_blocking=True)
-                ev_in[k % 2].record(s_in)
+                ev_in[k % nbuf].record(s_in)
             j = k - 1
             if 0 <= j < steps_e2e:  # compute step j
-                b = bufs[j % 2]
-                s_comp.wait_event(ev_in[j % 2])
+                b = bufs[j % nbuf]
+                s_comp.wait_event(ev_in[j % nbuf])
                 with torch.cuda.stream(s_comp):
-                    outputs[j % 2] = block(b["s"], b["z"], b["m"], b["p"])
-                ev_comp[j % 2].record(s_comp)
+                    outputs[j % nbuf] = block(b["s"], b["z"], b["m"], b["p"])
+                ev_comp[j % nbuf].record(s_comp)
             j = k - 2
             if 0 <= j < steps_e2e:  # results of step j
-                so, zo = outputs[j % 2]
-                s_out.wait_event(ev_comp[j % 2])
+                so, zo = outputs[j % nbuf]
+                s_out.wait_event(ev_comp[j % nbuf])
                 with torch.cuda.stream(s_out):
                     z_back.copy_(zo, non_blocking=True)
                     s_back.copy_(so, non_blocking=True)
-                ev_out[j % 2].record(s_out)
+                ev_out[j % nbuf].record(s_out)
         e_end.record(s_out)
         torch.cuda.synchronize()
         barrier()
@@ -462,7 +480,7 @@ def run_b200(args):
         "config": bench_config(n, world),
         "e2e": {"value": round(e2e_value, 4), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "steps": args.e2e_steps,
-                "pipeline": "pinned host buffers; H2D of step k+1 and D2H of step k-1 overlap step k (3 streams)"},
+                "pipeline": "pinned host buffers; H2D of step k+1 and D2H of step k-1 overlap step k (3 streams, 3 device buffer sets)"},
         "gpu_launches": launches_timed,
         "launches_per_step": launches_per_step,
         "roofline": roofline,
@@ -525,24 +543,27 @@ def run_sharded(args):
         if dist is not None:
             dist.barrier()
 
+    clocks = ClockSampler(device)
+    clocks.wait_ready()
     with torch.inference_mode():
         for _ in range(max(args.warmup, 3)):
             s, z_rows = sharded(s, z_rows, mask, pmask)
         torch.cuda.synchronize()
         observer = _lib.CallObserver(timed=())
         _lib.set_observer(observer)
-        clocks = ClockSampler(device)
         barrier()
         torch.cuda.synchronize()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.monotonic()
         start.record()
         for _ in range(args.steps):
             s, z_rows = sharded(s, z_rows, mask, pmask)
         end.record()
         torch.cuda.synchronize()
+        t1 = time.monotonic()
         _lib.set_observer(None)
         barrier()
-        clock_info = clocks.stop()
+        clock_info = clocks.stop((t0, t1))
         ms = max_over_ranks(start.elapsed_time(end), dist, device) / args.steps
         launches = observer.calls
         # End to end: this rank's rows and s in from pinned memory, back out, every step.

@@ -155,19 +155,17 @@ __device__ __forceinline__ void stage_row(uint8_t *buf, int lane, const uint32_t
   }
 }
 
-// One step of a butterfly reduce-scatter over N values per lane: lanes with
-// bit OFF set keep the upper half of the values, the others the lower half,
-// each adding the partner's copy.  Steps OFF = 16, 8, 4, 2 reduce 16 values
-// per lane to one partial sum per lane pair (index = lane / 2, lanes 2i and
-// 2i + 1 holding the two halves of the final sum).
-template <int OFF, int N> __device__ __forceinline__ void reduce_scatter_step(float (&v)[16], int lane) {
-  const bool upper = (lane & OFF) != 0;
-#pragma unroll
-  for (int i = 0; i < N / 2; ++i) {
-    const float send = upper ? v[i] : v[i + N / 2];
-    const float keep = upper ? v[i + N / 2] : v[i];
-    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, OFF);
-  }
+// Warp-level bf16 MMA (m16n8k16, fp32 accumulate) and its A-fragment load.
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&a)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+               "{%0, %1, %2, %3};"
+               : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+               : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 template <int KIND>
@@ -420,11 +418,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       lnw[e] = args.ln_w ? args.ln_w[lane * 4 + e] : 1.f;
       lnb[e] = args.ln_b ? args.ln_b[lane * 4 + e] : 0.f;
     }
-    uint2 wh[4];  // bf16 head weights of this lane's 4 channels, packed in pairs
-    if constexpr (KIND == PROJ_ATTENTION) {
-#pragma unroll
-      for (int hh = 0; hh < 4; ++hh) wh[hh] = *reinterpret_cast<const uint2 *>(args.w_heads + hh * kC + lane * 4);
-    }
     // This lane's 4 channels inside the swizzled A tile: K-block lane / 16,
     // 16-byte chunk (lane % 16) / 2, byte (lane % 2) * 8 within it.
     const uint32_t a_lane_off = (lane >> 4) * kKBlockBytes + (lane & 1) * 8;
@@ -471,7 +464,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
           for (int rr = 0; rr < 4; ++rr) var[rr] += __shfl_xor_sync(0xffffffffu, var[rr], o);
-        float heads[16];
 #pragma unroll
         for (int rr = 0; rr < 4; ++rr) {
           const int r = 4 * g + rr;
@@ -486,27 +478,44 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<uint2 *>(abuf + a_lane_off + tr * 128 + ((a_chunk ^ (tr & 7)) << 4)) = y;
           if constexpr (KIND == PROJ_TRIMUL) {
             if (live) *reinterpret_cast<uint2 *>(args.xn + (t.row0 + tr) * kC + lane * 4) = y;
-          } else {
-            const float y0 = bf16_lo(y.x), y1 = bf16_hi(y.x), y2 = bf16_lo(y.y), y3 = bf16_hi(y.y);
-#pragma unroll
-            for (int hh = 0; hh < 4; ++hh)
-              heads[rr * 4 + hh] = (y0 * bf16_lo(wh[hh].x) + y1 * bf16_hi(wh[hh].x)) +
-                                   (y2 * bf16_lo(wh[hh].y) + y3 * bf16_hi(wh[hh].y));
           }
         }
-        if constexpr (KIND == PROJ_ATTENTION) {
-          reduce_scatter_step<16, 16>(heads, lane);
-          reduce_scatter_step<8, 8>(heads, lane);
-          reduce_scatter_step<4, 4>(heads, lane);
-          reduce_scatter_step<2, 2>(heads, lane);
-          const float d = heads[0] + __shfl_xor_sync(0xffffffffu, heads[0], 1);
-          // Lane pair (2i, 2i + 1) holds head i % 4 of row 4 g + i / 4.
-          const int tr = rbase + 4 * g + (lane >> 3);
-          if ((lane & 1) == 0 && tr < t.valid) {
+      }
+    };
+
+    // Attention: the four triangle-bias heads of this warp's 16 rows,
+    // tri_bias[h][row] = bf16(x_hat[row] . w_heads[h]), read back from the A
+    // tile the warp has just written (bf16 x_hat, fp32 accumulation) with
+    // eight warp-level m16n8k16 MMAs (heads padded to 8 columns).  TMEM's 512
+    // columns hold the q | k | v | g accumulators, so the heads stay on the
+    // LayerNorm warp.
+    auto bias_heads = [&](const TileRows &t, uint8_t *abuf) {
+      const uint32_t a_base = tc::smem_u32(abuf);
+      const int mi = lane >> 3;                               // ldmatrix: 8x8 matrix this lane addresses
+      const int arow = row_lo + (mi & 1) * 8 + (lane & 7);    // its row
+      const int g = lane >> 2, tq = lane & 3;                 // mma fragment: row group, column pair
+      const uint32_t *wrow = reinterpret_cast<const uint32_t *>(args.w_heads + (g & 3) * kC);
+      float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int ks = 0; ks < kC / 16; ++ks) {
+        const int k = ks * 16 + (mi >> 1) * 8;
+        uint32_t a[4];
+        ldsm_x4(a_base + (k >> 6) * kKBlockBytes + arow * 128 + ((((k & 63) >> 3) ^ (arow & 7)) << 4), a);
+        const uint32_t b0 = g < 4 ? __ldg(wrow + ks * 8 + tq) : 0u;
+        const uint32_t b1 = g < 4 ? __ldg(wrow + ks * 8 + 4 + tq) : 0u;
+        mma_16816(c, a, b0, b1);
+      }
+      // c = D[g][2 tq], D[g][2 tq + 1], D[g + 8][2 tq], D[g + 8][2 tq + 1]: heads 2 tq, 2 tq + 1.
+      if (tq < 2) {
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+          const int tr = row_lo + g + 8 * hr;
+          if (tr < t.valid) {
             const int row = int(t.row0) + tr;  // n * n < 2^31
             const int q = row / args.n, k = row - q * args.n;
             const int64_t at = args.transpose ? int64_t(k) * args.bias_ld + q : int64_t(q) * args.bias_ld + k;
-            args.bias_planes[((lane >> 1) & 3) * args.bias_hs + at] = __float2bfloat16_rn(d);
+            args.bias_planes[(2 * tq) * args.bias_hs + at] = __float2bfloat16_rn(c[2 * hr]);
+            args.bias_planes[(2 * tq + 1) * args.bias_hs + at] = __float2bfloat16_rn(c[2 * hr + 1]);
           }
         }
       }
@@ -544,6 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&a_full[ab]);
+      if constexpr (KIND == PROJ_ATTENTION) bias_heads(t, abuf);
       t = next;
     }
   }
