@@ -69,7 +69,6 @@ constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kOCol = 128;
 constexpr uint32_t kOStride = 48;
 
-constexpr uint32_t kNegInf = 0xFF80FF80u;
 constexpr uint32_t kNegPad = 0xF14AF14Au;  // bf16x2 (-1e30, -1e30)
 
 struct TcArgs {
@@ -294,10 +293,14 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc::tc_fence_after();
       uint32_t sv[32];
       tc::tmem_ld_32x32b_x32(lane_base + b * kBK + half * 32, sv);
-      if (!(ok = warp_wait(&st_full[s], (j / kStages) & 1, args.status, 0x207))) break;
-      tc::tmem_ld_wait();
+      if (!(ok = warp_wait(&st_full[s], (j / kStages) & 1, args.status, 0x207))) {
+        tc::tmem_ld_wait();
+        break;
+      }
 
       // Ordered rounding: t = bf16(bf16(bf16(s) + mask) + bias), packed per key pair.
+      // The bias chunks and the tile's mask flag are read from shared memory
+      // while the S load from TMEM is still in flight.
       const int k0 = j * kBK + half * 32;
       const uint32_t bias_row = smem_base + kStageOff + s * kStageBytes + kKBytes + kVBytes + row * 128;
       // 16-byte bias chunk c = keys 8c .. 8c + 7 of this half (128-byte swizzled row).
@@ -307,10 +310,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint4 bv = lds128(bias_row + (((half * 4 + c) ^ (row & 7)) << 4));
         bw[4 * c] = bv.x, bw[4 * c + 1] = bv.y, bw[4 * c + 2] = bv.z, bw[4 * c + 3] = bv.w;
       }
+      const bool tile_unmasked = lds32(smem_base + kFlagOff + 4 * j) == 0;
+      tc::tmem_ld_wait_regs(sv);
       // The mask term is uniform per key tile: two straight-line versions
       // (a per-pair branch would split the unrolled block).
       uint32_t t[16];
-      if (lds32(smem_base + kFlagOff + 4 * j) == 0) {
+      if (tile_unmasked) {
 #pragma unroll
         for (int pr = 0; pr < 16; ++pr)
           t[pr] = add_bf16x2(cvt_bf16x2(__uint_as_float(sv[2 * pr]), __uint_as_float(sv[2 * pr + 1])), bw[pr]);
