@@ -14,18 +14,21 @@
 //     a|b[c][i][k] = bf16(bf16(p_c * bf16(sigmoid(g_c))) * mask[i, k])   p = p_in(x_hat), g = g_in(x_hat)
 //     x_hat rows stored in bf16 for the output gate g_out(x_hat)
 //
-// CTA (one per SM, persistent over 128-row tiles), 14 warps:
+// CTA (one per SM, persistent over 128-row tiles), 18 warps (96 registers
+// each: some SM sub-partition holds five of them):
 //   warp 0       TMA: the [512][128] bf16 weight, once per CTA (resident, 128 KB)
 //   warp 1       TMEM allocation (512 columns) + tcgen05.mma issue: four chunks
 //                of 128 output columns, chunk j into TMEM columns [128 j, 128 j + 128)
-//   warps 2..5   epilogue: tcgen05.ld a chunk (TMEM lane quarter = warp % 4),
-//                release its columns, apply the op's epilogue, stage the tile
-//                in shared memory and TMA-store it.  Attention computes
+//   warps 2..9   epilogue, two warps per TMEM lane quarter (warp % 4), each
+//                taking 64 of a chunk's 128 columns: tcgen05.ld, release the
+//                columns, apply the op's epilogue, stage a 32 x 64 block in
+//                shared memory and TMA-store it.  Attention computes
 //                D = X W^T (lane = pair row, the natural [row][512] output);
 //                the triangle multiplication computes D = W X^T (lane =
 //                channel, columns = pairs), so each thread's values already
 //                run along its channel plane and p / g of a channel share a lane
-//   warps 6..13  LayerNorm: each warp normalises 16 rows of the tile in fp32
+//   warps 10..17 LayerNorm: each warp normalises 16 rows of the tile in fp32
+//                (four batches of 4 rows, the next batch's loads in flight)
 //                and writes the bf16 result straight into the 128-byte-swizzled
 //                K-major A tile the MMA reads (double-buffered), plus the
 //                per-row side outputs (bias heads / x_hat rows); each warp
@@ -45,18 +48,20 @@ constexpr int kRows = 128;      // rows per tile (= TMEM lanes)
 constexpr int kChunks = 4;      // 128-column output chunks
 constexpr int kLnWarps = 8;
 constexpr int kLnRowsPerWarp = kRows / kLnWarps;  // 16, in two batches of 8
-constexpr int kFirstLnWarp = 6;
-constexpr int kThreads = (kFirstLnWarp + kLnWarps) * 32;
+constexpr int kFirstEpiWarp = 2;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quarter: columns 0-63 / 64-127 of every chunk
+constexpr int kFirstLnWarp = kFirstEpiWarp + kEpiWarps;
+constexpr int kThreads = (kFirstLnWarp + kLnWarps) * 32;  // 18 warps: <= 112 registers per thread
 
 constexpr int kWBytes = kOut * kC * 2;        // 128 KB: chunk j = [128 rows][128 K] as two SW128 K-blocks
 constexpr int kWChunkBytes = kRows * kC * 2;  // 32 KB
 constexpr int kKBlockBytes = kRows * 64 * 2;  // 16 KB: [128 rows][64 K] bf16, 128-byte swizzle
 constexpr int kABytes = kRows * kC * 2;       // 32 KB
-constexpr int kStagePerWarp = 8192;
+constexpr int kStagePerWarp = 4096;  // one staged 32 x 64 block per epilogue warp
 constexpr int kWOff = 0;
 constexpr int kAOff = kWOff + kWBytes;
 constexpr int kStageOff = kAOff + 2 * kABytes;
-constexpr int kBiasOff = kStageOff + 4 * kStagePerWarp;  // fp32 [512] projection bias
+constexpr int kBiasOff = kStageOff + kEpiWarps * kStagePerWarp;  // fp32 [512] projection bias
 constexpr int kBarOff = kBiasOff + kOut * 4;
 // The dynamic shared window starts 1024-byte aligned (checked at run time:
 // the kernel reports an error instead of running misaligned), so no slack.
@@ -169,7 +174,6 @@ __device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4],
 }
 
 template <int KIND>
-// 14 warps put four on one SM sub-partition (16K registers): <= 128 registers.
 __global__ void __launch_bounds__(kThreads, 1)
     pair_projection_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_out,
                            const ProjArgs args) {
@@ -183,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *a_full = bars + 1;   // [2] A tile written (8 LN warps arrive)
   uint64_t *a_empty = bars + 3;  // [2] MMAs reading A done
   uint64_t *c_full = bars + 5;   // [4] chunk accumulated in TMEM
-  uint64_t *c_empty = bars + 9;  // [4] chunk read out of TMEM (4 epilogue warps arrive)
+  uint64_t *c_empty = bars + 9;  // [4] chunk read out of TMEM (8 epilogue warps arrive)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 13);
   float *bias_s = reinterpret_cast<float *>(smem + kBiasOff);
 
@@ -196,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int j = 0; j < kChunks; ++j) {
       tc::mbar_init(&c_full[j], 1);
-      tc::mbar_init(&c_empty[j], 4);
+      tc::mbar_init(&c_empty[j], kEpiWarps);
     }
     tc::fence_mbar_init();
     tc::prefetch_tmap(&map_w);
@@ -267,9 +271,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < kFirstLnWarp) {
     // ---------------------------------------------------------------- epilogue
+    // TMEM lane quarter = warp % 4; `part` = which 64 of a chunk's 128
+    // columns this warp reads.  Each warp stages one 32 x 64 block at a time
+    // and waits for its previous TMA store to have read it before the next.
     const int quarter = warp & 3;
-    uint8_t *stage = smem + kStageOff + quarter * kStagePerWarp;
-    int it = 0, count = 0;
+    const int part = (warp - kFirstEpiWarp) >> 2;
+    uint8_t *stage = smem + kStageOff + (warp - kFirstEpiWarp) * kStagePerWarp;
+    int it = 0;
     bool ok = true;
     if constexpr (KIND == PROJ_ATTENTION) {
       for (int tile = blockIdx.x; ok && tile < args.tiles; tile += gridDim.x, ++it) {
@@ -281,23 +289,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc::tc_fence_after();
-          const uint32_t taddr = tc::tmem_addr(tmem_base, quarter * 32, j * 128);
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
+          const uint32_t taddr = tc::tmem_addr(tmem_base, quarter * 32, j * 128 + part * 64);
+          {
             uint32_t r0[32], r1[32];
-            tc::tmem_ld_32x32b_x32(taddr + h * 64, r0);
-            tc::tmem_ld_32x32b_x32(taddr + h * 64 + 32, r1);
+            tc::tmem_ld_32x32b_x32(taddr, r0);
+            tc::tmem_ld_32x32b_x32(taddr + 32, r1);
             tc::tmem_ld_wait_regs(r0, r1);
-            if (h == 1) {
-              tc::tc_fence_before();
-              __syncwarp();
-              if (lane == 0) tc::mbar_arrive(&c_empty[j]);
-            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&c_empty[j]);
             if (!warp_live) continue;
-            const int c0 = j * 128 + h * 64;
+            const int c0 = j * 128 + part * 64;
             const float4 *bq = reinterpret_cast<const float4 *>(bias_s + c0);  // same address in every lane
-            uint8_t *buf = stage + (count & 1) * 4096;
-            if (lane == 0) tc::bulk_wait_read<1>();
+            uint8_t *buf = stage;
+            if (lane == 0) tc::bulk_wait_read<0>();
             __syncwarp();
             // 16-byte chunk e of the staged row = columns 8 e .. 8 e + 7.  q
             // (chunk 0) leaves scaled, bf16(bf16(q) * q_scale); g (chunk 3)
@@ -315,29 +320,29 @@ __global__ void __launch_bounds__(kThreads, 1)
               tc::tma_store_2d(&map_out, buf, c0, int(t.row0) + quarter * 32);
               tc::bulk_commit();
             }
-            ++count;
           }
         }
       }
     } else {
       // Thread = channel 32 quarter + lane of plane group G (a: G = 0, b: G = 1);
-      // TMEM columns = the tile's 128 pairs.  p of group G sits in chunk 2 G,
-      // g in chunk 2 G + 1.  Per pair: p, g rounded to bf16 (the autocast
-      // linears' outputs), s = bf16(sigmoid(g)), bf16(p * s) (exact as
-      // mul.rn.bf16x2), then bf16(. * mask).  The staged row of 64 pairs of
-      // one channel goes out as one TMA box row.
-      float *msk = bias_s + quarter * kRows;  // this warp's copy of the tile's mask
+      // TMEM columns = the tile's 128 pairs, of which this warp takes 64
+      // (`part`).  p of group G sits in chunk 2 G, g in chunk 2 G + 1.  Per
+      // pair: p, g rounded to bf16 (the autocast linears' outputs), s =
+      // bf16(sigmoid(g)), bf16(p * s) (exact as mul.rn.bf16x2), then
+      // bf16(. * mask).  The staged row of 64 pairs of one channel goes out
+      // as one TMA box row.
+      float *msk = bias_s + quarter * kRows + part * 64;  // this warp's copy of its 64 pairs' mask
       for (int tile = blockIdx.x; ok && tile < args.tiles; tile += gridDim.x, ++it) {
         const TileRows t = tile_rows<KIND>(args, tile);
-        float mv[4];
+        float mv[2];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int k = lane * 4 + e;
+        for (int e = 0; e < 2; ++e) {
+          const int k = part * 64 + lane * 2 + e;
           mv[e] = k < t.valid ? args.mask[t.row0 + k] : 0.f;
         }
         __syncwarp();
-        *reinterpret_cast<float4 *>(msk + lane * 4) = make_float4(mv[0], mv[1], mv[2], mv[3]);
-        const bool unit = __all_sync(0xffffffffu, mv[0] == 1.f && mv[1] == 1.f && mv[2] == 1.f && mv[3] == 1.f);
+        *reinterpret_cast<float2 *>(msk + lane * 2) = make_float2(mv[0], mv[1]);
+        const bool unit = __all_sync(0xffffffffu, mv[0] == 1.f && mv[1] == 1.f);
         __syncwarp();
         for (int G = 0; G < 2; ++G) {
           if (!warp_wait(&c_full[2 * G], it & 1, args.status, 0x304) ||
@@ -346,19 +351,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc::tc_fence_after();
-          const uint32_t tp = tc::tmem_addr(tmem_base, quarter * 32, 256 * G), tg = tp + 128;
+          const uint32_t tp = tc::tmem_addr(tmem_base, quarter * 32, 256 * G + 64 * part), tg = tp + 128;
           uint32_t pa[16], ga[16], pb[16], gb[16];
           tc::tmem_ld_32x32b_x16(tp, pa);
           tc::tmem_ld_32x32b_x16(tg, ga);
           tc::tmem_ld_wait_regs(pa, ga);
           uint8_t *buf = stage;
+          if (lane == 0) tc::bulk_wait_read<0>();  // the previous store has read the staging block
+          __syncwarp();
 #pragma unroll
-          for (int step = 0; step < 8; ++step) {  // 16 pairs per step
+          for (int step = 0; step < 4; ++step) {  // 16 pairs per step
             uint32_t(&pc)[16] = (step & 1) ? pb : pa;
             uint32_t(&gc)[16] = (step & 1) ? gb : ga;
             uint32_t(&pn)[16] = (step & 1) ? pa : pb;
             uint32_t(&gn)[16] = (step & 1) ? ga : gb;
-            if (step < 7) {  // next 16 pairs in flight while these are processed
+            if (step < 3) {  // next 16 pairs in flight while these are processed
               tc::tmem_ld_32x32b_x16(tp + 16 * (step + 1), pn);
               tc::tmem_ld_32x32b_x16(tg + 16 * (step + 1), gn);
             } else {
@@ -369,11 +376,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc::mbar_arrive(&c_empty[2 * G + 1]);
               }
             }
-            if ((step & 3) == 0) {
-              buf = stage + (count & 1) * 4096;
-              if (lane == 0) tc::bulk_wait_read<1>();
-              __syncwarp();
-            }
             uint32_t o[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
@@ -382,28 +384,24 @@ __global__ void __launch_bounds__(kThreads, 1)
               o[e] = mul_bf16x2(p2, cvt_bf16x2(sigmoid_mufu(bf16_lo(g2)), sigmoid_mufu(bf16_hi(g2))));
             }
             if (!unit) {
-              const float2 *m2 = reinterpret_cast<const float2 *>(msk + 64 * (step >> 2) + 16 * (step & 3));
+              const float2 *m2 = reinterpret_cast<const float2 *>(msk + 16 * step);
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
                 const float2 mm = m2[e];
                 o[e] = cvt_bf16x2(bf16_lo(o[e]) * mm.x, bf16_hi(o[e]) * mm.y);
               }
             }
-            const int c16 = 2 * (step & 3);  // 16-byte chunks of the 128-byte staged row
+            const int c16 = 2 * step;  // 16-byte chunks of the 128-byte staged row
             *reinterpret_cast<uint4 *>(buf + lane * 128 + ((c16 ^ (lane & 7)) * 16)) = make_uint4(o[0], o[1], o[2], o[3]);
             *reinterpret_cast<uint4 *>(buf + lane * 128 + (((c16 + 1) ^ (lane & 7)) * 16)) =
                 make_uint4(o[4], o[5], o[6], o[7]);
-            if ((step & 3) == 3) {
-              const int blk = step >> 2;
-              tc::fence_proxy_async_smem();
-              __syncwarp();
-              if (lane == 0 && 64 * blk < t.valid) {
-                tc::tma_store_3d(&map_out, buf, t.k0 + 64 * blk, t.i, 128 * G + 32 * quarter);
-                tc::bulk_commit();
-              }
-              ++count;
-            }
-            if (step < 7) tc::tmem_ld_wait_regs(pn, gn);
+            if (step < 3) tc::tmem_ld_wait_regs(pn, gn);
+          }
+          tc::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && 64 * part < t.valid) {
+            tc::tma_store_3d(&map_out, buf, t.k0 + 64 * part, t.i, 128 * G + 32 * quarter);
+            tc::bulk_commit();
           }
         }
       }
@@ -425,20 +423,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row_lo = lw * kLnRowsPerWarp;
 
     // Rows rbase .. rbase + 7 of tile t (zeros past the valid rows).
-    auto load_rows = [&](const TileRows &t, int rbase, float4 (&v)[8]) {
+    auto load_rows = [&](const TileRows &t, int rbase, float4 (&v)[4]) {
 #pragma unroll
-      for (int r = 0; r < 8; ++r)
+      for (int r = 0; r < 4; ++r)
         v[r] = rbase + r < t.valid
                    ? __ldg(reinterpret_cast<const float4 *>(args.x + (t.row0 + rbase + r) * kC) + lane)
                    : make_float4(0.f, 0.f, 0.f, 0.f);
     };
 
-    // LayerNorm of 8 rows into the A tile (+ side outputs).  Statistics in
+    // LayerNorm of 4 rows into the A tile (+ side outputs).  Statistics in
     // fp32 as the upstream layer_norm: mean, then the mean of squared
     // deviations, rstd = rsqrt(var + eps), y = bf16((x - mean) * rstd * w + b).
-    auto normalise = [&](const float4 (&v)[8], const TileRows &t, int rbase, uint8_t *abuf) {
-#pragma unroll
-      for (int g = 0; g < 2; ++g) {  // two groups of 4 rows
+    auto normalise = [&](const float4 (&v)[4], const TileRows &t, int rbase, uint8_t *abuf) {
+      {
+        constexpr int g = 0;
         float mean[4], var[4];
 #pragma unroll
         for (int rr = 0; rr < 4; ++rr) {
@@ -521,10 +519,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     };
 
-    // Software pipeline over 8-row batches: the next batch's rows (the second
-    // half of this tile, then the first half of the next tile) are in flight
-    // while the current batch is normalised.
-    float4 va[8], vb[8];
+    // Software pipeline over 4-row batches (four per tile): the next
+    // batch's rows (the rest of this tile, then the first batch of the next
+    // tile) are in flight while the current batch is normalised.
+    float4 va[4], vb[4];
     int tile = blockIdx.x, it = 0;
     TileRows t{};
     if (tile < args.tiles) {
@@ -534,7 +532,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (; tile < args.tiles; tile += gridDim.x, ++it) {
       const int ab = it & 1;
       uint8_t *abuf = smem + kAOff + ab * kABytes;
-      load_rows(t, row_lo + 8, vb);
+      load_rows(t, row_lo + 4, vb);
       // This warp's rows two tiles ahead go to L2 now, so the register loads
       // of later batches wait on L2 rather than on HBM.
       if (lane == 0 && tile + 2 * int(gridDim.x) < args.tiles) {
@@ -544,12 +542,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!warp_wait(&a_empty[ab], ((it >> 1) & 1) ^ 1, args.status, 0x305)) break;
       normalise(va, t, row_lo, abuf);
+      load_rows(t, row_lo + 8, va);
+      normalise(vb, t, row_lo + 4, abuf);
+      load_rows(t, row_lo + 12, vb);
+      normalise(va, t, row_lo + 8, abuf);
       TileRows next = t;
       if (tile + int(gridDim.x) < args.tiles) {
         next = tile_rows<KIND>(args, tile + gridDim.x);
         load_rows(next, row_lo, va);
       }
-      normalise(vb, t, row_lo + 8, abuf);
+      normalise(vb, t, row_lo + 12, abuf);
       tc::fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&a_full[ab]);
