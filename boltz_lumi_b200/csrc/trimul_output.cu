@@ -11,14 +11,16 @@
 //
 // One persistent CTA per SM walks tiles of 128 consecutive j of one outer
 // index i (tiles never straddle i, so every plane segment is contiguous and
-// the 3-D z / x_hat maps clip rows past n).  Warps (10):
+// the 3-D z / x_hat maps clip rows past n).  Warps (14):
 //   0     TMA: p_out / g_out weights once (resident), x_hat tiles per tile
 //   1     TMEM allocation + MMA: D_p = o_hat p_out^T, D_g = x_hat g_out^T
 //         (N = 128 each), double-buffered across tiles (4 x 128 columns)
 //   2..5  epilogue: gate, bf16 y, TMA reduce-add into z (or store)
-//   6..9  LayerNorm: one thread per pair row reads its 128 channels down the
-//         planes (32 lanes = 64 contiguous bytes per channel), normalises in
-//         fp32 and writes the bf16 row into the K-major A tile
+//   6..13 LayerNorm: two threads per pair row, each reading 64 of its 128
+//         channels down the planes (16 lanes = 32 contiguous bytes per
+//         channel); the halves' sums meet in one shuffle, and each thread
+//         writes its 64 normalised channels (one K-block) into the K-major
+//         A tile
 #include "tc.cuh"
 
 namespace bl {
@@ -26,7 +28,7 @@ namespace {
 
 constexpr int kC = 128;
 constexpr int kRows = 128;
-constexpr int kLnWarps = 4;
+constexpr int kLnWarps = 8;
 constexpr int kThreads = (6 + kLnWarps) * 32;
 constexpr int kKBlock = kRows * 64 * 2;  // 16 KB
 constexpr int kTile = 2 * kKBlock;       // [128 rows][128 K] bf16 = 32 KB
@@ -240,16 +242,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) tc::bulk_wait<0>();
   } else {
     // ---------------------------------------------------------------- LayerNorm
-    // Thread = pair row j0 + t of the tile; channel c of it sits at
-    // prod[c * plane + i * ld + j0 + t].
-    const int t = (warp - 6) * 32 + lane;
-    const uint32_t a_row = t * 128, a_sw = t & 7;
+    // Two threads per pair row: lanes 0-15 of LayerNorm warp w take rows
+    // 16 w .. 16 w + 15 of the tile for channels 0..63, lanes 16-31 the same
+    // rows for channels 64..127 (= K-block h of the A tile).  Channel c of
+    // row r sits at prod[c * plane + i * ld + j0 + r].
+    const int r = (warp - 6) * 16 + (lane & 15);
+    const int h = lane >> 4;
+    const uint32_t a_row = r * 128, a_sw = r & 7;
     int it = 0;
     for (int tile = blockIdx.x; tile < args.tiles; tile += gridDim.x, ++it) {
       int i, j0, valid;
       tile_of(tile, i, j0, valid);
       const int b = it & 1;
-      const bool live = t < valid;
+      const bool live = r < valid;
       // The rows of tile + 2 grid go to L2 now (one 256-byte plane segment per channel).
       if (tile + 2 * int(gridDim.x) < args.tiles) {
         int i2, j2, v2;
@@ -258,41 +263,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = (warp - 6) * 32 + lane; c < kC; c += kLnWarps * 32)
           tc::prefetch_l2_bulk(args.prod + c * args.plane + int64_t(i2) * args.ld + j2, uint32_t(span));
       }
-      uint32_t v[64];  // channels 2 q, 2 q + 1 packed
-      const __nv_bfloat16 *src = args.prod + int64_t(i) * args.ld + j0 + t;
+      uint32_t v[32];  // channels 64 h + 2 q, 64 h + 2 q + 1 packed
+      const __nv_bfloat16 *src = args.prod + int64_t(64 * h) * args.plane + int64_t(i) * args.ld + j0 + r;
 #pragma unroll
-      for (int q = 0; q < 64; ++q) {
+      for (int q = 0; q < 32; ++q) {
         const uint16_t lo = live ? __ldg(reinterpret_cast<const unsigned short *>(src + (2 * q) * args.plane)) : 0;
         const uint16_t hi = live ? __ldg(reinterpret_cast<const unsigned short *>(src + (2 * q + 1) * args.plane)) : 0;
         v[q] = uint32_t(lo) | (uint32_t(hi) << 16);
       }
       float sum = 0.f;
 #pragma unroll
-      for (int q = 0; q < 64; ++q) sum += bf16_lo(v[q]) + bf16_hi(v[q]);
+      for (int q = 0; q < 32; ++q) sum += bf16_lo(v[q]) + bf16_hi(v[q]);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 16);
       const float mean = sum * (1.f / 128.f);
       float sq = 0.f;
 #pragma unroll
-      for (int q = 0; q < 64; ++q) {
+      for (int q = 0; q < 32; ++q) {
         const float d0 = bf16_lo(v[q]) - mean, d1 = bf16_hi(v[q]) - mean;
         sq += d0 * d0;
         sq += d1 * d1;
       }
+      sq += __shfl_xor_sync(0xffffffffu, sq, 16);
       const float rs = rsqrtf(sq * (1.f / 128.f) + args.eps);
       if (!warp_wait(&a_empty[b], ((it >> 1) & 1) ^ 1, args.status, 0x507)) break;
-      uint8_t *abuf = smem + kAOff + b * kTile;
+      uint8_t *abuf = smem + kAOff + b * kTile + h * kKBlock;
 #pragma unroll
-      for (int c16 = 0; c16 < 16; ++c16) {  // 8 channels per 16-byte chunk
+      for (int c16 = 0; c16 < 8; ++c16) {  // 8 channels per 16-byte chunk
         uint32_t o[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int c = 8 * c16 + 2 * e;
+          const int c = 64 * h + 8 * c16 + 2 * e;
           const uint32_t x2 = v[4 * c16 + e];
           o[e] = live ? cvt_bf16x2((bf16_lo(x2) - mean) * rs * lnw_s[c] + lnb_s[c],
                                    (bf16_hi(x2) - mean) * rs * lnw_s[c + 1] + lnb_s[c + 1])
                       : 0u;
         }
-        *reinterpret_cast<uint4 *>(abuf + (c16 >> 3) * kKBlock + a_row + (((c16 & 7) ^ a_sw) << 4)) =
-            make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4 *>(abuf + a_row + ((c16 ^ a_sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
       }
       tc::fence_proxy_async_smem();
       __syncwarp();
