@@ -76,7 +76,7 @@ template <int BN, int EPI> struct GemmShape {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = BN == 256 ? 3 : 5;
+  static constexpr int kStages = BN == 256 ? 4 : 5;  // 4 x 48 KB + 32 KB staging fits in 227 KB
   static constexpr int kRingBytes = kStages * kStageBytes;
   static constexpr int kStagingPerWarp = 2 * kStagingBytes;  // double-buffered 4 KB boxes
   static constexpr int kStagingTotal = 4 * kStagingPerWarp;
