@@ -48,8 +48,11 @@ def _mask(batch, n, gen, p_zero=0.2):
     return m.cuda()
 
 
+# (2, 128, 16, 48) and (1, 65, 2, 64) run the two-CTA key split, (1, 256, 16, 48)
+# and (1, 230, 8, 24) the four-CTA split (small grids), the rest one CTA per query tile.
 @pytest.mark.parametrize("batch,n,heads,d", [(1, 17, 16, 48), (2, 128, 16, 48), (1, 300, 16, 24),
-                                             (3, 64, 4, 32), (1, 65, 2, 64), (1, 1, 16, 48)])
+                                             (3, 64, 4, 32), (1, 65, 2, 64), (1, 1, 16, 48),
+                                             (1, 256, 16, 48), (1, 230, 8, 24)])
 def test_core_matches_torch(batch, n, heads, d):
     gen = torch.Generator().manual_seed(n * 7 + d)
     q, k, v, g = (torch.randn(batch, n, heads, d, generator=gen).cuda() for _ in range(4))
