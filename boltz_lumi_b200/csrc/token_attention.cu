@@ -317,8 +317,7 @@ __global__ void __launch_bounds__(kThreads, 2) token_attention_kernel(const TokA
       }
     }
     cluster_sync_all();  // peers may still be reading this CTA's partials
-    return;
-  }
+  } else {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
 #pragma unroll
@@ -338,6 +337,7 @@ __global__ void __launch_bounds__(kThreads, 2) token_attention_kernel(const TokA
       else
         dst[e] = out_v;
     }
+  }
   }
 }
 
