@@ -25,6 +25,7 @@ SIGNATURES = {
     "bl_last_error": [],
     "bl_version": [],
     "bl_device_status": [c_int],
+    "bl_wait_selftest": [c_int, c_int64, _p],
     "bl_layernorm": [_p, c_int, c_int64, c_int64, c_int, _p, _p, c_float, _p, c_int, _p],
     "bl_gate": [_p, _p, _p, c_int64, _p],
     "bl_gate_pack": [_p, _p, c_int64, _p, c_int64, c_int, _p, _p, _p],

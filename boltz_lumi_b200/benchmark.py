@@ -15,8 +15,8 @@ Follows the reference's harness (benchmark.py:20-240):
 - ``timings.json`` holds the settings, every call and round, the per-field errors, the warm
   means of both recipes and the time saved.
 
-This build is not bitwise identical to upstream: it matches it within north_star's
-tolerances. So the comparison reports errors per field and judges them against
+This build is not bitwise identical to upstream: it matches it within the end-to-end
+tolerances this package targets. So the comparison reports errors per field and judges them against
 :data:`TOLERANCES`, where the reference asks for atol = rtol = 0:
 
 - coordinate RMSD <= 0.1 Angstrom;

@@ -84,17 +84,20 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 // Bounded wait on `parity`.  Returns false (after recording `code` in the
-// status word) if the phase does not complete in time, or if another wait of
-// this launch or an earlier one already failed (status non-zero).
+// status word) if the phase does not complete within `limit_ns`, or if
+// another wait of this launch or an earlier one already failed (status
+// non-zero).  Kernels use the default limit; bl_wait_selftest passes a short
+// one to exercise the timeout path.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsigned int *status,
-                                          unsigned int code) {
+                                          unsigned int code, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
+  const uint32_t suspend_ns = limit_ns < 16000000ull ? uint32_t(limit_ns / 16 + 1) : 1000000u;
   for (uint32_t spin = 1;; ++spin) {
-    if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
+    if (mbar_try_wait_sleep(bar, parity, suspend_ns)) return true;
     if ((spin & 15u) == 0) {
       if (*reinterpret_cast<volatile unsigned int *>(status) != 0u) return false;
-      if (global_timer_ns() - start > kWaitLimitNs) {
+      if (global_timer_ns() - start > limit_ns) {
         atomicCAS(status, 0u, code);
         return false;
       }

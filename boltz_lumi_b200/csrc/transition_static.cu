@@ -38,7 +38,10 @@ static __device__ __align__(256) unsigned char g_transition_scratch[kScratchByte
 
 // Device address of the array, looked up once per device.  In host code the
 // array's name is only a host-side stand-in, so the address must come from
-// cudaGetSymbolAddress with that device current.
+// cudaGetSymbolAddress with that device current.  The cached address belongs
+// to the device's primary context: after cudaDeviceReset (or anything else
+// that destroys that context) it no longer points at the array, so this entry
+// point must not be used across a device reset within one process.
 constexpr int kMaxDevices = 64;
 std::mutex g_setup_lock;
 unsigned char *g_scratch_ptr[kMaxDevices] = {};
@@ -68,6 +71,8 @@ extern "C" int bl_pair_transition_static(const float *x, int64_t rows, const flo
              (long long)rows, (long long)kMaxRows);
   if (rows == 0) return BL_OK;
   BL_REQUIRE(x && w12 && w3 && out, "bl_pair_transition_static: null pointer");
+  BL_REQUIRE(bl::aligned_to(x, 16) && bl::aligned_to(w12, 16) && bl::aligned_to(w3, 16) && bl::aligned_to(out, 16),
+             "bl_pair_transition_static: x, w12, w3 and out must be 16-byte aligned");
   unsigned char *scratch = nullptr;
   int rc = scratch_for_current_device(&scratch);
   if (rc) return rc;

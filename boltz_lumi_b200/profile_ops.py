@@ -80,7 +80,7 @@ def main():
         "transition": lambda: forwards.transition_forward(block.transition_z, z, residual=z),
         "block": lambda: block(s, z, mask, pmask),
     }
-    # SURVEY measurement configs: C2 = both triangle attentions, C3 = both
+    # Composite measurement configs: c2 = both triangle attentions, c3 = both
     # triangle multiplications and the pair transition.
     ops["c2"] = lambda: (ops["att_start"](), ops["att_end"]())
     ops["c3"] = lambda: (ops["tri_mul_out"](), ops["tri_mul_in"](), ops["transition"]())

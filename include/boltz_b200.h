@@ -4,9 +4,10 @@
  * Every entry point takes plain device pointers, element counts and a
  * cudaStream_t passed as void*, launches asynchronously on that stream and
  * returns a BL_* status.  On failure bl_last_error() holds a message (per
- * calling thread).  No entry point allocates device memory; intermediate
- * buffers are passed in by the caller.  Inference only: nothing here records
- * autograd state.
+ * calling thread).  No entry point allocates device memory: intermediate
+ * buffers are passed in by the caller, except for bl_pair_transition_static,
+ * whose intermediates live in a fixed array compiled into the library (see
+ * its declaration).  Inference only: nothing here records autograd state.
  *
  * Each declaration names the reference interface it replaces
  * (lauritsf/boltz-lumi, path relative to src/boltz_lumi/).
@@ -56,6 +57,15 @@ BL_API int bl_version(void);
  * completed, otherwise a code naming the wait that gave up.  reset != 0
  * clears it.  Synchronises the device. */
 BL_API int bl_device_status(int reset);
+
+/* Self-test of the bounded device-side wait used by every tensor-core kernel:
+ * one thread waits on an mbarrier phase with a limit of limit_ns (at most
+ * 2 s).  arrive != 0 completes the phase first (the wait succeeds, the status
+ * word stays 0); arrive == 0 leaves it incomplete, so the wait gives up after
+ * limit_ns, records 0x7F01 in the status word (read it with
+ * bl_device_status) and the kernel returns normally.  Diagnostic only; no
+ * counterpart in the reference. */
+BL_API int bl_wait_selftest(int arrive, int64_t limit_ns, void *stream);
 
 /*
  * LayerNorm over `cols` channels, fp32 statistics.
@@ -350,10 +360,13 @@ BL_API int bl_diffusion_epilogue_split3(const float *a, const float *b, const fl
  *   x: fp32 [rows, 128]; ln_weight, ln_bias: fp32 [128] (may be NULL);
  *   w12: bf16 [1024, 128] (fc1 rows then fc2 rows); w3: bf16 [128, 512];
  *   out: bf16 [rows, 128].  rows <= 1024, otherwise BL_ERR_INVALID.
+ *   x, w12, w3 and out must be 16-byte aligned.
  * Runs on the current device.  Its first call on a device looks up the
  * array's device address, so make that first call before any stream
- * capture.  All calls on a device share the array: calls that overlap on the
- * GPU (e.g. on two streams) race; calls ordered on one stream do not.
+ * capture.  The address is kept for the life of the process: do not use
+ * this entry point across a cudaDeviceReset.  All calls on a device share
+ * the array: calls that overlap on the GPU (e.g. on two streams) race; calls
+ * ordered on one stream do not.
  */
 BL_API int bl_pair_transition_static(const float *x, int64_t rows, const float *ln_weight,
                                      const float *ln_bias, float eps, const void *w12, const void *w3,

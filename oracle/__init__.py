@@ -21,7 +21,7 @@ the reference's kernels preserve.  Parity status:
   cannot run in this environment.
 """
 
-from .numerics import bf16_round, linear_bf16, sigmoid_bf16  # noqa: F401
+from .numerics import GATE, GATED_SWIGLU, MODULATION, bf16_round, diffusion_epilogue, linear_bf16, sigmoid_bf16  # noqa: F401
 from .modules import (  # noqa: F401
     AdaLN,
     Attention,

@@ -30,7 +30,7 @@ import math
 import torch
 from torch import nn
 
-from .numerics import bf16_round, linear_bf16, sigmoid_bf16, silu_bf16
+from .numerics import GATE, GATED_SWIGLU, MODULATION, bf16_round, diffusion_epilogue, linear_bf16, sigmoid_bf16, silu_bf16
 
 
 def _linear(x, layer, bf16):
@@ -129,8 +129,8 @@ class TriangleAttention(nn.Module):
         """x: [B, N, N, C] fp32; mask: [B, N, N].  Returns the bf16-valued update.
 
         ``rows`` limits the computation to the first outer rows (of z, or of z
-        transposed for the ending node); the CPU-baseline timing uses it to
-        extrapolate from a bounded sample.
+        transposed for the ending node); the largest parity case (N = 2511)
+        checks that many rows only.
         """
         if mask is None:
             mask = x.new_ones(x.shape[:-1])
@@ -247,7 +247,7 @@ class AdaLN(nn.Module):
         a = _layer_norm(a, self.a_norm)
         s = _layer_norm(s, self.s_norm)
         # diffusion_hip.cu:15-18: the multiply and the add round separately.
-        return torch.sigmoid(self.s_scale(s)) * a + self.s_bias(s)
+        return diffusion_epilogue(MODULATION, a, self.s_scale(s), self.s_bias(s))
 
 
 class ConditionedTransitionBlock(nn.Module):
@@ -264,10 +264,8 @@ class ConditionedTransitionBlock(nn.Module):
 
     def forward(self, a, s):
         a = self.adaln(a, s)
-        x = self.swish_gate[0](a)
-        half = x.shape[-1] // 2
-        b = nn.functional.silu(x[..., half:]) * x[..., :half] * self.a_to_b(a)
-        return torch.sigmoid(self.output_projection[0](s)) * self.b_to_a(b)
+        b = diffusion_epilogue(GATED_SWIGLU, self.swish_gate[0](a), self.a_to_b(a))
+        return diffusion_epilogue(GATE, self.output_projection[0](s), self.b_to_a(b))
 
 
 class AttentionPairBias(nn.Module):

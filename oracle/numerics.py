@@ -36,3 +36,25 @@ def sigmoid_bf16(x: torch.Tensor) -> torch.Tensor:
 def silu_bf16(x: torch.Tensor) -> torch.Tensor:
     """``F.silu`` on a bf16 tensor, rounded to bf16 (``kernels/pair_hip.cu:12-17``)."""
     return bf16_round(torch.nn.functional.silu(bf16_round(x)))
+
+
+# Diffusion epilogue operation codes (the reference's diffusion.py:27).
+MODULATION, GATE, GATED_SWIGLU = 0, 1, 3
+
+
+def diffusion_epilogue(kind: int, a: torch.Tensor, b: torch.Tensor, c=None) -> torch.Tensor:
+    """The fp32 diffusion epilogues (``kernels/diffusion_hip.cu:13-27``), no autocast.
+
+    * MODULATION: ``sigmoid(b) * a + c`` (AdaLN, the multiply and add round separately);
+    * GATE: ``sigmoid(a) * b`` (the conditioned transition's output gate);
+    * GATED_SWIGLU: ``silu(a[..., h:]) * a[..., :h] * b`` with ``a`` of width 2h
+      (swish_gate's projection times a_to_b's).
+    """
+    if kind == MODULATION:
+        return torch.sigmoid(b) * a + c
+    if kind == GATE:
+        return torch.sigmoid(a) * b
+    if kind == GATED_SWIGLU:
+        half = a.shape[-1] // 2
+        return torch.nn.functional.silu(a[..., half:]) * a[..., :half] * b
+    raise ValueError(f"unknown diffusion epilogue kind {kind}")

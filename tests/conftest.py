@@ -39,6 +39,18 @@ def report(actual, expected):
     )
 
 
+def record_parity(case, info):
+    """Append a case's measured errors to the JSON-lines file named by BL_PARITY_LOG (if set),
+    so a GPU run leaves the per-op error table behind."""
+    path = os.environ.get("BL_PARITY_LOG")
+    if not path:
+        return
+    import json
+
+    with open(path, "a") as f:
+        f.write(json.dumps({"case": case, **{k: v for k, v in info.items()}}) + "\n")
+
+
 def assert_close(actual, expected, atol, rtol=0.0, rel_l2=None):
     """max |a - e| <= atol + rtol |e| elementwise, optional relative-L2 bound."""
     a = actual.detach().double().cpu()

@@ -3,8 +3,8 @@
 Case lists follow tests/test_operator_additions.py of the reference (token
 counts with tails, masked tokens, zero / ones / partial / fractional masks,
 N(0, 0.08) weights with unit-mean norms) at sizes the CPU oracle finishes in
-seconds.  Tolerances: north_star's per-op max abs error 2e-2 for the bf16
-trunk ops, 1e-4 for the fp32 diffusion ops.
+seconds.  Tolerances: per-op max abs error 2e-2 for the bf16 trunk ops,
+1e-4 for the fp32 diffusion ops.
 """
 
 import pytest
@@ -43,6 +43,8 @@ def pair_mask(n, kind, masked_tokens=3, seed=5):
     elif kind == "partial":
         mask[:, -masked_tokens:, :] = 0
         mask[:, :, -masked_tokens:] = 0
+    elif kind == "partial_rows":  # the reference's multiplication case: rows only
+        mask[:, -masked_tokens:, :] = 0
     elif kind == "fractional":
         mask = torch.rand(1, n, n, generator=torch.Generator().manual_seed(seed))
     return mask
@@ -91,11 +93,12 @@ def test_triangle_attention_reference_sizes(ending, n, kind, rows):
 
 @pytest.mark.parametrize("incoming", [False, True])
 @pytest.mark.parametrize("n", [312, 576])
-@pytest.mark.parametrize("kind", ["zero", "ones", "partial", "fractional"])
+@pytest.mark.parametrize("kind", ["zero", "ones", "partial", "partial_rows", "fractional"])
 def test_triangle_multiplication_reference_sizes(incoming, n, kind):
     """The reference's multiplication cases at N = 312 and 576 (test_operator_additions.py:68,
-    x * 0.3, the last two tokens masked), oracle on the GPU as the checker.  Bound: max(2e-2,
-    one bf16 ulp of the expected value) per element, relative L2 <= 1e-2."""
+    112-130: x * 0.3, masks zero / ones / last two rows / uniform; plus rows and columns),
+    oracle on the GPU as the checker.  Bound: max(2e-2, one bf16 ulp of the expected value)
+    per element, relative L2 <= 1e-2."""
     cls = (layers.TriangleMultiplicationIncoming, oracle.TriangleMultiplicationIncoming) if incoming else \
         (layers.TriangleMultiplicationOutgoing, oracle.TriangleMultiplicationOutgoing)
     mod, ref = build(*cls, 128)
@@ -110,7 +113,7 @@ def test_triangle_multiplication_reference_sizes(incoming, n, kind):
 
 @pytest.mark.parametrize("incoming", [False, True])
 @pytest.mark.parametrize("n", [7, 64, 117, 128])
-@pytest.mark.parametrize("kind", ["zero", "ones", "partial", "fractional"])
+@pytest.mark.parametrize("kind", ["zero", "ones", "partial", "partial_rows", "fractional"])
 def test_triangle_multiplication(incoming, n, kind):
     cls = (layers.TriangleMultiplicationIncoming, oracle.TriangleMultiplicationIncoming) if incoming else \
         (layers.TriangleMultiplicationOutgoing, oracle.TriangleMultiplicationOutgoing)
@@ -204,7 +207,7 @@ def test_conditioned_transition(tokens, dim):
 
 
 def test_pairformer_block_c1():
-    """one block at N = 64, s ~ N(0,1) [1,64,384], z ~ N(0,1), pair mask ones."""
+    """Block parity config: one block at N = 64, s ~ N(0,1) [1,64,384], z ~ N(0,1), pair mask ones."""
     n = 64
     mod, ref = build(layers.PairformerLayer, oracle.PairformerLayer, std=1 / 128 ** 0.5)
     g = torch.Generator().manual_seed(11)

@@ -46,12 +46,33 @@ def test_sigmoid_gate_matches_reference_expression():
 
 
 def test_diffusion_epilogues_match_reference_expressions():
+    """The oracle's diffusion epilogues (the ones its AdaLN and ConditionedTransitionBlock
+    call) reproduce the reference expressions' golden values bitwise."""
     case = GOLDEN["epilogue"]
     a, b, c, wide = case["a"], case["b"], case["c"], case["wide"]
-    assert torch.allclose(torch.sigmoid(b) * a + c, case["modulation"], atol=0, rtol=0)
-    assert torch.allclose(torch.sigmoid(a) * b, case["gate"], atol=0, rtol=0)
-    swiglu = torch.nn.functional.silu(wide[:, 768:]) * wide[:, :768] * b
-    assert torch.allclose(swiglu, case["swiglu"], atol=0, rtol=0)
+    assert torch.equal(numerics.diffusion_epilogue(numerics.MODULATION, a, b, c), case["modulation"])
+    assert torch.equal(numerics.diffusion_epilogue(numerics.GATE, a, b), case["gate"])
+    assert torch.equal(numerics.diffusion_epilogue(numerics.GATED_SWIGLU, wide, b), case["swiglu"])
+
+
+def test_oracle_diffusion_modules_use_the_pinned_epilogues():
+    """AdaLN and ConditionedTransitionBlock of the oracle equal their formulas written out
+    with the same expressions the golden epilogue values pin."""
+    import oracle
+
+    g = torch.Generator().manual_seed(3)
+    block = oracle.randomize(oracle.ConditionedTransitionBlock(64, 64), std=0.1, generator=g)
+    a = torch.randn(5, 64, generator=g)
+    s = torch.randn(5, 64, generator=g)
+    ada = block.adaln
+    an = torch.nn.functional.layer_norm(a, (64,), eps=ada.a_norm.eps)
+    sn = torch.nn.functional.layer_norm(s, (64,), ada.s_norm.weight, None, ada.s_norm.eps)
+    modulated = torch.sigmoid(ada.s_scale(sn)) * an + ada.s_bias(sn)
+    assert torch.allclose(ada(a, s), modulated, atol=1e-6)
+    x = block.swish_gate[0](modulated)
+    bb = torch.nn.functional.silu(x[:, 64 * 2:]) * x[:, :64 * 2] * block.a_to_b(modulated)
+    expected = torch.sigmoid(block.output_projection[0](s)) * block.b_to_a(bb)
+    assert torch.allclose(block(a, s), expected, atol=1e-5)
 
 
 def test_oracle_module_shapes_and_masks():
