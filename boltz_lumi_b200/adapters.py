@@ -40,13 +40,22 @@ def _bf16_autocast():
     return torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16
 
 
+def _fp32_mode(x):
+    """Autocast off and fp32 input: upstream computes the whole op in fp32 (the
+    reference's fast path takes this case too, triangle.py:47-51)."""
+    return not torch.is_autocast_enabled("cuda") and x.dtype == torch.float32
+
+
 def _triangle_attention(self, x, mask=None, chunk_size=None, use_kernels=False):
     cls = type(self)
-    if (use_kernels or not _inference(self, x, mask) or not _bf16_autocast() or x.dim() != 4
+    fp32 = _fp32_mode(x)
+    if (use_kernels or not _inference(self, x, mask) or not (_bf16_autocast() or fp32) or x.dim() != 4
             or x.shape[-1] != 128 or not forwards._attention_supported(self) or x.shape[1] > 4096):
         return cls.forward(self, x, mask=mask, chunk_size=chunk_size, use_kernels=use_kernels)
     starting = getattr(self, "starting", cls.__name__ != "TriangleAttentionEndingNode")
     self.starting = starting
+    if fp32:
+        return forwards.triangle_attention_forward_fp32(self, x, mask, chunk_size)
     return forwards.triangle_attention_forward(self, x.float(), mask, chunk_size)
 
 

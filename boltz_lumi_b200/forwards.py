@@ -214,6 +214,70 @@ def triangle_attention_forward(self, x, mask=None, chunk_size=None, use_kernels=
     return residual if residual is not None else out
 
 
+def triangle_attention_forward_fp32(self, x, mask=None, chunk_size=None, use_kernels=False):
+    """Upstream ``TriangleAttention.forward`` in fp32 mode: fp32 input, autocast off.
+
+    The reference's fast path accepts this case too (triangle.py:47-51: ``q_x.dtype`` fp32 and
+    autocast disabled); upstream then computes every linear, the scores and the softmax in
+    fp32 and returns fp32.  Here:
+
+    1. ``bl_layernorm_split3``: LayerNorm of each pair row, written as the three bf16 split
+       planes of the next linear's operand;
+    2. ``bl_linear_split3``: q | k | v | g (linear_g's bias) and the 128 -> 4 triangle-bias
+       projection as one fp32-accurate tensor-core GEMM, [N*N, 516];
+    3. ``bl_token_attention``: fp32 flash attention per outer row, reading q / k / v / g, the
+       bias planes and the mask through strides (the ending node is the same call on z
+       transposed: swapped row strides, a transposed bias view and a transposed mask), with
+       sigmoid(g) applied in its epilogue and its output written as split planes;
+    4. ``bl_linear_split3``: linear_o with its bias.
+
+    Returns fp32 [B, N, N, 128].  Error: within 1e-4 of upstream's fp32 eager path on O(1)
+    outputs (the split linears keep every product to 2^-24 relative).
+    """
+    _check_pair_input(x, mask)
+    if not _attention_supported(self):
+        raise RuntimeError("triangle attention kernels cover c_z = 128, 4 heads x 32 only")
+    if x.dtype != torch.float32:
+        raise RuntimeError("fp32-mode triangle attention takes fp32 input")
+    starting = getattr(self, "starting", True)
+    batch, n = x.shape[0], x.shape[1]
+    if mask is None:
+        mask = x.new_ones(x.shape[:-1], dtype=torch.float32)
+    mask = mask.float()
+    mha, ln = self.mha, self.layer_norm
+    out = torch.empty(batch, n, n, 128, device=x.device, dtype=torch.float32)
+    if n == 0 or batch == 0:
+        return out
+    stream = stream_of(x)
+    width = 516  # q | k | v | g | 4 bias heads
+    with torch.autocast("cuda", enabled=False):
+        for b in range(batch):
+            x3 = kernels.layer_norm_split3(x[b].reshape(n * n, 128), ln.weight, ln.bias, ln.eps)
+            proj = _linear32_planes(self, "_bl_w3_tri_fp32", x3, (n, n),
+                                    [mha.linear_q.weight, mha.linear_k.weight, mha.linear_v.weight,
+                                     mha.linear_g.weight, self.linear.weight],
+                                    [None, None, None, mha.linear_g.bias, None])
+            heads = proj[..., 512:516]  # [i, j, h]
+            if starting:  # outer row i, inner j: element (a, b) at a*N*W + b*W
+                strides = (n * width, width, 32)
+                bias = heads.permute(2, 0, 1).unsqueeze(0)  # bias[h][q][k] = lin(LN(z))[q, k, h]
+                mask_rows = mask[b].contiguous()
+            else:  # z transposed: outer row a = column of z, inner b = row of z
+                strides = (width, n * width, 32)
+                bias = heads.permute(2, 1, 0).unsqueeze(0)  # lin(LN(z^T))[q, k, h] = lin(LN(z))[k, q, h]
+                mask_rows = mask[b].t().contiguous()
+            out3 = torch.empty(3, n * n, 128, device=x.device, dtype=torch.bfloat16)
+            base = proj.data_ptr()
+            kernels.launch_token_attention(base, base + 128 * 4, base + 256 * 4, base + 384 * 4, strides, bias,
+                                           mask_rows, float(getattr(self, "inf", 1e9)), n, 4, n, 32, None, stream,
+                                           out3=out3)
+            del proj
+            y = _linear32_planes(self, "_bl_w3_tri_fp32_o", out3, (n, n), [mha.linear_o.weight],
+                                 [mha.linear_o.bias])
+            out[b].copy_(y if starting else y.transpose(0, 1))
+    return out
+
+
 # ---------------------------------------------------------------------------
 # Triangle multiplication (outgoing / incoming)
 # ---------------------------------------------------------------------------
@@ -518,5 +582,6 @@ __all__ = [
     "normalization_forward",
     "transition_forward",
     "triangle_attention_forward",
+    "triangle_attention_forward_fp32",
     "triangle_multiplication_forward",
 ]

@@ -91,6 +91,48 @@ def test_triangle_attention_reference_sizes(ending, n, kind, rows):
     assert_close(actual.float(), expected, atol=BF16_ATOL, rtol=BF16_ULP, rel_l2=BF16_REL_L2)
 
 
+@pytest.mark.parametrize("ending", [False, True])
+@pytest.mark.parametrize("n,kind", [(17, "ones"), (64, "partial"), (130, "partial"), (200, "ones"), (312, "partial")])
+def test_triangle_attention_fp32_mode(ending, n, kind):
+    """fp32 mode: fp32 input with autocast off (the reference's fast path accepts it,
+    triangle.py:47-51).  An upstream-named module (the oracle's class) is rebound by
+    adapters.install and called without autocast; the result is fp32 and within the fp32
+    contract (1e-4) of upstream's fp32 semantics (the oracle with bf16=False)."""
+    import copy
+
+    from torch import nn
+
+    from boltz_lumi_b200 import adapters
+
+    cls = oracle.TriangleAttentionEndingNode if ending else oracle.TriangleAttention
+    ref = oracle.randomize(cls(128, 32, 4), std=128 ** -0.5, generator=torch.Generator().manual_seed(n))
+    x = torch.randn(1, n, n, 128, generator=torch.Generator().manual_seed(n + 3))
+    mask = pair_mask(n, kind)
+    expected = ref(x, mask, chunk_size=32, bf16=False)
+    model = nn.Module()
+    model.pairformer = nn.Module()
+    model.pairformer.tri_att = copy.deepcopy(ref).cuda().eval()
+    assert adapters.install(model) == 1
+    with torch.inference_mode():
+        actual = model.pairformer.tri_att(x.cuda(), mask.cuda(), chunk_size=32)
+    assert actual.dtype == torch.float32
+    info = assert_close(actual, expected, atol=FP32_ATOL)
+    assert info["relative_l2_error"] < 1e-5, info
+
+
+def test_triangle_attention_fp32_mode_differs_from_bf16_contract():
+    """The fp32 path is not the bf16 path in disguise: on the same module and input the
+    bf16-autocast result differs from the fp32 one by far more than the fp32 tolerance."""
+    from boltz_lumi_b200 import forwards
+
+    mod, ref = build(layers.TriangleAttention, oracle.TriangleAttention, 128, 32, 4, std=128 ** -0.5)
+    x = torch.randn(1, 48, 48, 128, generator=torch.Generator().manual_seed(9)).cuda()
+    with torch.inference_mode():
+        y32 = forwards.triangle_attention_forward_fp32(mod, x)
+        y16 = forwards.triangle_attention_forward(mod, x)
+    assert (y32 - y16.float()).abs().max().item() > 10 * FP32_ATOL
+
+
 @pytest.mark.parametrize("incoming", [False, True])
 @pytest.mark.parametrize("n", [312, 576])
 @pytest.mark.parametrize("kind", ["zero", "ones", "partial", "partial_rows", "fractional"])
