@@ -53,6 +53,8 @@ def parse_args():
     # way a longer job would (at ~3 ms per step the region stays < 0.1 s).
     p.add_argument("--e2e-steps", type=int, default=24)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-sub-records", action="store_true",
+                   help="skip the row-sharded N=2048 block and the diffusion sampler sub-records")
     p.add_argument("--sharded", action="store_true",
                    help="one block at --n (default 2048) row-sharded over the ranks (strong scaling)")
     return p.parse_args()
@@ -490,6 +492,12 @@ def run_b200(args):
         "clocks": clock_info,
         "kernels_ms_per_step": {k: round(v["ms"], 4) for k, v in sorted(per_label.items(), key=lambda kv: -kv[1]["ms"])},
     }
+    if not args.no_sub_records:
+        # Multi-GPU partitions beyond the replica headline: the row-sharded N = 2048 block
+        # (strong scaling, NCCL collectives) and the sample-parallel diffusion sampler
+        # (one input per GPU).  Every rank takes part; rank 0 reports.
+        line["sharded"] = measure_sharded(2048, min(args.steps, 10), 2, 2, dist, device)
+        line["diffusion"] = measure_diffusion(dist, device)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         # Same procedure as the reference arm: one untimed warm-up block, then one timed block.
         cpu_block_sample(n)
@@ -515,30 +523,21 @@ def traffic_for(label):
     return None
 
 
-def run_sharded(args):
-    """One Pairformer block at N (default 2048) row-sharded over the ranks:
-    each rank holds N / world rows of z, the collectives run on NCCL over
-    NVLink.  Total work per step is fixed (strong scaling); value = device
-    time per block, max over ranks."""
-    world, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    dist = None
+def measure_sharded(n, steps, warmup, e2e_steps, dist, device):
+    """One Pairformer block at n tokens row-sharded over the ranks (each rank holds
+    n / world rows of z; the row <-> column transposes and plane / bias gathers run on
+    NCCL over NVLink).  Total work per step is fixed (strong scaling).  Returns the
+    record (device time per block, max over ranks) on every rank."""
     from boltz_lumi_b200 import _lib, layers
     from boltz_lumi_b200.sharded import ShardedPairformer, SingleComm, TorchComm
 
-    if world > 1:
-        import datetime
-        import torch.distributed as dist_mod
-
-        dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-        dist = dist_mod
     comm = TorchComm() if dist is not None else SingleComm()
-    n = args.n if args.n != N_TOKENS else 2048
+    world, rank = comm.world, comm.rank
     n_loc = n // world
     block = seeded_block(layers.PairformerLayer).to(device)
     s_h, z_h, mask_h, pmask_h = synthetic_inputs(n, seed=1000)  # one block, split by rows
     zr_h = z_h[0, rank * n_loc:(rank + 1) * n_loc].contiguous()
+    del z_h
     s, mask, pmask = s_h.to(device), mask_h.to(device), pmask_h.to(device)
     z_rows = zr_h.to(device)
     sharded = ShardedPairformer(block, comm)
@@ -547,10 +546,8 @@ def run_sharded(args):
         if dist is not None:
             dist.barrier()
 
-    clocks = ClockSampler(device)
-    clocks.wait_ready()
     with torch.inference_mode():
-        for _ in range(max(args.warmup, 3)):
+        for _ in range(max(warmup, 1)):
             s, z_rows = sharded(s, z_rows, mask, pmask)
         torch.cuda.synchronize()
         observer = _lib.CallObserver(timed=())
@@ -558,17 +555,14 @@ def run_sharded(args):
         barrier()
         torch.cuda.synchronize()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        t0 = time.monotonic()
         start.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             s, z_rows = sharded(s, z_rows, mask, pmask)
         end.record()
         torch.cuda.synchronize()
-        t1 = time.monotonic()
         _lib.set_observer(None)
         barrier()
-        clock_info = clocks.stop((t0, t1))
-        ms = max_over_ranks(start.elapsed_time(end), dist, device) / args.steps
+        ms = max_over_ranks(start.elapsed_time(end), dist, device) / steps
         launches = observer.calls
         # End to end: this rank's rows and s in from pinned memory, back out, every step.
         zr_pin, s_pin = zr_h.pin_memory(), s_h.pin_memory()
@@ -577,7 +571,7 @@ def run_sharded(args):
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(args.e2e_steps):
+        for _ in range(e2e_steps):
             zd, sd = zr_pin.to(device, non_blocking=True), s_pin.to(device, non_blocking=True)
             so, zo = sharded(sd, zd, mask, pmask)
             z_back.copy_(zo, non_blocking=True)
@@ -585,26 +579,99 @@ def run_sharded(args):
         e1.record()
         torch.cuda.synchronize()
         barrier()
-        e2e = max_over_ranks(e0.elapsed_time(e1), dist, device) / args.e2e_steps
+        e2e = max_over_ranks(e0.elapsed_time(e1), dist, device) / e2e_steps
         assert torch.isfinite(z_back).all() and torch.isfinite(s_back).all(), "non-finite block output"
+    flops = 4.0 * n ** 3 * 4 * 32 * 2 + 2 * 2.0 * 128 * n ** 3 + 2.0 * n * n * (128 * 1024 + 512 * 128)
+    return {
+        "metric": f"Pairformer ms/block at N={n} row-sharded bf16", "value": round(ms, 4), "unit": UNIT,
+        "n_gpus": world, "steps": steps, "warmup": max(warmup, 1), "ms_per_step": round(ms, 4),
+        "higher_is_better": False, "scaling": "strong",
+        "workload": f"one Pairformer block N={n}, z rows split over {world} GPU(s) "
+                    "(all_to_all row/column transposes, all_gather of planes and biases, NCCL)",
+        "tokens": n, "rows_per_gpu": n_loc, "parallelism": f"row-sharded x{world}",
+        "e2e": {"value": round(e2e, 4), "unit": UNIT, "h2d_bytes_per_step": zr_pin.numel() * 4 + s_pin.numel() * 4,
+                "d2h_bytes_per_step": zr_pin.numel() * 4 + s_pin.numel() * 4, "steps": e2e_steps},
+        "gpu_launches": launches,
+        "tensor_tflops_pair_ops": round(flops / (ms * 1e-3) / 1e12, 1),
+    }
+
+
+DIFFUSION = {"tokens": 384, "steps": 200, "multiplicity": 5, "depth": 24, "c_token": 768, "heads": 16}
+
+
+def measure_diffusion(dist, device, steps=DIFFUSION["steps"]):
+    """Predictions per hour of the sample-parallel diffusion sampler (one input per GPU,
+    its multiplicity samples on that GPU, weak scaling; boltz_lumi_b200.sampling): the
+    200-step EDM sampler of AF3 Algorithm 18 over a 24-layer token transformer of this
+    package's diffusion kernels, coordinates gathered with one all_gather at the end.
+    Time = device time of the whole sampling call (max over ranks)."""
+    from boltz_lumi_b200 import sampling
+    from boltz_lumi_b200.sharded import SingleComm, TorchComm
+
+    comm = TorchComm() if dist is not None else SingleComm()
+    cfg = DIFFUSION
+    n, mult = cfg["tokens"], cfg["multiplicity"]
+    model = sampling.seeded_model(depth=cfg["depth"], c_token=cfg["c_token"], heads=cfg["heads"], seed=5,
+                                  device=device)
+    inputs = [sampling.synthetic_conditioning(n, cfg["depth"], cfg["heads"], seed=100 + i, device=device)
+              for i in range(comm.world)]
+
+    def runner(sampler):
+        def run(i, samples, gens):
+            s_trunk, bias, mask = inputs[i]
+            s_base = model.conditioning(s_trunk)
+            return sampler.sample(lambda x, sig: model(x, sig, s_base, bias, mask), n, gens, device)
+        return run
+
+    with torch.inference_mode():
+        sampling.distributed_sample(runner(sampling.EDMSampler(steps=3)), comm.world, mult, n, 1, comm, device)
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        coords = sampling.distributed_sample(runner(sampling.EDMSampler(steps=steps)), comm.world, mult, n, 2,
+                                             comm, device)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = max_over_ranks(e0.elapsed_time(e1), dist, device)
+        assert torch.isfinite(coords).all(), "non-finite coordinates"
+    return {
+        "metric": "predictions/hour (sample-parallel diffusion sampler, one input per GPU)",
+        "value": round(comm.world * 3600e3 / ms, 2), "unit": "predictions/hour", "higher_is_better": True,
+        "n_gpus": comm.world, "scaling": "weak", "seconds_per_prediction": round(ms / 1e3, 3),
+        "workload": (f"{cfg['tokens']} tokens, {steps} EDM steps, multiplicity {mult}, {cfg['depth']}-layer token "
+                     f"transformer (c={cfg['c_token']}, {cfg['heads']} heads) on this package's diffusion kernels; "
+                     "coordinates of all inputs x samples gathered on every rank"),
+        "data": "synthetic (seeded trunk conditioning and weights)",
+    }
+
+
+def run_sharded(args):
+    """``--sharded``: the row-sharded block alone, as its own JSON line."""
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist_mod
+
+        dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        dist = dist_mod
+    n = args.n if args.n != N_TOKENS else 2048
+    clocks = ClockSampler(device)
+    clocks.wait_ready()
+    t0 = time.monotonic()
+    record = measure_sharded(n, args.steps, args.warmup, args.e2e_steps, dist, device)
+    clock_info = clocks.stop((t0, time.monotonic()))
     if rank == 0:
-        flops = 4.0 * n ** 3 * 4 * 32 * 2 + 2 * 2.0 * 128 * n ** 3 + 2.0 * n * n * (128 * 1024 + 512 * 128)
-        line = {
-            "metric": f"Pairformer ms/block at N={n} row-sharded bf16", "value": round(ms, 4), "unit": UNIT,
-            "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
-            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded N(0,1) inputs, N(0,1/128) weights)",
-            "config": {"workload": f"one Pairformer block N={n}, z rows split over {world} GPU(s) "
-                                   "(all_to_all row/column transposes, all_gather of planes and biases, NCCL)",
-                       "tokens": n, "rows_per_gpu": n_loc, "parallelism": f"row-sharded x{world}",
-                       "l2": "inputs larger than L2 (z slab >= 256 MiB fp32)"},
-            "e2e": {"value": round(e2e, 4), "unit": UNIT, "h2d_bytes_per_step": zr_pin.numel() * 4 + s_pin.numel() * 4,
-                    "d2h_bytes_per_step": zr_pin.numel() * 4 + s_pin.numel() * 4, "steps": args.e2e_steps},
-            "gpu_launches": launches,
-            "tensor_tflops_pair_ops": round(flops / (ms * 1e-3) / 1e12, 1),
-            "clocks": clock_info,
-            "cpu_baseline": None,
-        }
+        line = dict(record)
+        line.update({"vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) inputs, N(0,1/128) weights)",
+                     "config": {"workload": record.pop("workload"), "tokens": n, "parallelism": record["parallelism"],
+                                "l2": "inputs larger than L2 (z slab >= 256 MiB fp32)"},
+                     "clocks": clock_info, "cpu_baseline": None})
+        line.pop("workload", None)
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.destroy_process_group()
