@@ -43,6 +43,8 @@ struct LinArgs {
   int tiles_m, tiles_n;
   int splits, kb_per_split;  // cluster kernel: K blocks [rank * kb_per_split, ...) per CTA
   const float *bias;
+  const float *res;  // optional residual added to y (rows of ldr), may alias nothing else
+  int64_t ldr;
   float *y;
   int64_t ldy;
   unsigned int *status;
@@ -203,6 +205,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int c = c0 + j;
           out[j] = (__uint_as_float(r[j]) + __uint_as_float(rl[j])) +
                    (args.bias && c < args.n ? __ldg(args.bias + c) : 0.f);
+        }
+        if (args.res && row0 + lane < args.m) {  // y = x W^T + bias + residual (n % 4 == 0: whole float4s)
+          const float *rrow = args.res + int64_t(row0 + lane) * args.ldr + c0;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            if (c0 + j < args.n) {
+              const float4 rv = __ldg(reinterpret_cast<const float4 *>(rrow + j));
+              out[j] += rv.x, out[j + 1] += rv.y, out[j + 2] += rv.z, out[j + 3] += rv.w;
+            }
+          }
         }
         uint8_t *buf = staging + (count & 1) * kStagingBytes;
         if (lane == 0) tc::bulk_wait_read<1>();
@@ -401,6 +413,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int col = n0 + c, row = m0 + r;
       if (row < args.m && col < args.n) {
         if (args.bias) v.x += args.bias[col], v.y += args.bias[col + 1], v.z += args.bias[col + 2], v.w += args.bias[col + 3];
+        if (args.res) {
+          const float4 rv = __ldg(reinterpret_cast<const float4 *>(args.res + int64_t(row) * args.ldr + col));
+          v.x += rv.x, v.y += rv.y, v.z += rv.z, v.w += rv.w;
+        }
         *reinterpret_cast<float4 *>(args.y + int64_t(row) * args.ldy + col) = v;
       }
     }
@@ -504,13 +520,15 @@ extern "C" int bl_split3_bf16(const float *x, int64_t rows, int64_t cols, int64_
 }
 
 extern "C" int bl_linear_split3(const void *x3, int64_t m, int64_t k, const void *w3, int64_t n, const float *bias,
-                                float *y, int64_t ldy, void *stream) {
+                                const float *residual, int64_t ldr, float *y, int64_t ldy, void *stream) {
   BL_REQUIRE(m >= 0 && n >= 0 && k >= 0, "bl_linear_split3: bad shape");
   if (m == 0 || n == 0) return BL_OK;
   BL_REQUIRE(k > 0 && x3 && w3 && y, "bl_linear_split3: null pointer or k = 0");
   BL_REQUIRE(k % 8 == 0 && n % 4 == 0 && ldy % 4 == 0 && ldy >= n, "bl_linear_split3: k % 8, n % 4, ldy % 4 must be 0");
   BL_REQUIRE(aligned_to(x3, 16) && aligned_to(w3, 16) && aligned_to(y, 16),
              "bl_linear_split3: pointers must be 16-byte aligned");
+  BL_REQUIRE(!residual || (aligned_to(residual, 16) && ldr % 4 == 0 && ldr >= n),
+             "bl_linear_split3: residual must be 16-byte aligned with ldr % 4 == 0 and ldr >= n");
   BL_REQUIRE(m < (1ll << 31) && n < (1ll << 31) && k < (1ll << 31), "bl_linear_split3: shape too large");
   // Every CTA streams its tile's A and B rows through the whole K range, so
   // the critical path is (waves of work units) x (bytes one unit loads).
@@ -559,6 +577,7 @@ extern "C" int bl_linear_split3(const void *x3, int64_t m, int64_t k, const void
   args.m = int(m), args.n = int(n), args.k = int(k);
   args.tiles_m = int((m + kBM - 1) / kBM);
   args.bias = bias;
+  args.res = residual, args.ldr = ldr;
   args.y = y, args.ldy = ldy;
   args.splits = 1, args.kb_per_split = 0;
   args.status = device_status_ptr();

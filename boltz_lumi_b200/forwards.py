@@ -122,18 +122,22 @@ def _linear32(module, name, x, weights, biases=None, x3=None):
     return F.linear(x, w, bias)
 
 
-def _linear32_planes(module, name, x3, lead, weights, biases=None):
+def _linear32_planes(module, name, x3, lead, weights, biases=None, residual=None):
     """:func:`_linear32` on an input already in split form (x3 = bf16 [3, rows, K],
-    written by a fused producer); the output is fp32 [*lead, N]."""
+    written by a fused producer); the output is fp32 [*lead, N], plus ``residual``
+    (contiguous fp32 [*lead, N]) when given, added inside the kernel's epilogue."""
     w3, bias = _split_weight(module, name, weights, biases)
     n = w3.shape[1]
     if n % 4 == 0:
         y = torch.empty(*lead, n, device=x3.device, dtype=torch.float32)
-        kernels.linear_split3_fast(x3, w3, bias, y)
+        if residual is not None and (not residual.is_contiguous() or residual.dtype != torch.float32):
+            residual = residual.float().contiguous()
+        kernels.linear_split3_fast(x3, w3, bias, y, residual=residual)
         return y
     x = x3.float().sum(0).view(*lead, x3.shape[-1])  # exact to 2^-27 relative
     w = torch.cat(list(weights), 0) if len(weights) > 1 else weights[0]
-    return F.linear(x, w, bias)
+    y = F.linear(x, w, bias)
+    return y if residual is None else y + residual
 
 
 def _split_input(x):
@@ -498,7 +502,7 @@ def token_attention_supported(module, s, k_in, bias, mask=None):
             and all(p.bias is None for p in (module.proj_k, module.proj_v, module.proj_g)))
 
 
-def attend_with_bias(self, s, bias, mask, k_in, s3=None):
+def attend_with_bias(self, s, bias, mask, k_in, s3=None, residual=None):
     """Upstream attentionv2 ``AttentionPairBias`` after ``proj_z``: projections,
     fused fp32 attention with bias, key mask and sigmoid gate, then ``proj_o``.
 
@@ -506,7 +510,8 @@ def attend_with_bias(self, s, bias, mask, k_in, s3=None):
     ``b`` reads bias ``b // (B / B')``).  When ``k_in is s`` the four input
     projections run as one GEMM over stacked weights; ``s3`` may pass s
     already in split form (a fused producer wrote it), with ``s`` then only
-    giving the shape.
+    giving the shape.  With ``residual`` the result is ``residual + attention``
+    (the add runs in proj_o's epilogue).
     """
     if not token_attention_supported(self, s, k_in, bias, mask):
         raise RuntimeError(f"token attention covers fp32 CUDA s [B, N, H*d] with d in {_TOKEN_HEAD_DIMS}, "
@@ -515,13 +520,14 @@ def attend_with_bias(self, s, bias, mask, k_in, s3=None):
     heads, d, c = self.num_heads, self.head_dim, self.c_s
     if torch.is_autocast_enabled("cuda"):  # the reference's math is fp32 throughout
         with torch.autocast("cuda", enabled=False):
-            return attend_with_bias(self, s, bias, mask, k_in, s3=s3)
+            return attend_with_bias(self, s, bias, mask, k_in, s3=s3, residual=residual)
     if bias.dtype != torch.float32:
         bias = bias.float()
     if mask is not None and (mask.dtype != torch.float32 or mask.stride(-1) != 1):
         mask = mask.float().contiguous()
     if b == 0 or n == 0:
-        return self.proj_o(s.new_zeros(b, n, c))
+        out = self.proj_o(s.new_zeros(b, n, c))
+        return out if residual is None else out + residual
     out3 = torch.empty(3, b * n, c, device=s.device, dtype=torch.bfloat16)  # the output, as proj_o's operand
     stream = stream_of(s)
     if k_in is s:
@@ -543,7 +549,8 @@ def attend_with_bias(self, s, bias, mask, k_in, s3=None):
         g = _linear32(self, "_bl_w3_g", s, [self.proj_g.weight], x3=s3)
         kernels.launch_token_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), (n * c, c, d), bias,
                                        mask, self.inf, b, heads, n, d, None, stream, out3=out3)
-    return _linear32_planes(self, "_bl_w3_o", out3, (b, n), [self.proj_o.weight], [self.proj_o.bias])
+    return _linear32_planes(self, "_bl_w3_o", out3, (b, n), [self.proj_o.weight], [self.proj_o.bias],
+                            residual=residual)
 
 
 def token_attention_forward(self, s, z, mask, k_in, multiplicity=1):

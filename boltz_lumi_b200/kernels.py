@@ -320,13 +320,14 @@ def split3_fast(x):
     return out
 
 
-def linear_split3_fast(x3, w3, bias, y):
+def linear_split3_fast(x3, w3, bias, y, residual=None):
     """bl_linear_split3 into the contiguous fp32 ``y`` [..., N] for callers
-    that have checked the operands (x3 = split3(x), w3 = split3(W))."""
+    that have checked the operands (x3 = split3(x), w3 = split3(W)); with
+    ``residual`` (contiguous fp32 [..., N]) the result is y = x W^T + bias + residual."""
     m, k = x3.shape[1], x3.shape[2]
     n = w3.shape[1]
-    call("bl_linear_split3", x3.data_ptr(), m, k, w3.data_ptr(), n, ptr(bias), y.data_ptr(), n,
-         torch.cuda.current_stream().cuda_stream)
+    call("bl_linear_split3", x3.data_ptr(), m, k, w3.data_ptr(), n, ptr(bias), ptr(residual),
+         0 if residual is None else n, y.data_ptr(), n, torch.cuda.current_stream().cuda_stream)
     return y
 
 

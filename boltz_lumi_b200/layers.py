@@ -180,15 +180,18 @@ class AttentionPairBias(nn.Module):
             return forwards.token_attention_forward(self, s, z, mask, k_in, multiplicity)
         return self.attend(s, self.pair_bias(z), mask, k_in)
 
-    def attend(self, s, bias, mask, k_in):
-        """The attention given the pair bias [b', heads, N, N] (fp32, b' dividing b)."""
-        return forwards.attend_with_bias(self, s, bias, mask, k_in)
+    def attend(self, s, bias, mask, k_in, residual=None):
+        """The attention given the pair bias [b', heads, N, N] (fp32, b' dividing b), plus
+        ``residual`` when given (added in proj_o's epilogue)."""
+        return forwards.attend_with_bias(self, s, bias, mask, k_in, residual=residual)
 
 
 class _FP32Transition(Transition):
     """Single-track transition: upstream runs it in fp32 without autocast."""
 
-    def forward(self, x, chunk_size=None):
+    def forward(self, x, chunk_size=None, residual=None):
+        """fc3(silu(fc1(LN(x))) * fc2(LN(x))), plus ``residual`` when given (added in
+        fc3's epilogue: the block's s = s + transition_s(s) in one pass)."""
         _inference_only(self)
         cols, hidden = x.shape[-1], self.fc1.weight.shape[0]
         if cols % 128 == 0 and cols <= 1024 and hidden % 8 == 0:
@@ -198,12 +201,13 @@ class _FP32Transition(Transition):
             xn3 = kernels.layer_norm_split3(x, self.norm.weight, self.norm.bias, self.norm.eps)
             h = forwards._linear32_planes(self, "_bl_w3_fc12", xn3, lead, [self.fc1.weight, self.fc2.weight])
             h3 = kernels.epilogue_split3(h, None, None, kernels.SWIGLU)
-            return forwards._linear32_planes(self, "_bl_w3_fc3", h3, lead, [self.fc3.weight])
+            return forwards._linear32_planes(self, "_bl_w3_fc3", h3, lead, [self.fc3.weight], residual=residual)
         xn = kernels.layer_norm(x.contiguous(), self.norm.weight, self.norm.bias, self.norm.eps,
                                 out_dtype=torch.float32)
         h = forwards._linear32(self, "_bl_w3_fc12", xn, [self.fc1.weight, self.fc2.weight])
         a, b = h.split(hidden, dim=-1)
-        return forwards._linear32(self, "_bl_w3_fc3", F.silu(a) * b, [self.fc3.weight])
+        y = forwards._linear32(self, "_bl_w3_fc3", F.silu(a) * b, [self.fc3.weight])
+        return y if residual is None else y + residual
 
 
 class PairformerLayer(nn.Module):
@@ -236,10 +240,12 @@ class PairformerLayer(nn.Module):
         if s.shape[-1] % 128 == 0 and s.shape[-1] <= 1024:
             # LN(s) goes straight into the q | k | v | g projection's split operand.
             s3 = kernels.layer_norm_split3(s, self.pre_norm_s.weight, self.pre_norm_s.bias, self.pre_norm_s.eps)
-            s = s + forwards.attend_with_bias(att, s, att.pair_bias(z), mask, s, s3=s3)
+            # s + attention(...) and s + transition_s(s): the residual adds run in
+            # the epilogues of proj_o and fc3 (new tensors; the caller's s is unchanged).
+            s = forwards.attend_with_bias(att, s, att.pair_bias(z), mask, s, s3=s3, residual=s)
         else:
             s_normed = kernels.layer_norm(s, self.pre_norm_s.weight, self.pre_norm_s.bias, self.pre_norm_s.eps,
                                           out_dtype=torch.float32)
             s = s + att(s_normed, z, mask, s_normed)
-        s = s + self.transition_s(s)
+        s = self.transition_s(s, residual=s)
         return s, z

@@ -296,5 +296,5 @@ class ShardedPairformer:
         bias = _gather_rows(bias_loc.view(att.num_heads, n_loc, n), comm).unsqueeze(0)  # [1, H, N, N]
         s_normed = kernels.layer_norm(s.contiguous(), blk.pre_norm_s.weight, blk.pre_norm_s.bias,
                                       blk.pre_norm_s.eps, out_dtype=torch.float32)
-        s = s + att.attend(s_normed, bias, mask, s_normed)
-        return s + blk.transition_s(s)
+        s = att.attend(s_normed, bias, mask, s_normed, residual=s)
+        return blk.transition_s(s, residual=s)

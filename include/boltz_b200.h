@@ -322,14 +322,16 @@ BL_API int bl_token_attention(const float *q, const float *k, const float *v, co
  *   planes x3 [3][m][k] and w3 [3][n][k] (bl_split3_bf16 of x and of the fp32
  *   weight), keeping every cross product down to 2^-24 relative (error
  *   within 2^-17 of the largest output); y fp32 rows of ldy; k % 8 == 0,
- *   n % 4 == 0, ldy % 4 == 0, pointers 16-byte aligned; bias may be NULL.
+ *   n % 4 == 0, ldy % 4 == 0, pointers 16-byte aligned; bias may be NULL;
+ *   residual (fp32 rows of ldr, NULL for none) is added to y: the block's
+ *   s = s + proj_o(o) and s = s + fc3(h) without a separate add pass.
  * Replaces the fp32 linears the reference leaves to the BLAS: the diffusion
  * AdaLN / ConditionedTransitionBlock projections (diffusion.py:55-68) and the
  * AttentionPairBias projections (pair_bias.py:22-28, 36).
  */
 BL_API int bl_split3_bf16(const float *x, int64_t rows, int64_t cols, int64_t ldx, void *out, void *stream);
 BL_API int bl_linear_split3(const void *x3, int64_t m, int64_t k, const void *w3, int64_t n, const float *bias,
-                            float *y, int64_t ldy, void *stream);
+                            const float *residual, int64_t ldr, float *y, int64_t ldy, void *stream);
 
 /*
  * Producers of fp32-linear operands that write the three bf16 planes

@@ -122,3 +122,23 @@ def test_swiglu_epilogue():
         out = kernels.epilogue(h, None, None, kernels.SWIGLU)
         assert (out - ref).abs().max().item() <= 1e-6 * ref.abs().max().item()
         assert torch.equal(kernels.epilogue_split3(h, None, None, kernels.SWIGLU), kernels.split3(out))
+
+
+@pytest.mark.parametrize("m,n,k", [(117, 768, 768), (512, 384, 1536), (2000, 768, 768), (40, 100, 72)])
+def test_linear_with_residual(m, n, k):
+    """y = x W^T + bias + residual (the single track's s + proj_o(o) and s + fc3(h)) on both
+    the one-CTA tiles and the K-split cluster path; the residual is read, not modified."""
+    g = torch.Generator().manual_seed(m * 7 + n)
+    x = torch.randn(m, k, generator=g)
+    w = torch.randn(n, k, generator=g) * k ** -0.5
+    bias = torch.randn(n, generator=g)
+    res = torch.randn(m, n, generator=g) * 3
+    ref = x.double() @ w.double().T + bias.double() + res.double()
+    with torch.inference_mode():
+        rc = res.cuda()
+        keep = rc.clone()
+        y = torch.empty(m, n, device="cuda")
+        kernels.linear_split3_fast(kernels.split3(x.cuda()), kernels.split3(w.cuda()), bias.cuda(), y, residual=rc)
+    assert torch.equal(rc, keep)
+    err = (y.double().cpu() - ref).abs().max().item()
+    assert err <= 2.0 ** -17 * ref.abs().max().item() + 1e-6, err
