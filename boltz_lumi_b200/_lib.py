@@ -51,7 +51,7 @@ SIGNATURES = {
     "bl_split3_bf16": [_p, c_int64, c_int64, c_int64, _p, _p],
     "bl_linear_split3": [_p, c_int64, c_int64, _p, c_int64, _p, _p, c_int64, _p, c_int64, _p],
     "bl_token_attention": [_p, _p, _p, _p, c_int64, c_int64, c_int64, _p, c_int64, c_int64, c_int64, c_int64, c_int64,
-                           _p, c_int64, c_float, c_float, c_int64, c_int64, c_int64, c_int64, _p, _p, _p],
+                           _p, c_int64, c_float, c_float, c_int64, c_int64, c_int64, c_int64, c_int64, _p, _p, _p],
     "bl_layernorm_split3": [_p, c_int64, c_int64, _p, _p, c_float, _p, _p],
     "bl_adaln_modulate_split3": [_p, _p, _p, _p, c_int64, c_int64, c_float, _p],
     "bl_diffusion_epilogue_split3": [_p, _p, _p, _p, c_int64, c_int64, c_int, _p],

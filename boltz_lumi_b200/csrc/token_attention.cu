@@ -49,7 +49,8 @@ struct TokArgs {
   int64_t mask_sb;
   float scale, inf;
   int heads, n;
-  float *out;  // [B][N][H][d] contiguous, or null when out3 is set
+  int nq;      // queries per batch entry (rows of q / g / bias / out); n for self-attention
+  float *out;  // [B][nq][H][d] contiguous, or null when out3 is set
   __nv_bfloat16 *out3;  // [3][B * N][H * d] bf16 planes of the output, or null
   int batch;
   int split;  // CTAs per cluster sharing one query tile's key range (kSplit kernels)
@@ -92,7 +93,7 @@ __global__ void __launch_bounds__(kThreads, 2) token_attention_kernel(const TokA
   const int split = kSplit ? a.split : 1;
   const int rank = kSplit ? int(blockIdx.x) % split : 0;
   const int q0 = (kSplit ? int(blockIdx.x) / split : int(blockIdx.x)) * kBQ, h = blockIdx.y, b = blockIdx.z;
-  const int n = a.n;
+  const int n = a.n, nq = a.nq;
   const float *qb = a.q + b * a.sb + h * a.sh, *kb = a.k + b * a.sb + h * a.sh, *vb = a.v + b * a.sb + h * a.sh;
   const float *bias = a.bias + int64_t(b / a.bias_div) * a.bias_sb + h * a.bias_sh;
   const float *mask = a.mask ? a.mask + b * a.mask_sb : nullptr;
@@ -101,7 +102,7 @@ __global__ void __launch_bounds__(kThreads, 2) token_attention_kernel(const TokA
   constexpr int kChunks = D / 4;  // 16-byte chunks per row
   for (int i = t; i < kBQ * kChunks; i += kThreads) {
     const int r = i / kChunks, c = i % kChunks;
-    const bool ok = q0 + r < n;
+    const bool ok = q0 + r < nq;
     cp_async16(smem_u32(qs + r * kLd + 4 * c), qb + (ok ? int64_t(q0 + r) * a.si + 4 * c : 0), ok ? 16 : 0);
   }
   auto load_tile = [&](int tile, int buf) {
@@ -120,14 +121,14 @@ __global__ void __launch_bounds__(kThreads, 2) token_attention_kernel(const TokA
         const int r = i >> 4, c = 4 * (i & 15);
         const int qi = q0 + r, kj = k0 + c;
         const int left = n - kj;
-        const int bytes = qi < n ? (left >= 4 ? 16 : left > 0 ? 4 * left : 0) : 0;
+        const int bytes = qi < nq ? (left >= 4 ? 16 : left > 0 ? 4 * left : 0) : 0;
         cp_async16(smem_u32(bt + r * kPld + c), bias + (bytes ? int64_t(qi) * a.bias_sq + kj : 0), bytes);
       }
     } else {
 #pragma unroll 4
       for (int i = t; i < kBQ * kBK; i += kThreads) {
         const int r = i >> 6, c = i & 63;
-        const bool ok = q0 + r < n && k0 + c < n;
+        const bool ok = q0 + r < nq && k0 + c < n;
         cp_async4(smem_u32(bt + r * kPld + c),
                   bias + (ok ? int64_t(q0 + r) * a.bias_sq + int64_t(k0 + c) * a.bias_sk : 0), ok);
       }
@@ -290,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 2) token_attention_kernel(const TokA
       sum = fmaf(lp[p], w[p], sum);
     }
     const float inv = 1.f / sum;
-    const int64_t at0 = ((int64_t(b) * n + qi) * a.heads + h) * D;
+    const int64_t at0 = ((int64_t(b) * nq + qi) * a.heads + h) * D;
     const float *gr = a.g ? a.g + b * a.sb + h * a.sh + int64_t(qi) * a.si : nullptr;
     for (int d0 = part; d0 < D; d0 += 4 * tpr) {
       float acc[4] = {0.f, 0.f, 0.f, 0.f}, ov[4][4];
@@ -306,11 +307,11 @@ __global__ void __launch_bounds__(kThreads, 2) token_attention_kernel(const TokA
 #pragma unroll
         for (int p = 0; p < 4; ++p) acc[u] = fmaf(ov[u][p], w[p], acc[u]);
         const int d = d0 + u * tpr;
-        if (qi < n && d < D) {
+        if (qi < nq && d < D) {
           const float y = acc[u] * inv;
           const float out_v = gr ? y * (1.f / (1.f + expf(-gr[d]))) : y;
           if (a.out3)
-            store_split3_1(a.out3, int64_t(a.batch) * n * a.heads * D, at0 + d, out_v);
+            store_split3_1(a.out3, int64_t(a.batch) * nq * a.heads * D, at0 + d, out_v);
           else
             a.out[at0 + d] = out_v;
         }
@@ -323,9 +324,9 @@ __global__ void __launch_bounds__(kThreads, 2) token_attention_kernel(const TokA
 #pragma unroll
     for (int off = 1; off < 8; off <<= 1) l[i] += __shfl_xor_sync(0xffffffffu, l[i], off);
     const int qi = q0 + 4 * tq + i;
-    if (qi >= n) continue;
+    if (qi >= nq) continue;
     const float inv = 1.f / l[i];
-    const int64_t at = ((int64_t(b) * n + qi) * a.heads + h) * D + tk * kDpt;
+    const int64_t at = ((int64_t(b) * nq + qi) * a.heads + h) * D + tk * kDpt;
     float *dst = a.out + at;
     const float *gr = a.g ? a.g + b * a.sb + h * a.sh + int64_t(qi) * a.si + tk * kDpt : nullptr;
 #pragma unroll
@@ -333,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 2) token_attention_kernel(const TokA
       const float y = o[i][e] * inv;
       const float out_v = gr ? y * (1.f / (1.f + expf(-gr[e]))) : y;
       if (a.out3)
-        store_split3_1(a.out3, int64_t(a.batch) * n * a.heads * D, at + e, out_v);
+        store_split3_1(a.out3, int64_t(a.batch) * nq * a.heads * D, at + e, out_v);
       else
         dst[e] = out_v;
     }
@@ -344,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 2) token_attention_kernel(const TokA
 template <int D> int launch_token(TokArgs a, int batch, cudaStream_t stream) {
   constexpr int kLd = D + 4;
   const int smem = (kBQ * kLd + 4 * kBK * kLd + 2 * kBQ * kPld + 2 * kBK) * 4;
-  const int q_tiles = (a.n + kBQ - 1) / kBQ;
+  const int q_tiles = (a.nq + kBQ - 1) / kBQ;
   // Split the key range over a cluster when the grid would occupy at most
   // half of the SMs (measured on B200: 18 -> 15 us at 117 tokens, 25 -> 17 us
   // at 200-256 tokens, 16 heads; neutral at 96-128 CTAs, 4 % slower at 256).
@@ -386,10 +387,11 @@ extern "C" int bl_token_attention(const float *q, const float *k, const float *v
                                   int64_t si, int64_t sh,
                                   const float *bias, int64_t bias_sb, int64_t bias_sh, int64_t bias_sq,
                                   int64_t bias_sk, int64_t bias_batch_div, const float *mask, int64_t mask_sb,
-                                  float scale, float inf, int64_t batch, int64_t heads, int64_t n, int64_t head_dim,
-                                  float *out, void *out3, void *stream) {
-  BL_REQUIRE(batch >= 0 && heads > 0 && n >= 0, "bl_token_attention: bad shape");
-  if (batch == 0 || n == 0) return BL_OK;
+                                  float scale, float inf, int64_t batch, int64_t heads, int64_t n, int64_t n_q,
+                                  int64_t head_dim, float *out, void *out3, void *stream) {
+  if (n_q == 0) n_q = n;
+  BL_REQUIRE(batch >= 0 && heads > 0 && n >= 0 && n_q >= 0, "bl_token_attention: bad shape");
+  if (batch == 0 || n == 0 || n_q == 0) return BL_OK;
   BL_REQUIRE(head_dim == 24 || head_dim == 32 || head_dim == 48 || head_dim == 64,
              "bl_token_attention: head_dim 24, 32, 48 or 64");
   BL_REQUIRE(q && k && v && bias && (out || out3) && bias_batch_div >= 1, "bl_token_attention: null pointer");
@@ -397,7 +399,7 @@ extern "C" int bl_token_attention(const float *q, const float *k, const float *v
                  sh % 4 == 0 &&
                  sb % 4 == 0,
              "bl_token_attention: q/k/v rows must be 16-byte aligned");
-  BL_REQUIRE(n < (1 << 20) && heads < 65536 && batch < 65536, "bl_token_attention: shape too large");
+  BL_REQUIRE(n < (1 << 20) && n_q < (1 << 20) && heads < 65536 && batch < 65536, "bl_token_attention: shape too large");
   TokArgs a{};
   a.q = q, a.k = k, a.v = v, a.g = g, a.sb = sb, a.si = si, a.sh = sh;
   a.bias = bias, a.bias_sb = bias_sb, a.bias_sh = bias_sh, a.bias_sq = bias_sq, a.bias_sk = bias_sk;
@@ -406,7 +408,7 @@ extern "C" int bl_token_attention(const float *q, const float *k, const float *v
                aligned_to(bias, 16);
   a.mask = mask, a.mask_sb = mask_sb;
   a.scale = scale, a.inf = inf;
-  a.heads = int(heads), a.n = int(n);
+  a.heads = int(heads), a.n = int(n), a.nq = int(n_q);
   a.out = out, a.out3 = static_cast<__nv_bfloat16 *>(out3), a.batch = int(batch);
   cudaStream_t s = as_stream(stream);
   if (head_dim == 24) return launch_token<24>(a, int(batch), s);

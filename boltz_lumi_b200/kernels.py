@@ -237,16 +237,17 @@ def attention_scale(head_dim):
 
 
 def launch_token_attention(q_ptr, k_ptr, v_ptr, g_ptr, strides, bias, mask, inf, batch, heads, n, d, out, stream,
-                           out3=None):
+                           out3=None, n_q=0):
     """bl_token_attention on raw operand pointers sharing ``strides`` (batch,
     token, head) -- no validation; callers have checked shapes and dtypes.
-    With ``out3`` (bf16 [3, batch * n, heads * d]) the result is written as the
-    split planes instead of into ``out``."""
+    With ``out3`` (bf16 [3, batch * n_q, heads * d]) the result is written as the
+    split planes instead of into ``out``.  ``n_q`` (0: n) queries from q_ptr / g_ptr
+    and the bias rows attend over n keys."""
     mask_ptr, mask_sb = (None, 0) if mask is None else (mask.data_ptr(), mask.stride(0))
     bs = bias.stride()
     call("bl_token_attention", q_ptr, k_ptr, v_ptr, g_ptr, strides[0], strides[1], strides[2], bias.data_ptr(),
          bs[0], bs[1], bs[2], bs[3], batch // bias.shape[0], mask_ptr, mask_sb, attention_scale(d), float(inf),
-         batch, heads, n, d, ptr(out), ptr(out3), stream)
+         batch, heads, n, n_q, d, ptr(out), ptr(out3), stream)
     return out
 
 
@@ -289,7 +290,7 @@ def token_attention(q, k, v, bias, mask, inf, gate=None, scale=None):
         return out
     call("bl_token_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), ptr(gate), q.stride(0), q.stride(1),
          q.stride(2), bias.data_ptr(), bias.stride(0), bias.stride(1), bias.stride(2), bias.stride(3),
-         batch // bias.shape[0], ptr(mask), mask_sb, float(scale), float(inf), batch, heads, n, d, out.data_ptr(),
+         batch // bias.shape[0], ptr(mask), mask_sb, float(scale), float(inf), batch, heads, n, 0, d, out.data_ptr(),
          None, stream_of(q))
     return out
 

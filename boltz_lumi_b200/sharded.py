@@ -15,8 +15,10 @@ the single-GPU path on its slab, with the exchanges the op needs:
 * TriangleAttentionEndingNode: the starting form on z^T (column layout), as
   upstream runs it (triangle.py:131 transposes the pair axes).
 * Transition: pointwise per pair row, no exchange.
-* Single track: the pair bias LN(z) W_z is computed per row block and
-  all-gathered; the s update is replicated on every rank.
+* Single track: sharded by query rows.  The pair bias rows of a rank's own
+  queries are local (its z rows); each rank attends with its queries over all
+  tokens, applies proj_o and transition_s to its rows, and one all_gather of
+  the updated s rows (N x c_s fp32) rebuilds s on every rank.
 
 Layout changes row <-> column are one all_to_all of the slab (each rank keeps
 1/P and sends (P - 1)/P of it) plus a local block transpose.  The collectives
@@ -283,18 +285,43 @@ class ShardedPairformer:
     __call__ = forward
 
     def _single_track(self, s, z_rows, mask):
-        """s += AttentionPairBias(LN(s), z) ; s += Transition(s): the pair bias
-        is computed per row block and gathered, the rest is replicated."""
+        """s += AttentionPairBias(LN(s), z); s += Transition(s), sharded by query rows.
+
+        Rank r holds z rows I_r, so the pair bias rows bias[h, i, :] for its own queries
+        i in I_r are local (bl_pair_bias on the slab).  LN(s) and the q | k | v | g
+        projection run for all tokens (replicated; small next to the pair ops), the
+        attention of the n_loc local queries against all N keys reads q / g at the local
+        rows (bl_token_attention with n_q = n_loc), proj_o adds the residual s[I_r], and
+        transition_s runs on the local rows.  One all_gather of the updated s rows
+        (N x c_s fp32) then gives every rank the full s: the [H, N, N] fp32 bias is never
+        gathered and the attention is not replicated."""
         blk, comm = self.block, self.comm
         att = blk.attention
         n_loc, n = z_rows.shape[0], z_rows.shape[1]
+        r0 = comm.rank * n_loc
+        heads, d = att.num_heads, att.head_dim
+        s = s.contiguous()
+        c = s.shape[-1]
+        if (d not in forwards._TOKEN_HEAD_DIMS or heads * d != c or s.dtype != torch.float32 or c % 128 or c > 1024
+                or any(lyr.bias is not None for lyr in (att.proj_k, att.proj_v, att.proj_g))):
+            raise RuntimeError("the sharded single track needs fp32 s [1, N, H*d] with d in (24, 32, 48, 64)")
         ln, lin = att.proj_z[0], att.proj_z[1]
         w_z = lin.weight.float().contiguous()
-        bias_loc = torch.empty(att.num_heads, n_loc * n, device=z_rows.device, dtype=torch.float32)
+        stream = stream_of(z_rows)
+        bias_loc = torch.empty(1, heads, n_loc, n, device=z_rows.device, dtype=torch.float32)
         call("bl_pair_bias", z_rows.data_ptr(), n_loc * n, _lib.ptr(ln.weight), _lib.ptr(ln.bias), float(ln.eps),
-             w_z.data_ptr(), att.num_heads, bias_loc.data_ptr(), stream_of(z_rows))
-        bias = _gather_rows(bias_loc.view(att.num_heads, n_loc, n), comm).unsqueeze(0)  # [1, H, N, N]
-        s_normed = kernels.layer_norm(s.contiguous(), blk.pre_norm_s.weight, blk.pre_norm_s.bias,
-                                      blk.pre_norm_s.eps, out_dtype=torch.float32)
-        s = att.attend(s_normed, bias, mask, s_normed, residual=s)
-        return blk.transition_s(s, residual=s)
+             w_z.data_ptr(), heads, bias_loc.data_ptr(), stream)
+        s3 = kernels.layer_norm_split3(s, blk.pre_norm_s.weight, blk.pre_norm_s.bias, blk.pre_norm_s.eps)
+        proj = forwards._linear32_planes(att, "_bl_w3_qkvg", s3, (1, n),
+                                         [att.proj_q.weight, att.proj_k.weight, att.proj_v.weight, att.proj_g.weight],
+                                         [att.proj_q.bias, None, None, None])  # [1, N, 4c]: q | k | v | g
+        base, row = proj.data_ptr(), 4 * c * 4
+        out3 = torch.empty(3, n_loc, c, device=s.device, dtype=torch.bfloat16)
+        maskf = None if mask is None else mask.float().contiguous()
+        kernels.launch_token_attention(base + r0 * row, base + c * 4, base + 2 * c * 4, base + r0 * row + 3 * c * 4,
+                                       (n * 4 * c, 4 * c, d), bias_loc, maskf, att.inf, 1, heads, n, d, None,
+                                       stream, out3=out3, n_q=n_loc)
+        s_loc = forwards._linear32_planes(att, "_bl_w3_o", out3, (n_loc,), [att.proj_o.weight], [att.proj_o.bias],
+                                          residual=s[0, r0:r0 + n_loc].contiguous())
+        s_loc = blk.transition_s(s_loc, residual=s_loc)
+        return comm.all_gather(s_loc).reshape(1, n, c)

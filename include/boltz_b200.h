@@ -300,18 +300,21 @@ BL_API int bl_triangle_attention(const void *q, const void *k, const void *v, co
  * prepared [B, L*H, N, N] token bias is passed without a copy and one bias
  * row serves the bias_batch_div diffusion samples of its input; mask: fp32
  * at b*mask_sb + j, or NULL for none; head_dim 24, 32, 48 or 64; out: fp32
- * [batch][n][heads][head_dim] contiguous.  Replaces the einsum / bias / mask /
- * softmax / einsum and the gate product of pair_bias.py:28-36 (prepared_forward).
+ * [batch][n_q][heads][head_dim] contiguous.  n_q queries (rows of q, g, bias and
+ * out; 0 means n) attend over the n keys: a rank of the row-sharded block passes
+ * its own query rows (pointers offset to them) against all keys.  Replaces the
+ * einsum / bias / mask / softmax / einsum and the gate product of
+ * pair_bias.py:28-36 (prepared_forward).
  * With out3 != NULL the result is written instead as three bf16 planes
- * [3][batch * n][heads * head_dim] (the operand form of bl_linear_split3,
+ * [3][batch * n_q][heads * head_dim] (the operand form of bl_linear_split3,
  * for proj_o) and out may be NULL.
  */
 BL_API int bl_token_attention(const float *q, const float *k, const float *v, const float *g, int64_t sb,
                               int64_t si, int64_t sh,
                               const float *bias, int64_t bias_sb, int64_t bias_sh, int64_t bias_sq,
                               int64_t bias_sk, int64_t bias_batch_div, const float *mask, int64_t mask_sb,
-                              float scale, float inf, int64_t batch, int64_t heads, int64_t n, int64_t head_dim,
-                              float *out, void *out3, void *stream);
+                              float scale, float inf, int64_t batch, int64_t heads, int64_t n, int64_t n_q,
+                              int64_t head_dim, float *out, void *out3, void *stream);
 
 /*
  * fp32-accurate linear layers on the bf16 tensor cores (three-way split).

@@ -109,3 +109,74 @@ def test_thread_ranks_equal_single_process(world):
     for out in results:
         assert_close(out, expected, atol=1e-3, rtol=1e-4)
     assert (expected[0, 0] - expected[0, 1]).abs().max() > 0.1  # independent samples
+
+
+def _nccl_rank(rank, world, port, results):
+    import datetime
+    import os
+
+    import torch.distributed as dist
+
+    from boltz_lumi_b200 import sampling
+    from boltz_lumi_b200.sharded import TorchComm
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    device = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=device)
+    try:
+        model = sampling.seeded_model(depth=DEPTH, c_token=C, heads=HEADS, c_s=C_S, seed=3, device=device)
+        s_trunk, bias, mask = sampling.synthetic_conditioning(N, DEPTH, HEADS, C_S, seed=4, device=device)
+        sampler = sampling.EDMSampler(steps=6)
+        with torch.inference_mode():
+            s_base = model.conditioning(s_trunk)
+
+            def run(i, samples, gens):
+                return sampler.sample(lambda x, sig: model(x, sig, s_base, bias, mask), N, gens, device)
+
+            out = sampling.distributed_sample(run, 2, 3, N, 5, TorchComm(), device)
+        results[rank] = out.cpu()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_sampler_nccl_two_gpus_equals_one():
+    """Two ranks over NCCL (each runs its units, one all_gather) give every rank the same
+    coordinates as one process running all units."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as sock:
+        sock.bind(("127.0.0.1", 0))
+        port = sock.getsockname()[1]
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    mp.start_processes(_nccl_rank, args=(2, port, results), nprocs=2, start_method="spawn", join=True)
+    model, s_trunk, bias, mask = _model_and_inputs()
+    mask[:, -3:] = 1  # the ranks above use the unmasked conditioning
+    with torch.inference_mode():
+        sampler = sampling.EDMSampler(steps=6)
+        s_base = model.conditioning(s_trunk)
+
+        def run(i, samples, gens):
+            return sampler.sample(lambda x, sig: model(x, sig, s_base, bias, mask), N, gens, "cuda")
+
+        expected = sampling.distributed_sample(run, 2, 3, N, 5, SingleComm(), "cuda").cpu()
+    for rank in range(2):
+        assert_close(results[rank], expected, atol=1e-3, rtol=1e-4)
+
+
+def test_graphed_denoiser_equals_eager():
+    """make_denoiser(cuda_graphs=True) replays the score model from a CUDA graph from its
+    third call on; the sampled coordinates equal the eager denoiser's."""
+    model, s_trunk, bias, mask = _model_and_inputs()
+    with torch.inference_mode():
+        outs = []
+        for graphed in (False, True):
+            gens = [torch.Generator(device="cuda").manual_seed(10 + m) for m in range(3)]
+            denoise = sampling.make_denoiser(model, s_trunk, bias, mask, cuda_graphs=graphed)
+            outs.append(sampling.EDMSampler(steps=6).sample(denoise, N, gens, "cuda"))
+    assert_close(outs[1], outs[0], atol=1e-4, rtol=1e-5)

@@ -185,3 +185,26 @@ def test_installed_model_matches_upstream():
     adapters.uninstall(model)
     assert "sample" not in model.structure_module.__dict__
     assert (out - ref).abs().max().item() <= 2 * TOL
+
+
+@pytest.mark.parametrize("n,r0,nq,heads,d", [(256, 64, 64, 16, 24), (512, 128, 128, 16, 24), (200, 0, 100, 8, 48),
+                                             (130, 65, 65, 4, 32)])
+def test_query_rows_subset(n, r0, nq, heads, d):
+    """n_q < n: the queries r0 .. r0 + n_q (q / g pointers and bias rows offset to them) over
+    all n keys, as a rank of the row-sharded block runs its own query rows; equal to the
+    same rows of the full attention."""
+    gen = torch.Generator().manual_seed(n + nq)
+    q, k, v, g = (torch.randn(1, n, heads, d, generator=gen).cuda() for _ in range(4))
+    bias = torch.randn(1, heads, n, n, generator=gen).cuda()
+    mask = _mask(1, n, gen)
+    with torch.inference_mode():
+        full = kernels.token_attention(q, k, v, bias, mask, 1e6, gate=g)
+        bias_rows = bias[:, :, r0:r0 + nq].contiguous()
+        out = torch.empty(1, nq, heads, d, device="cuda")
+        row = q.stride(1) * 4
+        kernels.launch_token_attention(q.data_ptr() + r0 * row, k.data_ptr(), v.data_ptr(), g.data_ptr() + r0 * row,
+                                       (q.stride(0), q.stride(1), q.stride(2)), bias_rows, mask, 1e6, 1, heads, n, d,
+                                       out, torch.cuda.current_stream().cuda_stream, n_q=nq)
+    expected = _reference_core(q, k, v, bias, mask, 1e6)[:, r0:r0 + nq] * torch.sigmoid(g[:, r0:r0 + nq])
+    assert (out - expected).abs().max().item() <= TOL
+    assert (out - full[:, r0:r0 + nq]).abs().max().item() <= 1e-5
