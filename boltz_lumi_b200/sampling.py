@@ -8,9 +8,11 @@ otherwise independent, and so are different inputs.  This module spreads the
 work units (input i, sample m) over the ranks with no collective inside the
 loop:
 
-* :func:`shard_units` deals the units round robin over the ranks; a rank runs
-  the samples of its units input by input, each input's samples as one
-  batch (its local multiplicity);
+* :func:`shard_units` gives each rank a contiguous block of units (in
+  input-major order), so with one input per rank every rank runs all samples
+  of its input as one batch, and with fewer inputs than ranks an input's
+  samples spread over several ranks; a rank runs its units input by input,
+  each input's samples as one batch (its local multiplicity);
 * every sample draws all of its noise from its own generator, seeded by
   :func:`sample_seed` from (seed, input, sample), so the coordinates do not
   depend on the number of ranks or on which rank ran the sample;
@@ -48,13 +50,20 @@ __all__ = ["shard_units", "sample_seed", "distributed_sample", "sample_upstream"
 # ---------------------------------------------------------------------------
 # Partition and gather
 # ---------------------------------------------------------------------------
+def unit_range(n_units, world, rank):
+    """Units [begin, end) of ``rank``: contiguous blocks whose sizes differ by at most one."""
+    return rank * n_units // world, (rank + 1) * n_units // world
+
+
 def shard_units(n_inputs, multiplicity, world, rank):
-    """The (input, sample) units of ``rank``: unit u = input * multiplicity + sample is
-    owned by rank u % world.  Returns {input: [samples]} in increasing order."""
+    """The (input, sample) units of ``rank``: unit u = input * multiplicity + sample, the
+    ranks owning contiguous blocks of units (:func:`unit_range`).  Returns
+    {input: [samples]} in increasing order."""
     if world < 1 or not 0 <= rank < world:
         raise ValueError(f"bad rank {rank} of world {world}")
     owned = {}
-    for unit in range(rank, n_inputs * multiplicity, world):
+    begin, end = unit_range(n_inputs * multiplicity, world, rank)
+    for unit in range(begin, end):
         owned.setdefault(unit // multiplicity, []).append(unit % multiplicity)
     return owned
 
@@ -93,8 +102,8 @@ def distributed_sample(run_samples, n_inputs, multiplicity, atoms, seed, comm, d
     gathered = comm.all_gather(local)  # [world, per_rank, atoms, 3]
     out = torch.empty(units, atoms, 3, device=device, dtype=torch.float32)
     for r in range(world):
-        mine = list(range(r, units, world))
-        out[mine] = gathered[r, :len(mine)]
+        begin, end = unit_range(units, world, r)
+        out[begin:end] = gathered[r, :end - begin]
     return out.view(n_inputs, multiplicity, atoms, 3)
 
 

@@ -103,3 +103,16 @@ def test_gloo_world2_equals_single_process():
     mp.start_processes(_gloo_rank, args=(2, port, results), nprocs=2, start_method="spawn", join=True)
     expected = _reference(2, 5)
     assert torch.equal(results[0], expected) and torch.equal(results[1], expected)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_one_input_per_rank_runs_as_one_batch(world):
+    """With as many inputs as ranks, rank r owns exactly input r's samples (one batch)."""
+    for rank in range(world):
+        assert shard_units(world, 5, world, rank) == {rank: [0, 1, 2, 3, 4]}
+
+
+def test_fewer_inputs_than_ranks_spread_samples():
+    owned = [shard_units(1, 5, 8, r) for r in range(8)]
+    assert sum(len(o.get(0, [])) for o in owned) == 5
+    assert max(len(o.get(0, [])) for o in owned) == 1
