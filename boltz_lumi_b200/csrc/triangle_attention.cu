@@ -31,6 +31,14 @@
 //     2^8, so P stays <= 256 and rescales are rare;
 //   * Q, K, V and the bias tiles arrive by TMA through a 4-deep ring (3-D
 //     maps carry the starting/ending-node strides); no multicast.
+//   * when the grid still fills the GPU several times over (N >= ~300 at
+//     one outer row per CTA row), one CTA runs two or four heads of its
+//     (outer row, query tile) back to back: the setup (barriers, TMEM), the
+//     mask pass and the key ring are shared, the next head's Q and first key
+//     tiles load while the previous head finishes, and only its epilogue sits
+//     between two heads (the first P.V of a head waits until the previous
+//     head's O has been read).  Measured at N = 512: 288 -> 268 us per launch
+//     (starting node), bitwise-identical output.
 // Warp roles: warp 0 TMA producer, warp 1 TMEM allocation + MMA issue, warps
 // 2..9 softmax and epilogue (TMEM lane quarter = warp % 4; warps 2..5 take key
 // half 0, warps 6..9 key half 1).
@@ -80,6 +88,7 @@ struct TcArgs {
   __nv_bfloat16 *out;
   int64_t out_ld;
   int n;
+  int heads_per_cta;  // 2 or 4 heads run back to back by one CTA (the kMulti kernel)
   unsigned int *status;
 };
 
@@ -141,6 +150,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, unsign
   return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, status, code));
 }
 
+template <bool kMulti>
 __global__ void __launch_bounds__(kThreads, 2)
     tri_flash_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_bias,
@@ -149,28 +159,32 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t smem_base = tc::smem_u32(smem);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBarOff);
-  uint64_t *q_full = bars + 0;
+  uint64_t *q_full = bars + 0;               // Q of the current head landed (one phase per head)
+  uint64_t *q_empty = bars + 1;              // every S MMA of a head completed: Q may be replaced
   uint64_t *st_full = bars + 2;              // [kStages] K, V, bias of a key tile landed
   uint64_t *st_empty = bars + 2 + kStages;   // [kStages] P.V of that tile completed
   uint64_t *s_full = bars + 2 + 2 * kStages; // [2] S tile in TMEM
   uint64_t *p_full = s_full + 2;             // [2] P tile in TMEM (and O rescaled if needed)
   uint64_t *pv_done = p_full + 2;            // [2] P.V reading TMEM buffer b completed
-  uint64_t *o_full = pv_done + 2;            // all P.V done
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(o_full + 1);
-  float *row_max = reinterpret_cast<float *>(smem + kMaxOff);
+  uint64_t *o_full = pv_done + 2;            // every P.V of a head done (one phase per head)
+  uint64_t *o_free = o_full + 1;             // the softmax warps have read O (one phase per head)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(o_free + 1);
+  float *row_max = reinterpret_cast<float *>(smem + kMaxOff);  // [2 heads parity][2 halves][128]
   int *tile_masked = reinterpret_cast<int *>(smem + kFlagOff);
   __nv_bfloat16 *mask_bias = reinterpret_cast<__nv_bfloat16 *>(smem + kMaskOff);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n = args.n;
-  const int h = blockIdx.x % kHeads;
-  const int q0 = (blockIdx.x / kHeads) * kBQ;
+  const int hpc = kMulti ? args.heads_per_cta : 1, groups = kHeads / hpc;
+  const int h_begin = (blockIdx.x % groups) * hpc;
+  const int q0 = (blockIdx.x / groups) * kBQ;
   const int outer = blockIdx.y;
   const int n_tiles = (n + kBK - 1) / kBK;
 
   if (tid < kMaxTiles) tile_masked[tid] = 0;
   if (tid == 0) {
     tc::mbar_init(q_full, 1);
+    tc::mbar_init(q_empty, 1);
     for (int s = 0; s < kStages; ++s) {
       tc::mbar_init(&st_full[s], 1);
       tc::mbar_init(&st_empty[s], 1);
@@ -181,6 +195,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc::mbar_init(&pv_done[b], 1);
     }
     tc::mbar_init(o_full, 1);
+    tc::mbar_init(o_free, kSoftmaxWarps);
     tc::fence_mbar_init();
   }
   // Ones block read as V's second N block (its swizzle is irrelevant: every element is 1).
@@ -198,22 +213,30 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer: the four heads back to back ----------------
     if (lane == 0) {
       tc::prefetch_tmap(&map_q);
       tc::prefetch_tmap(&map_k);
       tc::prefetch_tmap(&map_v);
       tc::prefetch_tmap(&map_bias);
-      tc::mbar_arrive_expect_tx(q_full, kBQ * kD * 2);
-      tc::tma_load_3d(smem + kQOff, &map_q, q_full, h * kD, q0, outer);
-      for (int j = 0; j < n_tiles; ++j) {
-        const int s = j % kStages;
-        if (j >= kStages && !tc::mbar_wait(&st_empty[s], ((j / kStages) & 1) ^ 1u, args.status, 0x201)) break;
-        uint8_t *stage = smem + kStageOff + s * kStageBytes;
-        tc::mbar_arrive_expect_tx(&st_full[s], kStageBytes);
-        tc::tma_load_3d(stage, &map_k, &st_full[s], h * kD, j * kBK, outer);
-        tc::tma_load_3d(stage + kKBytes, &map_v, &st_full[s], h * kD, j * kBK, outer);
-        tc::tma_load_3d(stage + kKBytes + kVBytes, &map_bias, &st_full[s], j * kBK, q0, h);
+      bool ok = true;
+      int g = 0;  // key tiles issued so far over all heads (ring position)
+#pragma unroll 1
+      for (int hl = 0; hl < hpc && ok; ++hl) {
+        const int h = h_begin + hl;
+        // Q of head h replaces Q of the previous head once its last S MMA has completed.
+        if (hl > 0 && !(ok = tc::mbar_wait(q_empty, (hl - 1) & 1, args.status, 0x20B))) break;
+        tc::mbar_arrive_expect_tx(q_full, kBQ * kD * 2);
+        tc::tma_load_3d(smem + kQOff, &map_q, q_full, h * kD, q0, outer);
+        for (int j = 0; j < n_tiles; ++j, ++g) {
+          const int s = g % kStages;
+          if (g >= kStages && !(ok = tc::mbar_wait(&st_empty[s], ((g / kStages) & 1) ^ 1u, args.status, 0x201))) break;
+          uint8_t *stage = smem + kStageOff + s * kStageBytes;
+          tc::mbar_arrive_expect_tx(&st_full[s], kStageBytes);
+          tc::tma_load_3d(stage, &map_k, &st_full[s], h * kD, j * kBK, outer);
+          tc::tma_load_3d(stage + kKBytes, &map_v, &st_full[s], h * kD, j * kBK, outer);
+          tc::tma_load_3d(stage + kKBytes + kVBytes, &map_bias, &st_full[s], j * kBK, q0, h);
+        }
       }
     }
   } else if (warp == 1) {
@@ -223,12 +246,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       constexpr uint32_t idesc_pv = tc::idesc_bf16(128, 48, false, true);
       const uint32_t q_addr = tc::smem_u32(smem + kQOff);
       const uint32_t ones_addr = tc::smem_u32(smem + kOnesOff);
-      bool ok = tc::mbar_wait(q_full, 0, args.status, 0x202);
-      auto issue_s = [&](int j) {
-        const int s = j % kStages, b = j & 1;
-        if (!tc::mbar_wait(&st_full[s], (j / kStages) & 1, args.status, 0x203)) return false;
-        // TMEM buffer b still holds P of tile j - 2: its P.V must have finished reading it.
-        if (j >= 2 && !tc::mbar_wait(&pv_done[b], ((j - 2) >> 1) & 1, args.status, 0x204)) return false;
+      // S of global tile g (head g / n_tiles) into TMEM buffer g & 1.
+      auto issue_s = [&](int g) {
+        const int s = g % kStages, b = g & 1;
+        if (!tc::mbar_wait(&st_full[s], (g / kStages) & 1, args.status, 0x203)) return false;
+        // TMEM buffer b still holds P of tile g - 2: its P.V must have finished reading it.
+        if (g >= 2 && !tc::mbar_wait(&pv_done[b], ((g - 2) >> 1) & 1, args.status, 0x204)) return false;
         tc::tc_fence_after();
         const uint32_t k_addr = tc::smem_u32(smem + kStageOff + s * kStageBytes);
 #pragma unroll
@@ -238,41 +261,52 @@ __global__ void __launch_bounds__(kThreads, 2)
         tc::umma_commit(&s_full[b]);
         return true;
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
-        const int s = j % kStages, b = j & 1;
-        if (!tc::mbar_wait(&p_full[b], (j >> 1) & 1, args.status, 0x205)) break;
+      bool ok = true;
+      int g = 0;
+#pragma unroll 1
+      for (int hl = 0; hl < hpc && ok; ++hl) {
+        if (!(ok = tc::mbar_wait(q_full, hl & 1, args.status, 0x202))) break;
         tc::tc_fence_after();
-        const uint32_t v_addr = tc::smem_u32(smem + kStageOff + s * kStageBytes + kKBytes);
-        const uint32_t lbo = ones_addr - v_addr;
+        if (!(ok = issue_s(g))) break;
+        if (kMulti && n_tiles == 1) tc::umma_commit(q_empty);
+        for (int j = 0; j < n_tiles; ++j, ++g) {
+          if (j + 1 < n_tiles) {
+            if (!(ok = issue_s(g + 1))) break;
+            if (kMulti && j + 2 == n_tiles) tc::umma_commit(q_empty);  // the head's last S MMA: Q may be replaced
+          }
+          const int s = g % kStages, b = g & 1;
+          if (!(ok = tc::mbar_wait(&p_full[b], (g >> 1) & 1, args.status, 0x205))) break;
+          // The first P.V of a head overwrites O: the previous head's O must have been read.
+          if (j == 0 && hl > 0 && !(ok = tc::mbar_wait(o_free, (hl - 1) & 1, args.status, 0x20C))) break;
+          tc::tc_fence_after();
+          const uint32_t v_addr = tc::smem_u32(smem + kStageOff + s * kStageBytes + kKBytes);
+          const uint32_t lbo = ones_addr - v_addr;
 #pragma unroll
-        for (int half = 0; half < 2; ++half)
+          for (int half = 0; half < 2; ++half)
 #pragma unroll
-          for (int kk = 0; kk < 2; ++kk)
-            tc::umma_f16_ts(tmem + kOCol + half * kOStride, tmem + uint32_t(b * kBK + half * 32 + kk * 8),
-                            desc_sw64(v_addr + (half * 2 + kk) * 1024, lbo), idesc_pv, (j | kk) != 0);
-        tc::umma_commit(&st_empty[s]);
-        tc::umma_commit(&pv_done[b]);
-        if (j + 1 == n_tiles) tc::umma_commit(o_full);
+            for (int kk = 0; kk < 2; ++kk)
+              tc::umma_f16_ts(tmem + kOCol + half * kOStride, tmem + uint32_t(b * kBK + half * 32 + kk * 8),
+                              desc_sw64(v_addr + (half * 2 + kk) * 1024, lbo), idesc_pv, (j | kk) != 0);
+          tc::umma_commit(&st_empty[s]);
+          tc::umma_commit(&pv_done[b]);
+          if (j + 1 == n_tiles) tc::umma_commit(o_full);
+        }
       }
     }
   } else {
-    // ---------------- softmax + epilogue: half a query row per thread ----------------
+    // ---------------- softmax + epilogue: half a query row per thread, four heads ----------------
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
     const uint32_t o_base = lane_base + kOCol + half * kOStride;
-    // The gate rows this thread's epilogue applies go to L2 now.
-    if (q0 + row < n) {
-      const int64_t pair = int64_t(outer) * args.so + int64_t(q0 + row) * args.si;
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(args.g + pair * args.ld + h * kD + half * 16));
-    }
-    // Mask bias of this outer row, 4 keys per thread (bf16; for mask in {0,
-    // 1} adding it rounds exactly like the fp32 value), and per-tile "any key
-    // masked" flags.  Only the softmax warps read them, so the TMA and MMA
-    // warps start without waiting for this pass.
+    const int qi = q0 + row;
+    const int64_t pair = int64_t(outer) * args.so + int64_t(qi) * args.si;
+    // The gate rows of all four heads (256 contiguous bytes of the pair row) go to L2 now.
+    if (qi < n) asm volatile("prefetch.global.L2 [%0];" ::"l"(args.g + pair * args.ld + half * 64));
+    // Mask bias of this outer row (shared by the four heads), 4 keys per
+    // thread (bf16; for mask in {0, 1} adding it rounds exactly like the fp32
+    // value), and per-tile "any key masked" flags.
     const float *mrow = args.mask + int64_t(outer) * args.ms_o;
     for (int k4 = (tid - 64) * 4; k4 < n_tiles * kBK; k4 += kSoftmaxWarps * 32 * 4) {
       float mb[4];
@@ -285,140 +319,138 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (mb[0] != 0.f || mb[1] != 0.f || mb[2] != 0.f || mb[3] != 0.f) atomicOr(&tile_masked[k4 / kBK], 1);
     }
     asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxWarps * 32) : "memory");
-    float m_ref = -INFINITY;  // reference maximum of this half-row's exponentials
     bool ok = true;
-    for (int j = 0; j < n_tiles && ok; ++j) {
-      const int s = j % kStages, b = j & 1;
-      if (!(ok = warp_wait(&s_full[b], (j >> 1) & 1, args.status, 0x206))) break;
-      tc::tc_fence_after();
-      uint32_t sv[32];
-      tc::tmem_ld_32x32b_x32(lane_base + b * kBK + half * 32, sv);
-      if (!(ok = warp_wait(&st_full[s], (j / kStages) & 1, args.status, 0x207))) {
-        tc::tmem_ld_wait();
-        break;
-      }
-
-      // Ordered rounding: t = bf16(bf16(bf16(s) + mask) + bias), packed per key pair.
-      // The bias chunks and the tile's mask flag are read from shared memory
-      // while the S load from TMEM is still in flight.
-      const int k0 = j * kBK + half * 32;
-      const uint32_t bias_row = smem_base + kStageOff + s * kStageBytes + kKBytes + kVBytes + row * 128;
-      // 16-byte bias chunk c = keys 8c .. 8c + 7 of this half (128-byte swizzled row).
-      uint32_t bw[16];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint4 bv = lds128(bias_row + (((half * 4 + c) ^ (row & 7)) << 4));
-        bw[4 * c] = bv.x, bw[4 * c + 1] = bv.y, bw[4 * c + 2] = bv.z, bw[4 * c + 3] = bv.w;
-      }
-      const bool tile_unmasked = lds32(smem_base + kFlagOff + 4 * j) == 0;
-      tc::tmem_ld_wait_regs(sv);
-      // The mask term is uniform per key tile: two straight-line versions
-      // (a per-pair branch would split the unrolled block).
-      uint32_t t[16];
-      if (tile_unmasked) {
-#pragma unroll
-        for (int pr = 0; pr < 16; ++pr)
-          t[pr] = add_bf16x2(cvt_bf16x2(__uint_as_float(sv[2 * pr]), __uint_as_float(sv[2 * pr + 1])), bw[pr]);
-      } else {
+    int g = 0;
+    // Every softmax warp runs the epilogue (and its named barrier) of every head,
+    // even after a bounded wait gave up (ok = false: the work is skipped), so the
+    // barrier counts always match.
+#pragma unroll 1
+    for (int hl = 0; hl < hpc; ++hl) {
+      const int h = h_begin + hl;
+      float m_ref = -INFINITY;  // reference maximum of this half-row's exponentials
+      for (int j = 0; j < n_tiles && ok; ++j, ++g) {
+        const int s = g % kStages, b = g & 1;
+        if (!(ok = warp_wait(&s_full[b], (g >> 1) & 1, args.status, 0x206))) break;
+        tc::tc_fence_after();
+        uint32_t sv[32];
+        tc::tmem_ld_32x32b_x32(lane_base + b * kBK + half * 32, sv);
+        if (!(ok = warp_wait(&st_full[s], (g / kStages) & 1, args.status, 0x207))) {
+          tc::tmem_ld_wait();
+          break;
+        }
+        const int k0 = j * kBK + half * 32;
+        const uint32_t bias_row = smem_base + kStageOff + s * kStageBytes + kKBytes + kVBytes + row * 128;
+        uint32_t bw[16];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          const uint4 m4 = lds128(smem_base + kMaskOff + 2 * k0 + 16 * c);
-          const uint32_t mw[4] = {m4.x, m4.y, m4.z, m4.w};
+          const uint4 bv = lds128(bias_row + (((half * 4 + c) ^ (row & 7)) << 4));
+          bw[4 * c] = bv.x, bw[4 * c + 1] = bv.y, bw[4 * c + 2] = bv.z, bw[4 * c + 3] = bv.w;
+        }
+        const bool tile_unmasked = lds32(smem_base + kFlagOff + 4 * j) == 0;
+        tc::tmem_ld_wait_regs(sv);
+        uint32_t t[16];
+        if (tile_unmasked) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int pr = 4 * c + e;
-            const uint32_t x = cvt_bf16x2(__uint_as_float(sv[2 * pr]), __uint_as_float(sv[2 * pr + 1]));
-            t[pr] = add_bf16x2(add_bf16x2(x, mw[e]), bw[pr]);
+          for (int pr = 0; pr < 16; ++pr)
+            t[pr] = add_bf16x2(cvt_bf16x2(__uint_as_float(sv[2 * pr]), __uint_as_float(sv[2 * pr + 1])), bw[pr]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint4 m4 = lds128(smem_base + kMaskOff + 2 * k0 + 16 * c);
+            const uint32_t mw[4] = {m4.x, m4.y, m4.z, m4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int pr = 4 * c + e;
+              const uint32_t x = cvt_bf16x2(__uint_as_float(sv[2 * pr]), __uint_as_float(sv[2 * pr + 1]));
+              t[pr] = add_bf16x2(add_bf16x2(x, mw[e]), bw[pr]);
+            }
           }
         }
-      }
-      // Keys past n: excluded from the maximum here and zeroed in P below.
-      const bool tail = k0 + 32 > n;
-      if (tail) {
+        const bool tail = k0 + 32 > n;
+        if (tail) {
+#pragma unroll
+          for (int pr = 0; pr < 16; ++pr) {
+            const int key = k0 + 2 * pr;
+            const uint32_t keep = (key < n ? 0x0000ffffu : 0u) | (key + 1 < n ? 0xffff0000u : 0u);
+            t[pr] = (t[pr] & keep) | (kNegPad & ~keep);
+          }
+        }
+        uint32_t mx[4] = {t[0], t[1], t[2], t[3]};
+#pragma unroll
+        for (int pr = 4; pr < 16; ++pr) mx[pr & 3] = max_bf16x2(mx[pr & 3], t[pr]);
+        const uint32_t tmax = max_bf16x2(max_bf16x2(mx[0], mx[1]), max_bf16x2(mx[2], mx[3]));
+        const float m_tile = fmaxf(bf16_lo(tmax), bf16_hi(tmax));
+        const bool first = j == 0;
+        const bool grow = !first && (m_tile - m_ref) * kLog2e > kRescaleLog2;
+        if (__any_sync(0xffffffffu, grow)) {
+          if (!(ok = warp_wait(&pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, args.status, 0x208))) break;
+          tc::tc_fence_after();
+          const float alpha = grow ? fast_exp2((m_ref - m_tile) * kLog2e) : 1.f;
+          uint32_t o[32], l16[16];
+          tc::tmem_ld_32x32b_x32(o_base, o);
+          tc::tmem_ld_32x32b_x16(o_base + 32, l16);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) l16[i] = __float_as_uint(__uint_as_float(l16[i]) * alpha);
+          tc::tmem_st_32x32b_x16(o_base, *reinterpret_cast<const uint32_t(*)[16]>(&o[0]));
+          tc::tmem_st_32x32b_x16(o_base + 16, *reinterpret_cast<const uint32_t(*)[16]>(&o[16]));
+          tc::tmem_st_32x32b_x16(o_base + 32, l16);
+        }
+        if (first || grow) m_ref = m_tile;
+        const float ml = m_ref * kLog2e;
+        uint32_t p[16];
 #pragma unroll
         for (int pr = 0; pr < 16; ++pr) {
-          const int key = k0 + 2 * pr;
-          const uint32_t keep = (key < n ? 0x0000ffffu : 0u) | (key + 1 < n ? 0xffff0000u : 0u);
-          t[pr] = (t[pr] & keep) | (kNegPad & ~keep);
+          float x0 = bf16_lo(t[pr]), x1 = bf16_hi(t[pr]);
+          fma_f32x2(x0, x1, kLog2e, -ml);
+          p[pr] = cvt_bf16x2(fast_exp2(x0), fast_exp2(x1));
         }
-      }
-      uint32_t mx[4] = {t[0], t[1], t[2], t[3]};
+        if (tail) {
 #pragma unroll
-      for (int pr = 4; pr < 16; ++pr) mx[pr & 3] = max_bf16x2(mx[pr & 3], t[pr]);
-      const uint32_t tmax = max_bf16x2(max_bf16x2(mx[0], mx[1]), max_bf16x2(mx[2], mx[3]));
-      const float m_tile = fmaxf(bf16_lo(tmax), bf16_hi(tmax));
-
-      // Reference maximum: set on the first tile; raised (with O_h rescaled)
-      // only when this tile's maximum exceeds it by more than 2^8 in exp2.
-      const bool first = j == 0;
-      const bool grow = !first && (m_tile - m_ref) * kLog2e > kRescaleLog2;
-      if (__any_sync(0xffffffffu, grow)) {
-        // O_h holds tiles < j: wait for the P.V of tile j - 1, then scale in place.
-        if (!(ok = warp_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, args.status, 0x208))) break;
-        tc::tc_fence_after();
-        const float alpha = grow ? fast_exp2((m_ref - m_tile) * kLog2e) : 1.f;
-        uint32_t o[32], l16[16];
-        tc::tmem_ld_32x32b_x32(o_base, o);
-        tc::tmem_ld_32x32b_x16(o_base + 32, l16);
-        tc::tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) l16[i] = __float_as_uint(__uint_as_float(l16[i]) * alpha);
-        tc::tmem_st_32x32b_x16(o_base, *reinterpret_cast<const uint32_t(*)[16]>(&o[0]));
-        tc::tmem_st_32x32b_x16(o_base + 16, *reinterpret_cast<const uint32_t(*)[16]>(&o[16]));
-        tc::tmem_st_32x32b_x16(o_base + 32, l16);
-      }
-      if (first || grow) m_ref = m_tile;
-      const float ml = m_ref * kLog2e;
-
-      // P (bf16x2 per key pair) over the first 16 columns of this S half.
-      uint32_t p[16];
-#pragma unroll
-      for (int pr = 0; pr < 16; ++pr) {
-        float x0 = bf16_lo(t[pr]), x1 = bf16_hi(t[pr]);
-        fma_f32x2(x0, x1, kLog2e, -ml);
-        p[pr] = cvt_bf16x2(fast_exp2(x0), fast_exp2(x1));
-      }
-      if (tail) {
-#pragma unroll
-        for (int pr = 0; pr < 16; ++pr) {
-          const int key = k0 + 2 * pr;
-          p[pr] &= (key < n ? 0x0000ffffu : 0u) | (key + 1 < n ? 0xffff0000u : 0u);
+          for (int pr = 0; pr < 16; ++pr) {
+            const int key = k0 + 2 * pr;
+            p[pr] &= (key < n ? 0x0000ffffu : 0u) | (key + 1 < n ? 0xffff0000u : 0u);
+          }
         }
+        tc::tmem_st_32x32b_x16(lane_base + b * kBK + half * 32, p);
+        tc::tmem_st_wait();
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&p_full[b]);
       }
-      tc::tmem_st_32x32b_x16(lane_base + b * kBK + half * 32, p);
-      tc::tmem_st_wait();
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&p_full[b]);
-    }
-    // Epilogue: merge the two key halves, O / l, bf16, gate, store.  This
-    // thread writes output channels 16 half .. 16 half + 15 of its row.
-    row_max[half * kBQ + row] = m_ref;
-    // The gate (bf16(sigmoid(g)) from the projection) is loaded before the
-    // barrier and the wait for the last P.V, which cover its latency.
-    const int qi = q0 + row;
-    const int64_t pair = int64_t(outer) * args.so + int64_t(qi) * args.si;
-    uint4 gate[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
-    if (qi < n) {
-      const uint4 *g4 = reinterpret_cast<const uint4 *>(args.g + pair * args.ld + h * kD + half * 16);
-      gate[0] = g4[0];
-      gate[1] = g4[1];
-    }
-    asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxWarps * 32) : "memory");
-    const float m_other = row_max[(half ^ 1) * kBQ + row];
-    if (ok && warp_wait(o_full, 0, args.status, 0x20A)) {
+      // Epilogue of head h: merge the two key halves, O / l, bf16, gate, store.
+      float *rmax = row_max;  // a warp rewrites it only after every warp started the next head
+      rmax[half * kBQ + row] = m_ref;
+      uint4 gate[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
+      if (qi < n) {
+        const uint4 *g4 = reinterpret_cast<const uint4 *>(args.g + pair * args.ld + h * kD + half * 16);
+        gate[0] = g4[0];
+        gate[1] = g4[1];
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxWarps * 32) : "memory");
+      const float m_other = rmax[(half ^ 1) * kBQ + row];
+      // After the exchange the next head's epilogue may rewrite rmax: every warp
+      // has read its partner's value before any warp leaves this barrier pair.
+      if (kMulti) asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxWarps * 32) : "memory");
+      if (!ok || !(ok = warp_wait(o_full, hl & 1, args.status, 0x20A))) continue;
       tc::tc_fence_after();
-      const float m0 = half == 0 ? m_ref : m_other, m1 = half == 0 ? m_other : m_ref;
-      const float m = fmaxf(m0, m1);
-      const float a0 = fast_exp2((m0 - m) * kLog2e), a1 = fast_exp2((m1 - m) * kLog2e);
       uint32_t o0[16], o1[16], l0, l1;  // row sums: column 32 of each half's accumulator
       tc::tmem_ld_32x32b_x16(lane_base + kOCol + half * 16, o0);
       tc::tmem_ld_32x32b_x16(lane_base + kOCol + kOStride + half * 16, o1);
       tc::tmem_ld_32x32b_x1(lane_base + kOCol + 32, l0);
       tc::tmem_ld_32x32b_x1(lane_base + kOCol + kOStride + 32, l1);
       tc::tmem_ld_wait();
+      // O has been read: the next head's first P.V may overwrite it.
+      if (kMulti && hl + 1 < hpc) {
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(o_free);
+      }
+      const float m0 = half == 0 ? m_ref : m_other, m1 = half == 0 ? m_other : m_ref;
+      const float m = fmaxf(m0, m1);
+      const float a0 = fast_exp2((m0 - m) * kLog2e), a1 = fast_exp2((m1 - m) * kLog2e);
       if (qi < n) {
         const float inv = fast_rcp(__uint_as_float(l0) * a0 + __uint_as_float(l1) * a1);
         uint4 *o4 = reinterpret_cast<uint4 *>(args.out + pair * args.out_ld + h * kD + half * 16);
@@ -498,13 +530,20 @@ extern "C" int bl_triangle_attention(const void *q, const void *k, const void *v
   args.out = static_cast<__nv_bfloat16 *>(out);
   args.out_ld = out_ld;
   args.n = int(n);
+
   args.status = device_status_ptr();
   BL_REQUIRE(args.status, "bl_triangle_attention: device status word unavailable");
   const int n_tiles = int((n + kBK - 1) / kBK);
   const int smem = kMaskOff + n_tiles * kBK * 2 + 1024;
-  BL_CUDA(ensure_smem_limit(reinterpret_cast<const void *>(tri_flash_tc_kernel), 232448));
-  dim3 grid(unsigned((n + kBQ - 1) / kBQ * kHeads), unsigned(n_outer));
-  tri_flash_tc_kernel<<<grid, kThreads, smem, as_stream(stream)>>>(map_q, map_k, map_v, map_bias, args);
+  // Heads run back to back by one CTA (sharing its setup, mask pass and key
+  // ring) when the grid still fills the GPU several times over.
+  const int64_t q_tiles = (n + kBQ - 1) / kBQ, slots = 2 * int64_t(num_sms());
+  const int hpc = q_tiles * n_outer >= 4 * slots ? 4 : 2 * q_tiles * n_outer >= 4 * slots ? 2 : 1;
+  args.heads_per_cta = hpc;
+  auto kernel = hpc > 1 ? tri_flash_tc_kernel<true> : tri_flash_tc_kernel<false>;
+  BL_CUDA(ensure_smem_limit(reinterpret_cast<const void *>(kernel), 232448));
+  dim3 grid(unsigned(q_tiles * (kHeads / hpc)), unsigned(n_outer));
+  kernel<<<grid, kThreads, smem, as_stream(stream)>>>(map_q, map_k, map_v, map_bias, args);
   BL_LAUNCH_CHECK();
   return BL_OK;
 }
