@@ -19,6 +19,7 @@ rank 0 runs it.
 import argparse
 import json
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -202,11 +203,15 @@ def algorithmic_work(name, a):
     if name == "bl_batched_gemm":
         batch, m, n, k = a[11], a[12], a[13], a[14]
         return "flops", 2.0 * batch * m * n * k, f"bl_batched_gemm[b={batch},m={m},n={n},k={k}]"
-    if name == "bl_triangle_attention":
+    if name in ("bl_triangle_attention", "bl_triangle_attention_residual"):
+        # q k^T and p v: 4 N^2 n_outer H d; the residual form adds linear_o (2 N n_outer 128^2)
         heads, d, n, n_outer = a[14], a[15], a[16], a[17]
-        label = f"bl_triangle_attention[n={n},heads={heads},d={d}]" if n_outer == n else \
-            f"bl_triangle_attention[n={n},n_outer={n_outer},heads={heads},d={d}]"
-        return "flops", 4.0 * n * n * n_outer * heads * d, label
+        label = f"{name}[n={n},heads={heads},d={d}]" if n_outer == n else \
+            f"{name}[n={n},n_outer={n_outer},heads={heads},d={d}]"
+        flops = 4.0 * n * n * n_outer * heads * d
+        if name == "bl_triangle_attention_residual":
+            flops += 2.0 * n * n_outer * 128 * 128
+        return "flops", flops, label
     if name == "bl_layernorm":
         size = {0: 4, 1: 2}
         rows, cols = a[2], a[3]
@@ -467,7 +472,8 @@ def run_b200(args):
         # per score on the MUFU pipe, 16 per clock per SM.  The peak is derived
         # from that rate, the SM count and the sampled SM clock (there is no
         # measured SFU figure).
-        exps = top["amount"] / (4 * 32)  # 4 N^3 H d FLOP with d = 32 -> N^3 H scores
+        dims = {key: int(val) for key, val in re.findall(r"(\w+)=(\d+)", top_label)}
+        exps = float(dims["n"] ** 2 * dims.get("n_outer", dims["n"]) * dims["heads"])  # one per score
         clock_mhz = (clock_info or {}).get("sm_mhz") or 1965.0
         sms = torch.cuda.get_device_properties(device).multi_processor_count
         sfu_peak = 16 * sms * clock_mhz * 1e6

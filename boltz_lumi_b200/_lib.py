@@ -47,6 +47,9 @@ SIGNATURES = {
     "bl_swiglu_rows": [_p, c_int64, c_int64, c_int64, _p, c_int64, _p],
     "bl_triangle_attention": [_p, _p, _p, _p, c_int64, c_int64, c_int64, _p, c_int64, c_int64, _p, c_int64,
                               c_int64, c_float, c_int64, c_int64, c_int64, c_int64, _p, c_int64, _p],
+    "bl_triangle_attention_residual": [_p, _p, _p, _p, c_int64, c_int64, c_int64, _p, c_int64, c_int64, _p, c_int64,
+                                       c_int64, c_float, c_int64, c_int64, c_int64, c_int64, _p, c_int64, _p, _p, _p,
+                                       c_int64, _p],
     "bl_pair_transition_static": [_p, c_int64, _p, _p, c_float, _p, _p, _p, _p],
     "bl_split3_bf16": [_p, c_int64, c_int64, c_int64, _p, _p],
     "bl_linear_split3": [_p, c_int64, c_int64, _p, c_int64, _p, _p, c_int64, _p, c_int64, _p],

@@ -207,14 +207,18 @@ def triangle_attention_forward(self, x, mask=None, chunk_size=None, use_kernels=
         so, si = (n, 1) if starting else (1, n)
         ms_o, ms_k = (n, 1) if starting else (1, n)
         base = proj.data_ptr()
-        call("bl_triangle_attention", base, base + 128 * 2, base + 256 * 2, base + 384 * 2, width, so, si,
-             bias.data_ptr(), n_pad, n * n_pad, mask[b].data_ptr(), ms_o, ms_k, float(getattr(self, "inf", 1e9)),
-             4, 32, n, n, gated.data_ptr(), 128, stream)
-        del proj, bias
+        args = (base, base + 128 * 2, base + 256 * 2, base + 384 * 2, width, so, si, bias.data_ptr(), n_pad,
+                n * n_pad, mask[b].data_ptr(), ms_o, ms_k, float(getattr(self, "inf", 1e9)), 4, 32, n, n,
+                gated.data_ptr(), 128)
         if residual is not None:
-            _linear_out(gated, w["w_out"], rows, 128, stream, bias=w["b_out"], residual=residual[b].view(rows, 128))
+            # linear_o and the residual add run in the attention kernel's epilogue
+            # when four heads share a CTA (else as one more GEMM launch, same bits).
+            call("bl_triangle_attention_residual", *args, w["w_out"].data_ptr(), w["b_out"].data_ptr(),
+                 residual[b].data_ptr(), 128, stream)
         else:
+            call("bl_triangle_attention", *args, stream)
             _linear_out(gated, w["w_out"], rows, 128, stream, bias=w["b_out"], out=out[b].view(rows, 128))
+        del proj, bias
     return residual if residual is not None else out
 
 

@@ -244,10 +244,10 @@ def _attention_slab(module, x, mask_rows, comm):
     bias_full = _gather_rows(bias, comm).contiguous()  # [4, N, n_pad]
     gated = torch.empty(n_loc * n, 128, device=x.device, dtype=_BF16)
     base = proj.data_ptr()
-    call("bl_triangle_attention", base, base + 128 * 2, base + 256 * 2, base + 384 * 2, 512, n, 1,
+    call("bl_triangle_attention_residual", base, base + 128 * 2, base + 256 * 2, base + 384 * 2, 512, n, 1,
          bias_full.data_ptr(), n_pad, n * n_pad, mask_rows.data_ptr(), n, 1, float(getattr(module, "inf", 1e9)),
-         4, 32, n, n_loc, gated.data_ptr(), 128, stream)
-    forwards._linear_out(gated, w["w_out"], n_loc * n, 128, stream, bias=w["b_out"], residual=x.view(n_loc * n, 128))
+         4, 32, n, n_loc, gated.data_ptr(), 128, w["w_out"].data_ptr(), w["b_out"].data_ptr(), x.data_ptr(), 128,
+         stream)
 
 
 class ShardedPairformer:

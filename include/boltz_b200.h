@@ -279,7 +279,7 @@ BL_API int bl_swiglu_rows(const void *x, int64_t x_ld, int64_t rows, int64_t wid
  * mask(a, c) at mask + a*ms_o + c*ms_k (fp32).  out rows of out_ld elements
  * at the same pair rows.  n is the key / query extent, n_outer the number of
  * outer rows a processed (n for a whole pair tensor, fewer for a row slab).
- * heads must be 4 and head_dim 32, n <= 4096; all pointers
+ * heads must be 4 and head_dim 32, n <= 4096, 0 <= inf <= 1e20; all pointers
  * 16-byte aligned, ld / out_ld / bias_ld / bias_hs multiples of 8.  Runs on
  * tcgen05 tensor cores (scores and P in TMEM, TMA-fed key tiles).
  */
@@ -288,6 +288,31 @@ BL_API int bl_triangle_attention(const void *q, const void *k, const void *v, co
                                  int64_t bias_hs, const float *mask, int64_t ms_o, int64_t ms_k,
                                  float inf, int64_t heads, int64_t head_dim, int64_t n, int64_t n_outer,
                                  void *out, int64_t out_ld, void *stream);
+
+/*
+ * Triangle attention followed by its output projection and the block's
+ * residual add (fp32 z):
+ *   z[pair] += bf16(out(a, b) . W_o^T + b_o)
+ * with out(a, b) as in bl_triangle_attention and pair = a*so + b*si.
+ * Replaces, on top of bl_triangle_attention's span, linear_o of upstream
+ * _wrap_up (triangle.py:104) and the Pairformer's residual add of the
+ * triangle-attention update.
+ * w_o: bf16 [128][128] row-major (linear_o.weight), b_o: fp32 [128];
+ * z: fp32 rows of z_ld elements (z_ld a multiple of 4, 16-byte aligned).
+ * scratch: bf16 rows of scratch_ld elements at the same pair rows, written
+ * only when the projection runs as a separate GEMM (fewer than four heads per
+ * CTA at this size; the output rows must then be contiguous: starting node,
+ * or ending node over the whole tensor).  When the grid fills the GPU eight
+ * times over (4 * ceil(n / 128) * n_outer >= 32 * SMs) the projection runs in
+ * the attention kernel's epilogue and the gated tensor never reaches memory.
+ * Either way z equals bl_triangle_attention + bl_linear_fused bit for bit.
+ */
+BL_API int bl_triangle_attention_residual(const void *q, const void *k, const void *v, const void *g,
+                                          int64_t ld, int64_t so, int64_t si, const void *bias,
+                                          int64_t bias_ld, int64_t bias_hs, const float *mask, int64_t ms_o,
+                                          int64_t ms_k, float inf, int64_t heads, int64_t head_dim, int64_t n,
+                                          int64_t n_outer, void *scratch, int64_t scratch_ld, const void *w_o,
+                                          const float *b_o, float *z, int64_t z_ld, void *stream);
 
 /*
  * Attention core of the diffusion token transformer, fp32 end to end:

@@ -40,3 +40,7 @@ def test_error_path_without_gpu():
     assert b"dtype" in lib.bl_last_error()
     with pytest.raises(RuntimeError, match="bl_gate_pack"):
         _lib.call("bl_gate_pack", None, None, 300, None, 4, 1, None, None, None)
+    # The residual form of triangle attention needs linear_o's weight.
+    with pytest.raises(RuntimeError, match="w_o is required"):
+        _lib.call("bl_triangle_attention_residual", None, None, None, None, 512, 8, 1, None, 8, 64, None, 8, 1,
+                  1e9, 4, 32, 8, 8, None, 128, None, None, None, 128, None)

@@ -92,6 +92,30 @@ def test_triangle_attention_reference_sizes(ending, n, kind, rows):
 
 
 @pytest.mark.parametrize("ending", [False, True])
+@pytest.mark.parametrize("n,kind", [(200, "partial"), (312, "ones"), (450, "partial"), (576, "ones"),
+                                    (1134, "partial")])
+def test_triangle_attention_residual(ending, n, kind):
+    """z += TriangleAttention(z) through bl_triangle_attention_residual (linear_o and the
+    residual add in the attention kernel's epilogue at N >= 385, one more GEMM below):
+    bit-identical to z + the module's bf16 output, so the parity of the module output
+    carries over.  N = 450 ends in a partial query tile; 200 and 312 take the separate
+    GEMM (one and two heads per CTA)."""
+    from boltz_lumi_b200 import forwards
+
+    cls = (layers.TriangleAttentionEndingNode, oracle.TriangleAttentionEndingNode) if ending else \
+        (layers.TriangleAttention, oracle.TriangleAttention)
+    mod, _ = build(*cls, 128, 32, 4)
+    g = torch.Generator().manual_seed(n + 1)
+    z = (torch.randn(1, n, n, 128, generator=g) * 0.3).cuda()
+    mask = pair_mask(n, kind).cuda()
+    with torch.inference_mode():
+        expected = z + mod(z, mask).float()
+        forwards.triangle_attention_forward(mod, z, mask, residual=z)
+    assert torch.isfinite(z).all()
+    assert torch.equal(z, expected), (z - expected).abs().max().item()
+
+
+@pytest.mark.parametrize("ending", [False, True])
 @pytest.mark.parametrize("n,kind", [(17, "ones"), (64, "partial"), (130, "partial"), (200, "ones"), (312, "partial")])
 def test_triangle_attention_fp32_mode(ending, n, kind):
     """fp32 mode: fp32 input with autocast off (the reference's fast path accepts it,
