@@ -531,8 +531,8 @@ def traffic_for(label):
 
 def measure_sharded(n, steps, warmup, e2e_steps, dist, device):
     """One Pairformer block at n tokens row-sharded over the ranks (each rank holds
-    n / world rows of z; the row <-> column transposes and plane / bias gathers run on
-    NCCL over NVLink).  Total work per step is fixed (strong scaling).  Returns the
+    n / world rows of z; the channel regrouping of the triangle-multiplication planes,
+    the row <-> column transposes and the bias gathers run on NCCL over NVLink).  Total work per step is fixed (strong scaling).  Returns the
     record (device time per block, max over ranks) on every rank."""
     from boltz_lumi_b200 import _lib, layers
     from boltz_lumi_b200.sharded import ShardedPairformer, SingleComm, TorchComm
@@ -593,7 +593,8 @@ def measure_sharded(n, steps, warmup, e2e_steps, dist, device):
         "n_gpus": world, "steps": steps, "warmup": max(warmup, 1), "ms_per_step": round(ms, 4),
         "higher_is_better": False, "scaling": "strong",
         "workload": f"one Pairformer block N={n}, z rows split over {world} GPU(s) "
-                    "(all_to_all row/column transposes, all_gather of planes and biases, NCCL)",
+                    "(triangle-multiplication products channel-sharded through all_to_all, row/column "
+                    "transposes around the ending-node attention, all_gather of the bias rows and s; NCCL)",
         "tokens": n, "rows_per_gpu": n_loc, "parallelism": f"row-sharded x{world}",
         "e2e": {"value": round(e2e, 4), "unit": UNIT, "h2d_bytes_per_step": zr_pin.numel() * 4 + s_pin.numel() * 4,
                 "d2h_bytes_per_step": zr_pin.numel() * 4 + s_pin.numel() * 4, "steps": e2e_steps},

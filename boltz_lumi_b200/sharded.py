@@ -4,11 +4,19 @@ The pair tensor z [N, N, 128] (fp32) is split by rows across P ranks: rank r
 holds rows I_r = [r N/P, (r + 1) N/P).  Every op then runs the same kernels as
 the single-GPU path on its slab, with the exchanges the op needs:
 
-* TriangleMultiplicationOutgoing (row layout): each rank projects its rows
-  into channel planes a_r, b_r; b is all-gathered, and O_c[I_r, :] =
-  a_r b_c^T is one per-channel GEMM per source rank (output columns I_p).
-* TriangleMultiplicationIncoming: run as the outgoing form on z^T (column
-  layout) with the two operand halves swapped:
+* Triangle multiplication, channel-sharded products (P divides 128): each
+  rank projects its rows into channel planes a, b ([c][row][col], rows I_r);
+  one all_to_all per operand regroups them by channel, so rank r holds all
+  rows of the planes of its channels C_r (128 / P of them); it computes
+  O_c = a_c b_c^T (outgoing) or a_c^T b_c (incoming: the contraction runs
+  over the row index, which the channel split makes local) for every pair,
+  and one all_to_all of O returns the rows I_p of all channels to rank p.
+  Per op a rank receives 3 (P - 1) / P^2 of a 1 GiB plane set at N = 2048
+  (a, b, O), and the incoming op needs no row <-> column transpose of z.
+  With P = 2 or 3 the outgoing op instead all-gathers b (less data there):
+  O_c[I_r, :] = a_r b_c^T as one per-channel GEMM per source rank, and P = 3
+  runs the incoming op as the outgoing form on z^T (column layout) with the
+  operand halves swapped:
   z[i, j] += sum_k a[k, i] b[k, j]  ==  z'[j, i] += sum_k b'[j, k] a'[i, k],  z' = z^T.
 * TriangleAttentionStartingNode (row layout): local rows; the triangle bias
   [4, N, N] (one row block per rank) is all-gathered.
@@ -194,10 +202,53 @@ def _gather_rows(local, comm):
 # ---------------------------------------------------------------------------
 # Per-op slab forwards (the single-GPU kernels on [n_loc, N] row slabs)
 # ---------------------------------------------------------------------------
-def _trimul_slab(module, x, mask_rows, comm, swap):
-    """z_slab += outgoing-form triangle multiplication of `module` on the row
-    slab x [n_loc, N, 128] (fp32, updated in place); `swap` exchanges the two
-    operand halves (the incoming op on the transposed tensor)."""
+def _plane_gemm(a, a_mn, b, b_mn, out, m, n, k, stream):
+    """out[c][:m, :n] = bf16(A_c B_c^T) (fp32 accumulation) for every channel c of
+    the strided plane views a ([cg, m, k] K-major, or [cg, k, m] with a_mn) and
+    b ([cg, n, k], or [cg, k, n] with b_mn); out is [cg, m, >= n]."""
+    call("bl_batched_gemm", a.data_ptr(), a_mn, a.stride(1), a.stride(0), b.data_ptr(), b_mn, b.stride(1),
+         b.stride(0), out.data_ptr(), out.stride(1), out.stride(0), out.shape[0], m, n, k, None, stream)
+
+
+def _channel_products(rows_op, cols_op, n, comm, incoming, stream):
+    """Per-channel products of the row-sharded planes, computed channel-sharded.
+
+    rows_op / cols_op: this rank's planes [128, n_loc, n_pad] (rows I_r).  Returns
+    prod [128, n_loc, n_pad]: O_c[i in I_r, j] for every channel, with
+    outgoing O_c = A_c B_c^T (planes [i][k]) and incoming O_c = A_c^T B_c (planes
+    [k][i], the contraction over the sharded row index)."""
+    world = comm.world
+    cg, n_loc, n_pad = 128 // world, rows_op.shape[1], rows_op.shape[2]
+    # Chunk p of the send buffer = channels C_p of my rows; chunk p received =
+    # rank p's rows I_p of my channels C_r.
+    a = comm.all_to_all(rows_op.reshape(world, cg, n_loc, n_pad))
+    b = comm.all_to_all(cols_op.reshape(world, cg, n_loc, n_pad))
+    b_all = b.permute(1, 0, 2, 3).reshape(cg, n, n_pad)  # [c][row in 0..N)[col]
+    del b
+    if incoming:
+        a_all = a.permute(1, 0, 2, 3).reshape(cg, n, n_pad)  # [c][k][i]
+        del a
+    out = torch.empty(world, cg, n_loc, n_pad, device=rows_op.device, dtype=_BF16)
+    for p in range(world):
+        # out[p] = O_c[i in I_p, all j] for c in C_r: sent back to rank p.
+        if incoming:  # A_c^T restricted to columns I_p (MN-major)
+            _plane_gemm(a_all[:, :, p * n_loc:(p + 1) * n_loc], 1, b_all, 1, out[p], n_loc, n, n, stream)
+        else:  # rank p's rows of A_c (K-major)
+            _plane_gemm(a[p], 0, b_all, 0, out[p], n_loc, n, n, stream)
+    del b_all
+    return comm.all_to_all(out).reshape(128, n_loc, n_pad)  # chunk p = channels C_p of my rows
+
+
+def _channel_split(comm):
+    return comm.world > 1 and 128 % comm.world == 0
+
+
+def _trimul_slab(module, x, mask_rows, comm, swap, incoming=False):
+    """z_slab += triangle multiplication of `module` on the row slab x [n_loc, N, 128]
+    (fp32, updated in place).  incoming=False: the outgoing form (`swap`
+    exchanges the two operand halves: the incoming op on the transposed tensor);
+    incoming=True: the incoming op on the row slab itself (channel-sharded
+    products only)."""
     n_loc, n = x.shape[0], x.shape[1]
     n_pad = forwards._pad8(n)
     w = forwards._multiplication_weights(module)
@@ -208,6 +259,11 @@ def _trimul_slab(module, x, mask_rows, comm, swap):
          _f32(module.norm_in.bias).data_ptr(), float(module.norm_in.eps), w["w_in"].data_ptr(),
          mask_rows.data_ptr(), planes.data_ptr(), n_pad, xn.data_ptr(), stream)
     rows_op, cols_op = (planes[128:], planes[:128]) if swap else (planes[:128], planes[128:])
+    if incoming or (_channel_split(comm) and comm.world >= 4):
+        prod = _channel_products(rows_op, cols_op, n, comm, incoming, stream)
+        del planes, rows_op, cols_op
+        _trimul_out(module, prod, xn, x, n, n_loc, n_pad, stream)
+        return
     prod = torch.empty(128, n_loc, n_pad, device=x.device, dtype=_BF16)
     plane = n_loc * n_pad
     # The other ranks' column planes arrive in channel groups: the per-channel
@@ -223,6 +279,12 @@ def _trimul_slab(module, x, mask_rows, comm, swap):
             call("bl_batched_gemm", rows_op.data_ptr() + off, 0, n_pad, plane, cols_all[p].data_ptr(), 0, n_pad,
                  plane, prod.data_ptr() + off + p * n_loc * 2, n_pad, plane, cg, n_loc, n_loc, n, None, stream)
         del cols_all
+    _trimul_out(module, prod, xn, x, n, n_loc, n_pad, stream)
+
+
+def _trimul_out(module, prod, xn, x, n, n_loc, n_pad, stream):
+    """LayerNorm over the product planes, p_out, g_out(x_hat), gate, z_slab += ."""
+    w = forwards._multiplication_weights(module)
     norm = module.norm_out
     call("bl_trimul_output", prod.data_ptr(), n, n_loc, n_pad, _f32(norm.weight).data_ptr(),
          _f32(norm.bias).data_ptr(), float(norm.eps), xn.data_ptr(), w["w_pg"].data_ptr(), x.data_ptr(), None,
@@ -271,9 +333,13 @@ class ShardedPairformer:
         mask_rows = pm[r0:r0 + n_loc].contiguous()
         mask_cols = pm.t()[r0:r0 + n_loc].contiguous()
         _trimul_slab(blk.tri_mul_out, z_rows, mask_rows, comm, swap=False)
-        z_cols = rows_to_columns(z_rows, comm)
-        _trimul_slab(blk.tri_mul_in, z_cols, mask_cols, comm, swap=True)
-        z_rows = rows_to_columns(z_cols, comm)
+        if _channel_split(comm) or comm.world == 1:
+            # The channel split makes the incoming contraction (over rows) local.
+            _trimul_slab(blk.tri_mul_in, z_rows, mask_rows, comm, swap=False, incoming=True)
+        else:
+            z_cols = rows_to_columns(z_rows, comm)
+            _trimul_slab(blk.tri_mul_in, z_cols, mask_cols, comm, swap=True)
+            z_rows = rows_to_columns(z_cols, comm)
         _attention_slab(blk.tri_att_start, z_rows, mask_rows, comm)
         z_cols = rows_to_columns(z_rows, comm)
         _attention_slab(blk.tri_att_end, z_cols, mask_cols, comm)

@@ -2,8 +2,9 @@
 
 P virtual ranks run as threads on one GPU (ThreadComm), and, when two GPUs are
 visible, two real ranks over NCCL.  Every pair op of the sharded block runs the
-same kernels on row slabs with the same accumulation order per output, so the
-sharded z must equal the unsharded one (checked to 1e-6 absolute).  The single
+same kernels on row slabs (the triangle-multiplication products on channel
+slabs) with the same accumulation order per output, so the sharded z must
+equal the unsharded one (checked to 1e-6 absolute).  The single
 track runs on query-row slabs, where the fp32 tensor-core linears and the
 token attention may split their K / key ranges differently than on all rows
 (fp32 summation order only): s is checked to 2e-5 absolute on O(1) values.
@@ -35,7 +36,7 @@ def _inputs(n, masked_tail):
     return s, z, mask, pmask
 
 
-@pytest.mark.parametrize("world,n,masked_tail", [(2, 128, 0), (4, 128, 9), (2, 192, 5)])
+@pytest.mark.parametrize("world,n,masked_tail", [(2, 128, 0), (4, 128, 9), (2, 192, 5), (8, 128, 3), (4, 256, 7)])
 def test_sharded_block_matches_single_gpu_threads(world, n, masked_tail):
     block = bench.seeded_block(layers.PairformerLayer).cuda()
     s, z, mask, pmask = (t.cuda() for t in _inputs(n, masked_tail))

@@ -1,10 +1,12 @@
 """Row-sharding layout and collectives of the sharded Pairformer (CPU).
 
 The sharded block (boltz_lumi_b200/sharded.py) moves the pair tensor between
-row and column ownership with one all_to_all and gathers plane / bias row
-blocks with all_gather.  These tests check that plumbing on CPU tensors: with
+row and column ownership with one all_to_all, gathers plane / bias row
+blocks with all_gather, and regroups the triangle-multiplication planes by
+channel with all_to_all.  These tests check that plumbing on CPU tensors: with
 the thread-emulated group and with real gloo ranks (world size 2), against
-the single-process transpose / concatenation it must equal.
+the single-process transpose / concatenation / einsum it must equal (the
+per-channel GEMM is replaced by torch.bmm on the same strided views).
 """
 
 import os
@@ -15,6 +17,7 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
+from boltz_lumi_b200 import sharded
 from boltz_lumi_b200.sharded import ThreadComm, TorchComm, _gather_rows, rows_to_columns
 
 
@@ -98,3 +101,33 @@ def test_rows_to_columns_gloo_world2():
     results = manager.dict()
     mp.start_processes(_gloo_rank, args=(2, port, 3, results), nprocs=2, start_method="spawn", join=True)
     assert dict(results) == {0: (True, True, True), 1: (True, True, True)}
+
+
+def _bmm_plane_gemm(a, a_mn, b, b_mn, out, m, n, k, stream):
+    """The CPU stand-in for bl_batched_gemm on strided plane views."""
+    a_mk = (a.transpose(1, 2) if a_mn else a)[:, :m, :k].float()
+    b_nk = (b.transpose(1, 2) if b_mn else b)[:, :n, :k].float()
+    out[:, :m, :n] = torch.bmm(a_mk, b_nk.transpose(1, 2)).to(out.dtype)
+
+
+@pytest.mark.parametrize("world,incoming", [(1, True), (2, False), (2, True), (4, True), (8, False), (8, True)])
+def test_channel_products_threads(world, incoming, monkeypatch):
+    """Channel-sharded per-channel products equal the unsharded einsum on every rank's rows:
+    outgoing O_c[i, j] = sum_k a[i, k] b[j, k], incoming O_c[i, j] = sum_k a[k, i] b[k, j]."""
+    monkeypatch.setattr(sharded, "_plane_gemm", _bmm_plane_gemm)
+    n_loc = 3
+    n, n_pad = world * n_loc, world * n_loc + 5
+    g = torch.Generator().manual_seed(world + 10 * incoming)
+    # small integers: every product and sum is exact in bf16 / fp32
+    a = torch.randint(-2, 3, (128, n, n_pad), generator=g).to(torch.bfloat16)
+    b = torch.randint(-2, 3, (128, n, n_pad), generator=g).to(torch.bfloat16)
+    af, bf = a[:, :, :n].float(), b[:, :, :n].float()
+    expected = torch.einsum("cki,ckj->cij", af, bf) if incoming else torch.einsum("cik,cjk->cij", af, bf)
+
+    def rank_fn(comm):
+        rows = slice(comm.rank * n_loc, (comm.rank + 1) * n_loc)
+        return sharded._channel_products(a[:, rows].contiguous(), b[:, rows].contiguous(), n, comm, incoming, None)
+
+    for r, prod in enumerate(_run_threads(world, rank_fn)):
+        assert prod.shape == (128, n_loc, n_pad)
+        assert torch.equal(prod[:, :, :n].float(), expected[:, r * n_loc:(r + 1) * n_loc]), r
