@@ -52,7 +52,7 @@ def parse_args():
     # The end-to-end pipeline's fill (first input copy) and drain (last
     # output copy) are inside the timed region; 24 steps amortise them the
     # way a longer job would (at ~3 ms per step the region stays < 0.1 s).
-    p.add_argument("--e2e-steps", type=int, default=24)
+    p.add_argument("--e2e-steps", type=int, default=64)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-sub-records", action="store_true",
                    help="skip the row-sharded N=2048 block and the diffusion sampler sub-records")
