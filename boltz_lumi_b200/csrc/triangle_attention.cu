@@ -95,7 +95,7 @@ constexpr uint32_t kNegPad = 0xF14AF14Au;  // bf16x2 (-1e30, -1e30)
 // value itself, and t log2 e - m log2 e would leave the fma's rounding residual
 // (up to 2^76 at that magnitude) inside exp2, overflowing the register row sum.
 // With the floor the padded exponentials underflow to exactly 0; scores of real
-// keys stay far above it (masked keys sit at -inf = -1e9).
+// keys stay far above it (masked keys sit at -inf, and the host requires inf <= 1e20).
 constexpr float kMaxFloor = -1e29f;
 
 struct TcArgs {
