@@ -25,15 +25,14 @@
 // waiting for the later MMA2.  The residual update is a TMA reduce-add of the
 // fp32 y tile into z, so z is never loaded by the SM for the residual.
 //
-// Warps (19): 0 TMA producer, 1 TMEM allocation + MMA1 issue, 2..9 SwiGLU
-// (TMEM lane quarter = warp % 4; warps 2..5 take hidden units 0..31 of each
-// chunk, warps 6..9 units 32..63), 10..13 LayerNorm (32 rows each, the next
-// rows in flight while normalising), 14 MMA2 issue, 15..18 output (one per
-// lane quarter, all 128 columns).  MMA1 and MMA2 have their own issuing
-// threads, so MMA1 of chunk h + 1 never waits behind MMA2 of chunk h - 1, and
-// the output of tile t runs on its own warps while the SwiGLU warps start on
-// tile t + 1 (measured at N = 512: 157 -> 151 us for the split issue, -> 142 us
-// with the output warps; bitwise-identical output).
+// Warps (15): 0 TMA producer, 1 TMEM allocation + MMA1 issue, 2..9 SwiGLU and
+// output (TMEM lane quarter = warp % 4; warps 2..5 take hidden units 0..31
+// of each chunk and output columns 0..63, warps 6..9 the other halves),
+// 10..13 LayerNorm (32 rows each, next rows in flight while normalising),
+// 14 MMA2 issue.  With MMA1 and MMA2 on their own issuing threads, MMA1 of
+// chunk h + 1 no longer waits behind MMA2 of chunk h - 1 (which waits for the
+// SwiGLU of chunk h - 1): measured at N = 512 with z updated in place,
+// 156.5 -> 149.4 us, bitwise-identical output.
 #include "tc.cuh"
 
 namespace bl {
@@ -49,9 +48,7 @@ constexpr int kLnWarps = 4;
 constexpr int kFirstEpiWarp = 2;
 constexpr int kFirstLnWarp = kFirstEpiWarp + kEpiWarps;
 constexpr int kMma2Warp = kFirstLnWarp + kLnWarps;  // fc3 MMA issue
-constexpr int kOutWarps = 4;                          // output epilogue, one per TMEM lane quarter
-constexpr int kFirstOutWarp = kMma2Warp + 1;
-constexpr int kThreads = (kFirstOutWarp + kOutWarps) * 32;
+constexpr int kThreads = (kMma2Warp + 1) * 32;
 
 constexpr int kKBlock = kRows * 64 * 2;  // [128 rows][64 K] bf16, 128-byte swizzle: 16 KB
 constexpr int kABytes = 2 * kKBlock;     // x_hat tile, K = 128
@@ -127,7 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::mbar_init(&u_full[b], kEpiWarps);
       tc::mbar_init(&u_empty[b], 1);
       tc::mbar_init(&d2_full[b], 1);
-      tc::mbar_init(&d2_empty[b], kOutWarps);
+      tc::mbar_init(&d2_empty[b], kEpiWarps);
     }
     tc::fence_mbar_init();
     tc::prefetch_tmap(&map_w12);
@@ -242,9 +239,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------- SwiGLU and output
     const int quarter = warp & 3, half = (warp - kFirstEpiWarp) >> 2;
     const int row = quarter * 32 + lane;  // TMEM lane = tile row
+    uint8_t *stage = smem + kStageOff + (warp - kFirstEpiWarp) * 4096;
     int it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < args.tiles; tile += gridDim.x, ++it) {
+      const int64_t row0 = int64_t(tile) * kRows;
       for (int h = 0; h < kChunks; ++h) {
         const int g = it * kChunks + h, b = g & 1;
         const uint32_t par = (g >> 1) & 1;
@@ -284,34 +283,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) tc::mbar_arrive(&u_full[b]);
       }
       if (!ok) break;
-    }
-  } else if (warp >= kFirstOutWarp) {
-    // ------------------------------------------------------------ output epilogue
-    // z rows of this warp's TMEM lane quarter += bf16(y) (or out = bf16(y)), all
-    // 128 columns, while the SwiGLU warps already work on the next tile.
-    const int quarter = warp & 3;
-    uint8_t *stage = smem + kStageOff + (warp - kFirstOutWarp) * 4096;
-    int it = 0;
-    for (int tile = blockIdx.x; tile < args.tiles; tile += gridDim.x, ++it) {
-      const int64_t row0 = int64_t(tile) * kRows;
+      // Output columns 64 half .. 64 half + 63 of this warp's 32 rows.
       const int db = it & 1;
       if (!warp_wait(&d2_full[db], (it >> 1) & 1, args.status, 0x40B)) break;
       tc::tc_fence_after();
+      const uint32_t d2 = tc::tmem_addr(tmem_base, quarter * 32, 256 + 128 * db + 64 * half);
+      uint32_t y0[32], y1[32];
+      tc::tmem_ld_32x32b_x32(d2, y0);
+      tc::tmem_ld_32x32b_x32(d2 + 32, y1);
+      tc::tmem_ld_wait_regs(y0, y1);
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&d2_empty[db]);
       const bool live = row0 + quarter * 32 < args.rows;
-#pragma unroll 1
-      for (int cb = 0; cb < 4; ++cb) {
-        uint32_t y[32];
-        tc::tmem_ld_32x32b_x32(tc::tmem_addr(tmem_base, quarter * 32, 256 + 128 * db + 32 * cb), y);
-        tc::tmem_ld_wait_regs(y);
-        if (cb == 3) {
-          tc::tc_fence_before();
+      if (args.residual) {
+        // Two [32 rows][32 fp32] boxes; y rounded to bf16 first (fc3's output).
+#pragma unroll
+        for (int bx = 0; bx < 2; ++bx) {
+          const uint32_t *y = bx ? y1 : y0;
+          if (lane == 0) tc::bulk_wait_read<0>();
           __syncwarp();
-          if (lane == 0) tc::mbar_arrive(&d2_empty[db]);
-        }
-        if (lane == 0) tc::bulk_wait_read<0>();
-        __syncwarp();
-        if (args.residual) {
-          // [32 rows][32 fp32] box; y rounded to bf16 first (fc3's output).
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const uint32_t p0 = cvt_bf16x2(__uint_as_float(y[4 * e]), __uint_as_float(y[4 * e + 1]));
@@ -322,26 +313,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc::fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0 && live) {
-            tc::tma_reduce_add_2d(&map_out, stage, 32 * cb, int(row0) + quarter * 32);
+            tc::tma_reduce_add_2d(&map_out, stage, 64 * half + 32 * bx, int(row0) + quarter * 32);
             tc::bulk_commit();
           }
-        } else {
-          // Half of a [32 rows][64 bf16] box per column block; stored after the odd one.
+        }
+      } else {
+        // One [32 rows][64 bf16] box.
+        if (lane == 0) tc::bulk_wait_read<0>();
+        __syncwarp();
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            *reinterpret_cast<uint4 *>(stage + lane * 128 + (((4 * (cb & 1) + e) ^ (lane & 7)) << 4)) =
-                make_uint4(cvt_bf16x2(__uint_as_float(y[8 * e]), __uint_as_float(y[8 * e + 1])),
-                           cvt_bf16x2(__uint_as_float(y[8 * e + 2]), __uint_as_float(y[8 * e + 3])),
-                           cvt_bf16x2(__uint_as_float(y[8 * e + 4]), __uint_as_float(y[8 * e + 5])),
-                           cvt_bf16x2(__uint_as_float(y[8 * e + 6]), __uint_as_float(y[8 * e + 7])));
-          if (cb & 1) {
-            tc::fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0 && live) {
-              tc::tma_store_2d(&map_out, stage, 64 * (cb >> 1), int(row0) + quarter * 32);
-              tc::bulk_commit();
-            }
-          }
+        for (int e = 0; e < 8; ++e) {
+          const uint32_t *y = e < 4 ? y0 + 8 * e : y1 + 8 * (e - 4);
+          *reinterpret_cast<uint4 *>(stage + lane * 128 + ((e ^ (lane & 7)) << 4)) =
+              make_uint4(cvt_bf16x2(__uint_as_float(y[0]), __uint_as_float(y[1])),
+                         cvt_bf16x2(__uint_as_float(y[2]), __uint_as_float(y[3])),
+                         cvt_bf16x2(__uint_as_float(y[4]), __uint_as_float(y[5])),
+                         cvt_bf16x2(__uint_as_float(y[6]), __uint_as_float(y[7])));
+        }
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && live) {
+          tc::tma_store_2d(&map_out, stage, 64 * half, int(row0) + quarter * 32);
+          tc::bulk_commit();
         }
       }
     }
@@ -362,19 +355,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t left = args.rows - int64_t(tile) * kRows;
       return left < kRows ? int(left) : kRows;
     };
-    auto load_rows = [&](int tile, int rbase, float4 (&v)[4]) {
+    auto load_rows = [&](int tile, int rbase, float4 (&v)[8]) {
       const int valid = valid_rows(tile);
 #pragma unroll
-      for (int r = 0; r < 4; ++r)
+      for (int r = 0; r < 8; ++r)
         v[r] = rbase + r < valid
                    ? __ldg(reinterpret_cast<const float4 *>(args.x + (int64_t(tile) * kRows + rbase + r) * kC) + lane)
                    : make_float4(0.f, 0.f, 0.f, 0.f);
     };
     // fp32 LayerNorm of 8 rows into the A tile: mean, mean of squared
     // deviations, rstd = rsqrt(var + eps), bf16((x - mean) * rstd * w + b).
-    auto normalise = [&](const float4 (&v)[4], int valid, int rbase, uint8_t *abuf) {
+    auto normalise = [&](const float4 (&v)[8], int valid, int rbase, uint8_t *abuf) {
 #pragma unroll
-      for (int g = 0; g < 1; ++g) {
+      for (int g = 0; g < 2; ++g) {
         float mean[4], var[4];
 #pragma unroll
         for (int rr = 0; rr < 4; ++rr) {
@@ -414,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     };
-    float4 va[4], vb[4];
+    float4 va[8], vb[8];
     int tile = blockIdx.x, it = 0;
     if (tile < args.tiles) load_rows(tile, row_lo, va);
     for (; tile < args.tiles; tile += gridDim.x, ++it) {
@@ -427,18 +420,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (rows_ahead > 0)
           tc::prefetch_l2_bulk(args.x + (int64_t(ahead) * kRows + row_lo) * kC, uint32_t(rows_ahead) * kC * 4);
       }
-      load_rows(tile, row_lo + 4, vb);
+      load_rows(tile, row_lo + 8, vb);
       if (!warp_wait(&a_empty[ab], ((it >> 1) & 1) ^ 1, args.status, 0x40C)) break;
-#pragma unroll
-      for (int q = 0; q < 6; q += 2) {
-        normalise(va, valid, row_lo + 4 * q, abuf);
-        load_rows(tile, row_lo + 4 * q + 8, va);
-        normalise(vb, valid, row_lo + 4 * q + 4, abuf);
-        load_rows(tile, row_lo + 4 * q + 12, vb);
-      }
-      normalise(va, valid, row_lo + 24, abuf);
+      normalise(va, valid, row_lo, abuf);
+      load_rows(tile, row_lo + 16, va);
+      normalise(vb, valid, row_lo + 8, abuf);
+      load_rows(tile, row_lo + 24, vb);
+      normalise(va, valid, row_lo + 16, abuf);
       if (next < args.tiles) load_rows(next, row_lo, va);
-      normalise(vb, valid, row_lo + 28, abuf);
+      normalise(vb, valid, row_lo + 24, abuf);
       tc::fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&a_full[ab]);
