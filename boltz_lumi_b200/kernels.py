@@ -317,7 +317,7 @@ def split3_fast(x):
         x = x.contiguous()
     rows = x.numel() // cols
     out = torch.empty(3, rows, cols, device=x.device, dtype=torch.bfloat16)
-    call("bl_split3_bf16", x.data_ptr(), rows, cols, cols, out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    call("bl_split3_bf16", x.data_ptr(), rows, cols, cols, out.data_ptr(), _lib.current_stream_handle())
     return out
 
 
@@ -328,7 +328,7 @@ def linear_split3_fast(x3, w3, bias, y, residual=None):
     m, k = x3.shape[1], x3.shape[2]
     n = w3.shape[1]
     call("bl_linear_split3", x3.data_ptr(), m, k, w3.data_ptr(), n, ptr(bias), ptr(residual),
-         0 if residual is None else n, y.data_ptr(), n, torch.cuda.current_stream().cuda_stream)
+         0 if residual is None else n, y.data_ptr(), n, _lib.current_stream_handle())
     return y
 
 
@@ -359,7 +359,7 @@ def layer_norm_split3(x, weight, bias, eps):
     rows = x.numel() // cols
     out = torch.empty(3, rows, cols, device=x.device, dtype=torch.bfloat16)
     call("bl_layernorm_split3", x.data_ptr(), rows, cols, ptr(weight), ptr(bias), float(eps), out.data_ptr(),
-         torch.cuda.current_stream().cuda_stream)
+         _lib.current_stream_handle())
     return out
 
 
@@ -370,7 +370,7 @@ def adaln_modulate_split3(a, scale, shift, eps):
     rows = a.numel() // cols
     out = torch.empty(3, rows, cols, device=a.device, dtype=torch.bfloat16)
     call("bl_adaln_modulate_split3", a.data_ptr(), scale.data_ptr(), shift.data_ptr(), out.data_ptr(), rows, cols,
-         float(eps), torch.cuda.current_stream().cuda_stream)
+         float(eps), _lib.current_stream_handle())
     return out
 
 
@@ -380,5 +380,5 @@ def epilogue_split3(a, b, c, kind):
     rows = a.numel() // a.shape[-1]
     out = torch.empty(3, rows, cols, device=a.device, dtype=torch.bfloat16)
     call("bl_diffusion_epilogue_split3", a.data_ptr(), ptr(b), ptr(c), out.data_ptr(), rows, cols, kind,
-         torch.cuda.current_stream().cuda_stream)
+         _lib.current_stream_handle())
     return out

@@ -168,7 +168,7 @@ class AttentionPairBias(nn.Module):
         zf = z.float().contiguous()
         bias = torch.empty(b, self.num_heads, n, n, device=z.device, dtype=torch.float32)
         w_z = lin.weight.float().contiguous()
-        stream = torch.cuda.current_stream(z.device).cuda_stream
+        stream = _lib.stream_of(z)
         for i in range(b):
             _lib.call("bl_pair_bias", zf[i].data_ptr(), n * n, _lib.ptr(ln.weight), _lib.ptr(ln.bias),
                       float(ln.eps), w_z.data_ptr(), self.num_heads, bias[i].data_ptr(), stream)
