@@ -670,6 +670,10 @@ int triangle_attention(const void *q, const void *k, const void *v, const void *
   // kStages: when the producer finishes the last head's loads, the o_full phases of the
   // earlier heads have completed and its parity wait names the last head's phase.)
   const bool fuse = w_o && hpc == kHeads && n_tiles > kStages;
+  // The separate linear_o runs over rows 0 .. n_outer * n - 1 of out and z: a whole
+  // tensor or a starting-node row slab (checked before anything is launched).
+  BL_REQUIRE(!w_o || fuse || (so == n && si == 1) || (so == 1 && si == n && n_outer == n),
+             "bl_triangle_attention: the unfused w_o path needs contiguous output rows");
   auto kernel = fuse ? tri_flash_tc_kernel<true, true>
                      : hpc > 1 ? tri_flash_tc_kernel<true, false> : tri_flash_tc_kernel<false, false>;
   BL_CUDA(ensure_smem_limit(reinterpret_cast<const void *>(kernel), 232448));
@@ -677,9 +681,6 @@ int triangle_attention(const void *q, const void *k, const void *v, const void *
   kernel<<<grid, kThreads, smem, as_stream(stream)>>>(map_q, map_k, map_v, map_bias, map_wo, args);
   BL_LAUNCH_CHECK();
   if (w_o && !fuse) {
-    // Rows 0 .. n_outer * n - 1 of out and z (a whole tensor or a starting-node row slab).
-    BL_REQUIRE((so == n && si == 1) || (so == 1 && si == n && n_outer == n),
-               "bl_triangle_attention: the unfused w_o path needs contiguous output rows");
     return linear_fused(out, out_ld, nullptr, 0, 128, w_o, 128, n_outer * n, 128, 128, b_o, 0, z, z_ld, nullptr, 0,
                         as_stream(stream));
   }

@@ -115,6 +115,30 @@ def test_triangle_attention_residual(ending, n, kind):
     assert torch.equal(z, expected), (z - expected).abs().max().item()
 
 
+def test_triangle_attention_residual_rejects_strided_slab():
+    """Below four heads per CTA the residual entry runs linear_o as a separate GEMM over
+    contiguous rows; an ending-node slab (n_outer < n) is refused before any launch and
+    z is left untouched."""
+    from boltz_lumi_b200 import _lib
+
+    n, n_outer, n8 = 200, 40, 200
+    dev = "cuda"
+    proj = torch.zeros(n * n, 512, device=dev, dtype=torch.bfloat16)
+    bias = torch.zeros(4, n, n8, device=dev, dtype=torch.bfloat16)
+    mask = torch.ones(n, n, device=dev)
+    w_o = torch.zeros(128, 128, device=dev, dtype=torch.bfloat16)
+    b_o = torch.zeros(128, device=dev)
+    z = torch.ones(n * n, 128, device=dev)
+    scratch = torch.empty(n * n, 128, device=dev, dtype=torch.bfloat16)
+    base = proj.data_ptr()
+    with pytest.raises(RuntimeError, match="contiguous output rows"):
+        _lib.call("bl_triangle_attention_residual", base, base + 256, base + 512, base + 768, 512, 1, n,
+                  bias.data_ptr(), n8, n * n8, mask.data_ptr(), 1, n, 1e9, 4, 32, n, n_outer, scratch.data_ptr(), 128,
+                  w_o.data_ptr(), b_o.data_ptr(), z.data_ptr(), 128, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert torch.equal(z, torch.ones_like(z))
+
+
 @pytest.mark.parametrize("ending", [False, True])
 @pytest.mark.parametrize("n,kind", [(17, "ones"), (64, "partial"), (130, "partial"), (200, "ones"), (312, "partial")])
 def test_triangle_attention_fp32_mode(ending, n, kind):
